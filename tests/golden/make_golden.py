@@ -1,0 +1,174 @@
+"""Generate the golden fixtures that pin the CPU oracle to the reference.
+
+Run in a container that has the reference checkout (it is read-only there):
+
+    python tests/golden/make_golden.py /root/reference/attention
+
+For each test runner of the reference (``run_*test`` in attention/*.py) this
+script rebuilds that runner's inputs on the CPU -- same seed, same sequence of
+``torch.randn`` / ``torch.randperm`` calls, fp16 -- calls the reference's own
+``torch_*_reference`` functions and index builders, and stores:
+
+  * in ``reference_golden_inputs.json``: the sha256 of every input tensor (tests
+    regenerate the inputs with ``golden_inputs.py`` and check the hash);
+  * ``<case>/out`` (+ ``rows``) the reference output, fp16; for large outputs
+                           only the token rows listed in ``rows`` are kept;
+  * index tensors (top-k rows, compression offsets) in full, and the compressed
+    K/V of the CSA/HCA runners.
+
+The reference's Triton kernels need an Ascend NPU and are not run; the torch
+reference functions are what the reference's tests compare them against.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+import golden_inputs as gi  # noqa: E402
+
+MAX_ROWS = 24
+
+
+def sha(t):
+    return hashlib.sha256(t.contiguous().view(torch.uint8).numpy().tobytes()).hexdigest()
+
+
+def subset_rows(n_rows, cu):
+    if n_rows <= MAX_ROWS:
+        return np.arange(n_rows, dtype=np.int32)
+    step = -(-n_rows // (MAX_ROWS - 2 * (len(cu) - 1)))
+    rows = set(range(0, n_rows, step))
+    for i in range(len(cu) - 1):
+        if cu[i + 1] > cu[i]:
+            rows.add(int(cu[i]))
+            rows.add(int(cu[i + 1]) - 1)
+    return np.asarray(sorted(rows), np.int32)
+
+
+def main(ref_dir):
+    sys.path.insert(0, ref_dir)
+    import flash_attention_prefill as FP
+    import paged_attention_decode as PD
+    import sparse_attn_fwd as SA
+    import csa as CSA
+    import hca as HCA
+
+    store, meta = {}, {}
+
+    def put(name, arr):
+        store[name] = arr
+
+    def put_inputs(case, tensors):
+        meta[case] = {k: sha(v) for k, v in tensors.items() if isinstance(v, torch.Tensor)}
+
+    def put_out(case, out, cu=None):
+        o = out.to(torch.float16).numpy()
+        rows = subset_rows(o.shape[0], cu if cu is not None else [0, o.shape[0]])
+        put(f"{case}/rows", rows)
+        put(f"{case}/out", o[rows])
+
+    # FP:235-286
+    for hq, hkv in gi.FP_HEADS:
+        for causal in (True, False):
+            case = f"fp_h{hq}_{hkv}_c{int(causal)}"
+            inp = gi.fp_inputs(hq, hkv)
+            put_inputs(case, inp)
+            out = FP.torch_prefill_tnd_reference(inp["q"], inp["k"], inp["v"], inp["cu_seqlens"], causal=causal)
+            put_out(case, out, gi.FP_CU)
+
+    # PD:208-266
+    for hq, hkv in gi.PD_HEADS:
+        case = f"pd_h{hq}_{hkv}"
+        inp = gi.pd_inputs(hq, hkv)
+        put_inputs(case, inp)
+        out = PD.torch_paged_attention_reference(inp["q"], inp["k_cache"], inp["v_cache"], inp["block_tables"],
+                                                 inp["context_lens"], gi.PD_BLOCK)
+        put_out(case, out)
+
+    # SA:504-581
+    for hkv, grp in gi.SA_HEADS:
+        for sink_on, inp in gi.sa_prefill_inputs(hkv, grp):
+            case = f"sap_h{hkv * grp}_{hkv}_s{int(sink_on)}"
+            put_inputs(case, inp)
+            out = SA.torch_sparse_prefill_reference(inp["q"], inp["k"], inp["v"], inp["topk_idxs"],
+                                                    inp["cu_seqlens"], attn_sink=inp.get("attn_sink"))
+            put_out(case, out, gi.SA_CU)
+
+    # SA:588-675
+    for hkv, grp in gi.SA_HEADS:
+        for sink_on, inp in gi.sa_decode_inputs(hkv, grp):
+            case = f"sad_h{hkv * grp}_{hkv}_s{int(sink_on)}"
+            put_inputs(case, inp)
+            out = SA.torch_sparse_decode_reference(inp["q"], inp["k_cache"], inp["v_cache"], inp["compressed_k"],
+                                                   inp["compressed_v"], inp["block_tables"], inp["topk_idxs"],
+                                                   inp["context_lens"], block_size=gi.SA_BLOCK,
+                                                   attn_sink=inp.get("attn_sink"))
+            put_out(case, out)
+
+    # CSA:470-525
+    for hkv, grp in gi.SA_HEADS:
+        for sink_on, inp in gi.csa_prefill_inputs(hkv, grp):
+            case = f"csap_h{hkv * grp}_{hkv}_s{int(sink_on)}"
+            put_inputs(case, inp)
+            q, k, v, cu = inp["q"], inp["k"], inp["v"], inp["cu_seqlens"]
+            ck, cv, offs = CSA.compress_kv_overlap(k, v, cu, gi.CSA_M)
+            idx = CSA.build_csa_topk_idxs(q, ck, cu, offs, gi.CSA_NWIN_P, gi.CSA_TOPK, gi.CSA_M)
+            out = CSA.torch_csa_prefill_reference(q, k, v, cu, gi.CSA_NWIN_P, gi.CSA_TOPK, gi.CSA_M,
+                                                  attn_sink=inp.get("attn_sink"))
+            put(f"{case}/ck", ck.numpy())
+            put(f"{case}/cv", cv.numpy())
+            put(f"{case}/comp_offsets", offs.numpy())
+            put(f"{case}/topk_idxs", idx.numpy())
+            put_out(case, out, gi.SA_CU)
+
+    # CSA:528-594
+    for hkv, grp in gi.SA_HEADS:
+        for sink_on, inp in gi.csa_decode_inputs(hkv, grp):
+            case = f"csad_h{hkv * grp}_{hkv}_s{int(sink_on)}"
+            put_inputs(case, inp)
+            out = CSA.torch_csa_decode_reference(inp["q"], inp["k_cache"], inp["v_cache"], inp["block_tables"],
+                                                 inp["context_lens"], gi.CSA_NWIN_D, gi.CSA_TOPK, gi.CSA_M,
+                                                 block_size=gi.SA_BLOCK, attn_sink=inp.get("attn_sink"))
+            put_out(case, out)
+
+    # HCA:416-470
+    for hkv, grp in gi.SA_HEADS:
+        for sink_on, inp in gi.hca_prefill_inputs(hkv, grp):
+            case = f"hcap_h{hkv * grp}_{hkv}_s{int(sink_on)}"
+            put_inputs(case, inp)
+            q, k, v, cu = inp["q"], inp["k"], inp["v"], inp["cu_seqlens"]
+            ck, cv, offs = HCA.compress_kv_simple(k, v, cu, gi.HCA_M)
+            idx = HCA.build_hca_topk_idxs(cu, offs, q.shape[0], gi.HCA_NWIN, gi.HCA_M)
+            out = HCA.torch_hca_prefill_reference(q, k, v, cu, gi.HCA_NWIN, gi.HCA_M, attn_sink=inp.get("attn_sink"))
+            put(f"{case}/ck", ck.numpy())
+            put(f"{case}/cv", cv.numpy())
+            put(f"{case}/comp_offsets", offs.numpy())
+            put(f"{case}/topk_idxs", idx.numpy())
+            put_out(case, out, gi.HCA_CU)
+
+    # HCA:473-538
+    for hkv, grp in gi.SA_HEADS:
+        for sink_on, inp in gi.hca_decode_inputs(hkv, grp):
+            case = f"hcad_h{hkv * grp}_{hkv}_s{int(sink_on)}"
+            put_inputs(case, inp)
+            out = HCA.torch_hca_decode_reference(inp["q"], inp["k_cache"], inp["v_cache"], inp["block_tables"],
+                                                 inp["context_lens"], gi.HCA_NWIN, gi.HCA_M,
+                                                 block_size=gi.SA_BLOCK, attn_sink=inp.get("attn_sink"))
+            put_out(case, out)
+
+    np.savez_compressed(os.path.join(HERE, "reference_golden.npz"), **store)
+    with open(os.path.join(HERE, "reference_golden_inputs.json"), "w") as f:
+        json.dump({"torch": torch.__version__, "sha256": meta}, f, indent=1, sort_keys=True)
+    print(f"wrote {len(store)} arrays for {len(meta)} cases")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/attention")
