@@ -1,0 +1,201 @@
+/*
+ * tak_attention.h -- C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Drop-in native backend for suluner/triton-ascend-kernels' attention/*.py.
+ * Each entry point below replaces one Triton launch (or host-side loop) of the
+ * reference; the file:line of the interface it replaces is cited with it.
+ * The Python modules of this package (attention/*.py, same names and call
+ * signatures as the reference's) bind these symbols with ctypes.
+ *
+ * Conventions
+ *   - Every pointer is a device pointer (CUDA global memory) unless stated.
+ *   - Strides are in elements, int64, one per tensor dimension, passed as a
+ *     pointer to a small host array (e.g. q_strides[3] for q[T, H, D]).
+ *   - dtype: TAK_F16, TAK_BF16 or TAK_F32; q, k, v and out share it.
+ *   - Index tensors (cu_seqlens, block tables, top-k rows, offsets) are int32.
+ *   - lse (optional, may be NULL) is float32 [rows, H] contiguous: the natural
+ *     log of the softmax denominator, sink term included; -inf for a row with
+ *     no key.  The reference has no LSE output; it is an addition.
+ *   - stream is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *     asynchronous; no entry point synchronises the device.
+ *   - Return value: 0 on success, nonzero on error (1 = invalid argument,
+ *     2 = unsupported shape, 3 = CUDA error); tak_last_error() describes the
+ *     last error of the calling thread.  No entry point aborts the process.
+ */
+#ifndef TAK_ATTENTION_H_
+#define TAK_ATTENTION_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { TAK_F16 = 0, TAK_BF16 = 1, TAK_F32 = 2 };
+
+/* Library version, e.g. "tak-b200 0.1". */
+const char* tak_version(void);
+
+/* Message of the last error returned on the calling thread ("" if none). */
+const char* tak_last_error(void);
+
+/* Synchronises `stream`, returns the device-side error word (0 = none,
+ * 1 = a bounded wait inside a kernel timed out, 2 = TMEM allocation failed)
+ * and clears it.  For tests and diagnostics, not for the hot path. */
+int tak_read_device_error(void* stream);
+
+/* Kernel selection for cross-checking: 0 = automatic (tensor-core kernels
+ * where the shape allows), 1 = always the generic CUDA-core kernels.
+ * Process-wide; returns the previous value. */
+int tak_set_kernel_path(int path);
+
+/*
+ * Varlen flash prefill.  Replaces flash_attention_prefill(q, k, v, cu_seqlens,
+ * causal) of attention/flash_attention_prefill.py:108-171 (Triton launch at
+ * :158).  q [T,H,D], k/v [T,H_kv,D], out [T,H,D]; cu_seqlens [num_seqs+1].
+ * scale is the softmax scale (the reference uses 1/sqrt(D), :136).
+ * No host synchronisation: the (sequence, row-block) schedule the reference
+ * builds on the host (:144-153) is derived on the device.
+ */
+int tak_flash_attention_prefill(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                const void* v, const int64_t* v_strides, const int32_t* cu_seqlens,
+                                int64_t num_seqs, void* out, const int64_t* out_strides, float* lse,
+                                int64_t total_tokens, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                float scale, int causal, int dtype, void* stream);
+
+/*
+ * Paged decode.  Replaces paged_attention_decode(q, k_cache, v_cache,
+ * block_tables, context_lens, block_size, block_n) of
+ * attention/paged_attention_decode.py:104-151 (Triton launch at :138).
+ * q [B,H,D], k_cache/v_cache [num_blocks,H_kv,cache_rows,D],
+ * block_tables [B,max_blocks], context_lens [B], out [B,H,D].
+ * workspace: device scratch of at least tak_paged_attention_decode_workspace_size()
+ * bytes for the split-KV partials (may be NULL if that size is 0).
+ * split_pages: pages per split-KV work unit, 0 = automatic.
+ */
+size_t tak_paged_attention_decode_workspace_size(int64_t num_seqs, int64_t num_q_heads, int64_t num_kv_heads,
+                                                 int64_t head_dim, int64_t block_size, int64_t max_blocks,
+                                                 int split_pages);
+int tak_paged_attention_decode(const void* q, const int64_t* q_strides, const void* k_cache,
+                               const int64_t* k_strides, const void* v_cache, const int64_t* v_strides,
+                               const int32_t* block_tables, const int64_t* bt_strides, const int32_t* context_lens,
+                               void* out, const int64_t* out_strides, float* lse, int64_t num_seqs,
+                               int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
+                               int64_t max_blocks, int64_t num_blocks, int64_t cache_rows, float scale, int dtype,
+                               void* workspace, size_t workspace_bytes, int split_pages, void* stream);
+
+/*
+ * Top-k sparse prefill with per-head sink logits.  Replaces
+ * sparse_attn_prefill(q, k, v, topk_idxs, cu_seqlens, attn_sink) of
+ * attention/sparse_attn_fwd.py:263-314 (Triton launch at :298).
+ * q [T,H,Dqk], k [rows,H_kv,Dqk], v [rows,H_kv,Dv] (Dv may differ from Dqk:
+ * the reference requires equal shapes, :279), topk_idxs [T,k_topk] (< 0 =
+ * masked; >= rows is treated as masked too), attn_sink [H] float32 or NULL,
+ * out [T,H,Dv].  cu_seqlens does not enter the math (as in the reference
+ * kernel, whose grid covers every token, :296) and is not an argument.
+ */
+int tak_sparse_attn_prefill(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                            const void* v, const int64_t* v_strides, const int32_t* topk_idxs,
+                            const int64_t* topk_strides, const float* attn_sink, void* out,
+                            const int64_t* out_strides, float* lse, int64_t total_tokens, int64_t num_q_heads,
+                            int64_t num_kv_heads, int64_t head_dim, int64_t head_dim_v, int64_t kv_rows,
+                            int64_t k_topk, float scale, int dtype, void* stream);
+
+/*
+ * Top-k sparse decode over a paged window plus compressed rows.  Replaces
+ * sparse_attn_decode(q, k_cache, v_cache, compressed_k, compressed_v,
+ * block_tables, topk_idxs, context_lens, num_win, block_size, attn_sink) of
+ * attention/sparse_attn_fwd.py:317-382 (Triton launch at :359), with its
+ * slot-position rule (:151-210): slots < num_win address the paged cache and
+ * need 0 <= idx < ctx; later slots address compressed rows idx - ctx.
+ */
+int tak_sparse_attn_decode(const void* q, const int64_t* q_strides, const void* k_cache, const int64_t* k_strides,
+                           const void* v_cache, const int64_t* v_strides, const void* compressed_k,
+                           const int64_t* ck_strides, const void* compressed_v, const int64_t* cv_strides,
+                           const int32_t* block_tables, const int64_t* bt_strides, const int32_t* topk_idxs,
+                           const int64_t* topk_strides, const int32_t* context_lens, const float* attn_sink,
+                           void* out, const int64_t* out_strides, float* lse, int64_t num_seqs,
+                           int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t head_dim_v,
+                           int64_t num_compressed, int64_t k_topk, int64_t num_win, int64_t block_size,
+                           float scale, int dtype, void* stream);
+
+/* token -> sequence map (0 for tokens outside every sequence).  Replaces
+ * build_token_to_seq of attention/sparse_attn_fwd.py:253-260. */
+int tak_build_token_to_seq(const int32_t* cu_seqlens, int64_t num_seqs, int64_t total_tokens, int32_t* out,
+                           void* stream);
+
+/*
+ * Window pooling of K and V into compressed slots.  Replaces
+ * compress_kv_overlap (attention/csa.py:9-69; window = 2m, stride = m) and
+ * compress_kv_simple (attention/hca.py:9-69; window = stride = m').
+ * k [T,H_kv,D], v [T,H_kv,Dv], comp_offsets [num_seqs+1] (computed by the
+ * caller: max(1, ceil(L/stride)) slots per non-empty sequence), compressed
+ * outputs [num_compressed,H_kv,D(v)].  gate: NULL = plain mean (the
+ * reference); else float32 [T] logits and each slot is the softmax(gate)-
+ * weighted sum of its window (an addition, no counterpart in the reference).
+ */
+int tak_compress_kv(const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                    const float* gate, int64_t gate_stride, const int32_t* cu_seqlens, const int32_t* comp_offsets,
+                    int64_t num_seqs, int64_t num_compressed, void* compressed_k, const int64_t* ck_strides,
+                    void* compressed_v, const int64_t* cv_strides, int64_t num_kv_heads, int64_t head_dim,
+                    int64_t head_dim_v, int64_t stride, int64_t window, int dtype, void* stream);
+
+/*
+ * Same pooling, reading each sequence's first context_lens[s] rows straight
+ * from a paged cache [num_blocks,H_kv,P,D].  Replaces the page gather +
+ * compress of csa_decode_forward (attention/csa.py:225-256) and
+ * hca_decode_forward (attention/hca.py:204-232).  gate (optional) is
+ * float32 [num_blocks, P] with strides gate_strides[2].
+ */
+int tak_compress_kv_paged(const void* k_cache, const int64_t* k_strides, const void* v_cache,
+                          const int64_t* v_strides, const float* gate, const int64_t* gate_strides,
+                          const int32_t* block_tables, const int64_t* bt_strides, const int32_t* context_lens,
+                          int64_t block_size, const int32_t* comp_offsets, int64_t num_seqs,
+                          int64_t num_compressed, void* compressed_k, const int64_t* ck_strides,
+                          void* compressed_v, const int64_t* cv_strides, int64_t num_kv_heads, int64_t head_dim,
+                          int64_t head_dim_v, int64_t stride, int64_t window, int dtype, void* stream);
+
+/* Sliding-window columns [0, n_win) of prefill index rows (row stride ld).
+ * Replaces attention/csa.py:108-117 (same rule at hca.py:133-137). */
+int tak_build_window_idxs(const int32_t* cu_seqlens, int64_t num_seqs, int64_t total_tokens, int64_t n_win,
+                          int32_t* out, int64_t ld, void* stream);
+
+/* Full HCA prefill index rows [T, n_win + max_n_comp].  Replaces
+ * build_hca_topk_idxs of attention/hca.py:76-146 (max_n_comp from :103-115,
+ * computed by the caller). */
+int tak_build_hca_topk_idxs(const int32_t* cu_seqlens, const int32_t* comp_offsets, int64_t num_seqs,
+                            int64_t total_tokens, int64_t n_win, int64_t max_n_comp, int64_t m_prime,
+                            int32_t* out, int64_t ld, void* stream);
+
+/* Decode index rows [B, n_win + n_comp_cols]: window ctx - n_win + wi, and
+ * with m_prime > 0 the HCA compressed part (attention/hca.py:245-259); with
+ * m_prime == 0 the compressed columns are -1 for tak_csa_indexer_topk to fill
+ * (attention/csa.py:263-276). */
+int tak_build_decode_topk_idxs(const int32_t* context_lens, const int32_t* comp_offsets, int64_t num_seqs,
+                               int64_t n_win, int64_t n_comp_cols, int64_t m_prime, int32_t* out, int64_t ld,
+                               void* stream);
+
+/*
+ * CSA Lightning indexer: columns [n_win, n_win + top_k) of the index rows.
+ * Replaces the indexer of build_csa_topk_idxs (attention/csa.py:119-164) and
+ * of csa_decode_forward (:278-302).  Prefill (cu_seqlens != NULL): one row per
+ * token, entry = total_tokens + comp_offsets[s] + slot.  Decode (cu_seqlens ==
+ * NULL, context_lens given): one row per sequence, entry = ctx +
+ * comp_offsets[s] + slot.  Scores are unscaled q.k~ of the last query head
+ * against the last KV head (the head whose choice survives in the reference),
+ * rounded to dtype; slot causal iff slot*m < position; descending score, ties
+ * to the lower slot; masked slots appended in ascending order when fewer than
+ * min(top_k, n_c) are causal.  max_comp_per_seq bounds n_c (<= 51200).
+ */
+int tak_csa_indexer_topk(const void* q, const int64_t* q_strides, const void* compressed_k,
+                         const int64_t* ck_strides, const int32_t* cu_seqlens, const int32_t* context_lens,
+                         const int32_t* comp_offsets, int64_t num_seqs, int64_t total_tokens, int64_t num_q_heads,
+                         int64_t num_kv_heads, int64_t head_dim, int64_t n_win, int64_t top_k, int64_t m,
+                         int64_t max_comp_per_seq, int32_t* out, int64_t ld, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TAK_ATTENTION_H_ */

@@ -1,0 +1,115 @@
+"""CPU-side checks of the boundary: the C-ABI library loads and exports every
+symbol include/tak_attention.h declares, the ctypes signatures cover exactly
+those symbols, and the drop-in modules keep the reference's call signatures
+and refuse non-CUDA tensors the way the reference refuses non-NPU ones."""
+
+import ctypes
+import inspect
+import os
+import re
+
+import pytest
+import torch
+
+import _tak_b200 as T
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "tak_attention.h")
+
+
+def header_symbols():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(tak_\w+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    if not os.path.exists(T.LIB_PATH):
+        pytest.skip("libtak_b200.so not built (run __graft_entry__.build())")
+    h = ctypes.CDLL(T.LIB_PATH)
+    syms = header_symbols()
+    assert len(syms) >= 15
+    for s in syms:
+        assert hasattr(h, s), f"{s} declared in tak_attention.h but not exported"
+    assert set(T._SIGS) == set(syms), "ctypes table and header disagree"
+    assert T.lib().tak_version().decode().startswith("tak-b200")
+
+
+def test_reference_signatures_kept():
+    import flash_attention_prefill as FP
+    import paged_attention_decode as PD
+    import sparse_attn_fwd as SA
+    import csa as CSA
+    import hca as HCA
+
+    def pos(fn):
+        return [(p.name, p.default) for p in inspect.signature(fn).parameters.values()
+                if p.kind == p.POSITIONAL_OR_KEYWORD]
+
+    E = inspect.Parameter.empty
+    assert pos(FP.flash_attention_prefill) == [("q", E), ("k", E), ("v", E), ("cu_seqlens", E), ("causal", True)]
+    assert pos(PD.paged_attention_decode) == [("q", E), ("k_cache", E), ("v_cache", E), ("block_tables", E),
+                                              ("context_lens", E), ("block_size", 16), ("block_n", 16)]
+    assert pos(SA.sparse_attn_prefill) == [("q", E), ("k", E), ("v", E), ("topk_idxs", E), ("cu_seqlens", E),
+                                           ("attn_sink", None)]
+    assert [n for n, _ in pos(SA.sparse_attn_decode)] == [
+        "q", "k_cache", "v_cache", "compressed_k", "compressed_v", "block_tables", "topk_idxs", "context_lens",
+        "num_win", "block_size", "attn_sink"]
+    assert [n for n, _ in pos(SA.build_token_to_seq)] == ["cu_seqlens", "total_tokens", "device"]
+    assert [n for n, _ in pos(CSA.compress_kv_overlap)] == ["k", "v", "cu_seqlens", "m"]
+    assert [n for n, _ in pos(CSA.build_csa_topk_idxs)] == ["q", "compressed_k", "cu_seqlens", "comp_offsets",
+                                                           "n_win", "top_k", "m"]
+    assert [n for n, _ in pos(CSA.csa_prefill_forward)] == ["q", "k", "v", "cu_seqlens", "n_win", "top_k", "m",
+                                                           "attn_sink"]
+    assert [n for n, _ in pos(CSA.csa_decode_forward)] == ["q", "k_cache", "v_cache", "block_tables",
+                                                          "context_lens", "n_win", "top_k", "m", "block_size",
+                                                          "attn_sink"]
+    assert [n for n, _ in pos(HCA.compress_kv_simple)] == ["k", "v", "cu_seqlens", "m_prime"]
+    assert [n for n, _ in pos(HCA.build_hca_topk_idxs)] == ["cu_seqlens", "comp_offsets", "total_tokens", "n_win",
+                                                           "m_prime"]
+    assert [n for n, _ in pos(HCA.hca_prefill_forward)] == ["q", "k", "v", "cu_seqlens", "n_win", "m_prime",
+                                                           "attn_sink"]
+    assert [n for n, _ in pos(HCA.hca_decode_forward)] == ["q", "k_cache", "v_cache", "block_tables",
+                                                          "context_lens", "n_win", "m_prime", "block_size",
+                                                          "attn_sink"]
+
+
+def test_cpu_tensors_rejected_like_the_reference():
+    import flash_attention_prefill as FP
+    import paged_attention_decode as PD
+    import sparse_attn_fwd as SA
+
+    q = torch.zeros(4, 2, 8)
+    with pytest.raises(AssertionError):
+        FP.flash_attention_prefill(q, q[:, :1], q[:, :1], torch.tensor([0, 4], dtype=torch.int32))
+    with pytest.raises(AssertionError):
+        PD.paged_attention_decode(q, torch.zeros(2, 1, 16, 8), torch.zeros(2, 1, 16, 8),
+                                  torch.zeros(4, 1, dtype=torch.int32), torch.ones(4, dtype=torch.int32))
+    with pytest.raises(AssertionError):
+        SA.sparse_attn_prefill(q, q[:, :1], q[:, :1], torch.zeros(4, 2, dtype=torch.int32), None)
+
+
+def test_paged_decode_block_n_assertion():
+    import paged_attention_decode as PD
+
+    # PD:121-123: block_n must divide block_size and not exceed it
+    q = torch.zeros(1, 1, 8)
+    with pytest.raises(AssertionError):
+        PD.paged_attention_decode(q, q, q, q, q, block_size=16, block_n=32)
+
+
+def test_workspace_size_is_host_only():
+    if not os.path.exists(T.LIB_PATH):
+        pytest.skip("libtak_b200.so not built")
+    n = T.lib().tak_paged_attention_decode_workspace_size(64, 32, 8, 128, 128, 64, 0)
+    assert n > 64 * 32 * 130 * 4
+    # one page per split: one partial per page
+    n1 = T.lib().tak_paged_attention_decode_workspace_size(2, 4, 1, 128, 16, 10, 1)
+    assert n1 >= 2 * 4 * 10 * 130 * 4
+
+
+def test_comp_offsets_host_matches_oracle():
+    from oracle import attention_oracle as O
+
+    for lens, st in (([0, 3, 4, 5, 130], 4), ([256, 512, 384], 128), ([], 4), ([1], 128)):
+        assert T.comp_offsets_host(lens, st) == O.comp_offsets_for(lens, st).tolist()

@@ -1,0 +1,426 @@
+"""CUDA path vs the CPU oracle (and vs the reference's golden outputs).
+
+Every test here calls the drop-in modules, which call libtak_b200.so through
+its C ABI.  Tolerances: fp16/bf16 outputs max-abs <= 2e-2 of the float64
+oracle (the bf16 rounding of an O(1) output is 4e-3), LSE <= 1e-3; fp32
+outputs <= 1e-4; index tensors bit-exact.
+"""
+
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+from oracle import attention_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+import _tak_b200 as T  # noqa: E402
+import flash_attention_prefill as FP  # noqa: E402
+import paged_attention_decode as PD  # noqa: E402
+import sparse_attn_fwd as SA  # noqa: E402
+import csa as CSA  # noqa: E402
+import hca as HCA  # noqa: E402
+
+DEV = "cuda"
+TOL16 = 2e-2
+TOL_LSE = 1e-3
+TOL32 = 1e-4
+HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+GOLD = np.load(os.path.join(HERE, "reference_golden.npz"))
+CASES = sorted(json.load(open(os.path.join(HERE, "reference_golden_inputs.json")))["sha256"])
+
+
+def npy(t):
+    return t.detach().float().cpu().numpy()
+
+
+def cu(x):
+    return x.to(DEV) if isinstance(x, torch.Tensor) else x
+
+
+def close(out, ref, tol):
+    out = npy(out) if isinstance(out, torch.Tensor) else out
+    err = np.abs(out.astype(np.float64) - ref).max() if out.size else 0.0
+    assert err <= tol, f"max abs err {err:.3e} > {tol:.1e}"
+    return err
+
+
+def close_lse(lse, ref):
+    lse = npy(lse)
+    fin = np.isfinite(ref)
+    assert (np.isfinite(lse) == fin).all()
+    if fin.any():
+        assert np.abs(lse[fin] - ref[fin]).max() <= TOL_LSE
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert T.read_device_error() == 0, "a kernel reported a timed-out wait"
+
+
+@pytest.fixture(params=[0, 1], ids=["auto", "generic"])
+def kernel_path(request):
+    old = T.set_kernel_path(request.param)
+    yield request.param
+    T.set_kernel_path(old)
+
+
+def assert_topk_match(got, ref, q, ck, base_of_row, n_win, ulp):
+    """Index rows equal, except that two slots whose indexer scores differ by
+    at most one rounding step of the score dtype may trade places (the CUDA
+    kernel accumulates the dot product in fp32, the oracle in float64, so a
+    score within one ulp of a rounding boundary can round either way)."""
+    np.testing.assert_array_equal(got[:, :n_win], ref[:, :n_win])
+    qn, ckn = q[:, -1, :].astype(np.float64), ck[:, -1, :].astype(np.float64)
+    for t in np.nonzero((got != ref).any(1))[0]:
+        a, b = got[t, n_win:], ref[t, n_win:]
+        assert ((a >= 0) == (b >= 0)).all()
+        base = base_of_row(t)
+        sa = ckn[a[a >= 0] - base] @ qn[t]
+        sb = ckn[b[b >= 0] - base] @ qn[t]
+        tol = ulp * np.maximum(np.abs(sa), np.abs(sb)) + 1e-6
+        assert (np.abs(sa - sb) <= tol).all(), f"row {t}: {a} vs {b}"
+
+
+# ---------------------------------------------------------------------------
+# reference runner configurations (golden fixtures)
+# ---------------------------------------------------------------------------
+
+def _golden(case, out):
+    rows = GOLD[f"{case}/rows"]
+    np.testing.assert_allclose(npy(out)[rows], GOLD[f"{case}/out"].astype(np.float64), atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c.startswith("fp_")])
+def test_golden_prefill(case, kernel_path):
+    inp = {k: cu(v) for k, v in gi.case_inputs(case).items()}
+    causal = case.endswith("c1")
+    out, lse = FP.flash_attention_prefill(inp["q"], inp["k"], inp["v"], inp["cu_seqlens"], causal=causal,
+                                          return_lse=True)
+    ref, ref_lse = O.prefill(inp["q"].cpu(), inp["k"].cpu(), inp["v"].cpu(), gi.FP_CU, causal)
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+    _golden(case, out)
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c.startswith("pd_")])
+def test_golden_paged_decode(case, kernel_path):
+    inp = {k: cu(v) for k, v in gi.case_inputs(case).items()}
+    out, lse = PD.paged_attention_decode(inp["q"], inp["k_cache"], inp["v_cache"], inp["block_tables"],
+                                         inp["context_lens"], gi.PD_BLOCK, 16, return_lse=True)
+    ref, ref_lse = O.paged_decode(*(npy(inp[k]) for k in ("q", "k_cache", "v_cache")),
+                                  inp["block_tables"].cpu(), inp["context_lens"].cpu(), gi.PD_BLOCK)
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+    _golden(case, out)
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c.startswith("sap_")])
+def test_golden_sparse_prefill(case, kernel_path):
+    inp = {k: cu(v) for k, v in gi.case_inputs(case).items()}
+    sink = inp.get("attn_sink")
+    out, lse = SA.sparse_attn_prefill(inp["q"], inp["k"], inp["v"], inp["topk_idxs"], inp["cu_seqlens"], sink,
+                                      return_lse=True)
+    ref, ref_lse = O.sparse_prefill(inp["q"].cpu(), inp["k"].cpu(), inp["v"].cpu(), inp["topk_idxs"].cpu(),
+                                    None, None if sink is None else sink.cpu())
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+    _golden(case, out)
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c.startswith("sad_")])
+def test_golden_sparse_decode(case, kernel_path):
+    inp = {k: cu(v) for k, v in gi.case_inputs(case).items()}
+    sink = inp.get("attn_sink")
+    args = [inp[k] for k in ("q", "k_cache", "v_cache", "compressed_k", "compressed_v", "block_tables",
+                             "topk_idxs", "context_lens")]
+    out, lse = SA.sparse_attn_decode(*args, num_win=gi.SA_NWIN_D, block_size=gi.SA_BLOCK, attn_sink=sink,
+                                     return_lse=True)
+    ref, ref_lse = O.sparse_decode(*(a.cpu() for a in args), gi.SA_NWIN_D, gi.SA_BLOCK,
+                                   None if sink is None else sink.cpu())
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+    _golden(case, out)
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c.startswith("csap_")])
+def test_golden_csa_prefill(case):
+    inp = {k: cu(v) for k, v in gi.case_inputs(case).items()}
+    q, k, v, cuq = inp["q"], inp["k"], inp["v"], inp["cu_seqlens"]
+    ck, cv, offs = CSA.compress_kv_overlap(k, v, cuq, gi.CSA_M)
+    np.testing.assert_array_equal(offs.cpu().numpy(), GOLD[f"{case}/comp_offsets"])
+    np.testing.assert_allclose(npy(ck), GOLD[f"{case}/ck"].astype(np.float64), atol=2e-3, rtol=2e-3)
+    np.testing.assert_allclose(npy(cv), GOLD[f"{case}/cv"].astype(np.float64), atol=2e-3, rtol=2e-3)
+    idx = CSA.build_csa_topk_idxs(q, ck, cuq, offs, gi.CSA_NWIN_P, gi.CSA_TOPK, gi.CSA_M)
+    mine = O.build_csa_topk_idxs(q.cpu(), npy(ck), gi.SA_CU, offs.cpu(), gi.CSA_NWIN_P, gi.CSA_TOPK, gi.CSA_M,
+                                 "float16")
+    Tn = q.shape[0]      # entries are Tn + global compressed row
+    assert_topk_match(idx.cpu().numpy(), mine, npy(q), npy(ck), lambda t: Tn, gi.CSA_NWIN_P, 2.0 ** -10)
+    out = CSA.csa_prefill_forward(q, k, v, cuq, gi.CSA_NWIN_P, gi.CSA_TOPK, gi.CSA_M, inp.get("attn_sink"))
+    kf = np.concatenate([npy(k), npy(ck)], 0)
+    vf = np.concatenate([npy(v), npy(cv)], 0)
+    sink = inp.get("attn_sink")
+    ref, _ = O.sparse_prefill(q.cpu(), kf, vf, mine, None, None if sink is None else sink.cpu())
+    close(out, ref, TOL16)
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c.startswith("hcap_")])
+def test_golden_hca_prefill(case):
+    inp = {k: cu(v) for k, v in gi.case_inputs(case).items()}
+    q, k, v, cuq = inp["q"], inp["k"], inp["v"], inp["cu_seqlens"]
+    ck, cv, offs = HCA.compress_kv_simple(k, v, cuq, gi.HCA_M)
+    np.testing.assert_allclose(npy(ck), GOLD[f"{case}/ck"].astype(np.float64), atol=2e-3, rtol=2e-3)
+    idx = HCA.build_hca_topk_idxs(cuq, offs, q.shape[0], gi.HCA_NWIN, gi.HCA_M)
+    np.testing.assert_array_equal(idx.cpu().numpy(), GOLD[f"{case}/topk_idxs"])
+    out = HCA.hca_prefill_forward(q, k, v, cuq, gi.HCA_NWIN, gi.HCA_M, inp.get("attn_sink"))
+    _golden(case, out)
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c.startswith("csad_")])
+def test_golden_csa_decode(case):
+    inp = {k: cu(v) for k, v in gi.case_inputs(case).items()}
+    args = [inp[k] for k in ("q", "k_cache", "v_cache", "block_tables", "context_lens")]
+    out = CSA.csa_decode_forward(*args, gi.CSA_NWIN_D, gi.CSA_TOPK, gi.CSA_M, gi.SA_BLOCK, inp.get("attn_sink"))
+    _golden(case, out)
+    sink = inp.get("attn_sink")
+    ref, _, _ = O.csa_decode_forward(*(a.cpu() for a in args), gi.CSA_NWIN_D, gi.CSA_TOPK, gi.CSA_M, gi.SA_BLOCK,
+                                     None if sink is None else sink.cpu(), "float16")
+    close(out, ref, TOL16)
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c.startswith("hcad_")])
+def test_golden_hca_decode(case):
+    inp = {k: cu(v) for k, v in gi.case_inputs(case).items()}
+    args = [inp[k] for k in ("q", "k_cache", "v_cache", "block_tables", "context_lens")]
+    out = HCA.hca_decode_forward(*args, gi.HCA_NWIN, gi.HCA_M, gi.SA_BLOCK, inp.get("attn_sink"))
+    _golden(case, out)
+
+
+# ---------------------------------------------------------------------------
+# BASELINE-shaped configurations and edge cases
+# ---------------------------------------------------------------------------
+
+def _cu_t(lens):
+    return torch.tensor([0] + np.cumsum(lens).tolist(), dtype=torch.int32, device=DEV)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("causal", [True, False])
+def test_prefill_varlen_gqa(dtype, causal, kernel_path):
+    """Varlen prefill, lengths {17,128,300,511}, 8 q heads / 2 KV heads, d=128."""
+    lens = [17, 128, 300, 511]
+    g = torch.Generator().manual_seed(0)
+    Tn = sum(lens)
+    q = torch.randn(Tn, 8, 128, generator=g).to(DEV, dtype)
+    k = torch.randn(Tn, 2, 128, generator=g).to(DEV, dtype)
+    v = torch.randn(Tn, 2, 128, generator=g).to(DEV, dtype)
+    out, lse = FP.flash_attention_prefill(q, k, v, _cu_t(lens), causal, return_lse=True)
+    ref, ref_lse = O.prefill(npy(q), npy(k), npy(v), [0] + np.cumsum(lens).tolist(), causal)
+    close(out, ref, TOL32 if dtype == torch.float32 else TOL16)
+    close_lse(lse, ref_lse)
+    assert out.dtype == dtype
+
+
+def test_prefill_edge_lengths(kernel_path):
+    """Empty sequences, length-1 sequences, a 129-row sequence (one row past a
+    128-row tile), trailing tokens outside every sequence, strided q."""
+    lens = [0, 1, 129, 0, 64, 1]
+    Tn = sum(lens) + 3
+    g = torch.Generator().manual_seed(1)
+    qb = torch.randn(Tn, 4, 2, 64, generator=g).to(DEV, torch.bfloat16)
+    q = qb[:, :, 0, :]                                  # non-contiguous
+    k = torch.randn(Tn, 1, 64, generator=g).to(DEV, torch.bfloat16)
+    v = torch.randn(Tn, 1, 64, generator=g).to(DEV, torch.bfloat16)
+    cuq = _cu_t(lens)
+    out, lse = FP.flash_attention_prefill(q, k, v, cuq, True, return_lse=True)
+    ref, ref_lse = O.prefill(npy(q), npy(k), npy(v), cuq.cpu(), True)
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+    assert (npy(out)[-3:] == 0).all()
+
+
+def _paged_case(B, H, Hkv, D, P, max_ctx, pool, dtype, seed, ctx=None):
+    g = torch.Generator().manual_seed(seed)
+    if ctx is None:
+        ctx = torch.randint(1, max_ctx + 1, (B,), generator=g)
+    ctx = torch.as_tensor(ctx, dtype=torch.int32)
+    maxb = (max_ctx + P - 1) // P
+    perm = torch.randperm(pool, generator=g).to(torch.int32)
+    bt = torch.zeros(B, maxb, dtype=torch.int32)
+    i = 0
+    for b in range(B):
+        for j in range((int(ctx[b]) + P - 1) // P):
+            bt[b, j] = perm[i]
+            i += 1
+    kc = torch.randn(pool, Hkv, P, D, generator=g).to(DEV, dtype)
+    vc = torch.randn(pool, Hkv, P, D, generator=g).to(DEV, dtype)
+    q = torch.randn(B, H, D, generator=g).to(DEV, dtype)
+    return q, kc, vc, bt.to(DEV), ctx.to(DEV)
+
+
+@pytest.mark.parametrize("P", [16, 64, 128])
+@pytest.mark.parametrize("G", [1, 4, 8])
+def test_paged_decode_shapes(P, G, kernel_path):
+    """Batch 12, 32 query heads, head_dim 128, bf16, contexts up to 1500
+    (several splits), including ctx 1, ctx = P and ctx = 0."""
+    B, H = 12, 32
+    ctx = [1, P, P + 1, 1500, 777, 0, 3 * P, 1024, 5, 1499, 64, 250]
+    q, kc, vc, bt, cl = _paged_case(B, H, H // G, 128, P, 1500, 200, torch.bfloat16, 3, ctx)
+    out, lse = PD.paged_attention_decode(q, kc, vc, bt, cl, P, min(P, 16), return_lse=True)
+    ref, ref_lse = O.paged_decode(npy(q), npy(kc), npy(vc), bt.cpu(), cl.cpu(), P)
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+
+
+@pytest.mark.parametrize("split_pages", [1, 2, 64])
+def test_paged_decode_split_invariance(split_pages):
+    """The split-KV partition must not change the result beyond rounding."""
+    q, kc, vc, bt, cl = _paged_case(8, 32, 8, 128, 128, 4096, 300, torch.bfloat16, 5)
+    out = PD.paged_attention_decode(q, kc, vc, bt, cl, 128, 16, split_pages=split_pages)
+    ref, _ = O.paged_decode(npy(q), npy(kc), npy(vc), bt.cpu(), cl.cpu(), 128)
+    close(out, ref, TOL16)
+
+
+def test_paged_decode_fp32_and_stale_tail():
+    """fp32 cache (generic kernel); and NaN garbage in the unused tail rows of
+    the last page must not leak into the bf16 fast path."""
+    q, kc, vc, bt, cl = _paged_case(4, 8, 2, 128, 16, 200, 64, torch.float32, 7, [13, 35, 200, 1])
+    out = PD.paged_attention_decode(q, kc, vc, bt, cl, 16, 16)
+    ref, _ = O.paged_decode(npy(q), npy(kc), npy(vc), bt.cpu(), cl.cpu(), 16)
+    close(out, ref, TOL32)
+    q, kc, vc, bt, cl = _paged_case(4, 8, 2, 128, 64, 300, 64, torch.bfloat16, 8, [13, 65, 300, 1])
+    ref, _ = O.paged_decode(npy(q), npy(kc), npy(vc), bt.cpu(), cl.cpu(), 64)
+    for b, c in enumerate(cl.cpu().tolist()):
+        last = int(bt[b, (c - 1) // 64])
+        kc[last, :, c % 64 or 64:, :] = float("nan")
+        vc[last, :, c % 64 or 64:, :] = float("nan")
+    out = PD.paged_attention_decode(q, kc, vc, bt, cl, 64, 16)
+    close(out, ref, TOL16)
+
+
+def test_paged_decode_cfg2_sample():
+    """BASELINE decode shape (batch 64, 32/8 heads, d=128, page 128, pool 5000,
+    ctx U[1,8192]) -- checked against the oracle on 6 of the 64 requests."""
+    q, kc, vc, bt, cl = _paged_case(64, 32, 8, 128, 128, 8192, 5000, torch.bfloat16, 11)
+    out, lse = PD.paged_attention_decode(q, kc, vc, bt, cl, 128, 128, return_lse=True)
+    pick = [0, 1, 17, 33, 50, 63]
+    idx = torch.tensor(pick, device=DEV)
+    ref, ref_lse = O.paged_decode(npy(q[idx]), npy(kc), npy(vc), bt[idx].cpu(), cl[idx].cpu(), 128, acc=np.float32)
+    close(out[idx], ref, TOL16)
+    close_lse(lse[idx], ref_lse)
+
+
+def _sparse_case(Tn, H, Hkv, D, Dv, rows, K, dtype, seed, shared_latent=False, pad=True):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(Tn, H, D, generator=g).to(DEV, dtype)
+    k = torch.randn(rows, Hkv, D, generator=g).to(DEV, dtype)
+    v = k[..., :Dv] if shared_latent else torch.randn(rows, Hkv, Dv, generator=g).to(DEV, dtype)
+    idx = torch.stack([torch.randperm(rows, generator=g)[:K] for _ in range(Tn)]).sort(1).values.to(torch.int32)
+    if pad:
+        for t in range(0, Tn, 3):
+            idx[t, (t * 7) % K:] = -1        # ragged -1 padding, one fully masked row
+        idx[1, :] = -1
+    sink = torch.randn(H, generator=g).to(DEV)
+    return q, k, v, idx.to(DEV), sink
+
+
+@pytest.mark.parametrize("with_sink", [False, True])
+def test_sparse_prefill_mla_shape(with_sink, kernel_path):
+    """BASELINE sparse shape at small size: 64 query heads sharing 1 KV head,
+    Dqk 576 (512 latent + 64 rope), Dv 512 with v a view of k's first 512
+    dims, 256 indices per token with -1 padding and a fully masked row."""
+    q, k, v, idx, sink = _sparse_case(24, 64, 1, 576, 512, 1500, 256, torch.bfloat16, 21, shared_latent=True)
+    s = sink if with_sink else None
+    out, lse = SA.sparse_attn_prefill(q, k, v, idx, None, s, return_lse=True)
+    ref, ref_lse = O.sparse_prefill(npy(q), npy(k), npy(v), idx.cpu(), None, None if s is None else s.cpu())
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+
+
+def test_sparse_prefill_gqa_fp32_and_oob():
+    q, k, v, idx, sink = _sparse_case(40, 8, 2, 128, 128, 300, 64, torch.float32, 22)
+    idx[5, 3] = 10_000            # past the last row: masked
+    out = SA.sparse_attn_prefill(q, k, v, idx, None, sink)
+    ref, _ = O.sparse_prefill(npy(q), npy(k), npy(v), idx.cpu(), None, sink.cpu())
+    close(out, ref, TOL32)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("gated", [False, True])
+def test_compress_csa_hca(dtype, gated):
+    lens = [0, 3, 4, 5, 130, 257, 1]
+    Tn = sum(lens)
+    g = torch.Generator().manual_seed(31)
+    k = torch.randn(Tn, 2, 128, generator=g).to(DEV, dtype)
+    v = torch.randn(Tn, 2, 128, generator=g).to(DEV, dtype)
+    gate = torch.randn(Tn, generator=g).to(DEV) if gated else None
+    cuq = _cu_t(lens)
+    for fn, stride, window in ((CSA.compress_kv_overlap, 4, 8), (HCA.compress_kv_simple, 128, 128)):
+        ck, cv, offs = fn(k, v, cuq, stride, gate=gate)
+        rk, rv, roffs = O.compress_kv(npy(k), npy(v), cuq.cpu(), stride, window,
+                                      None if gate is None else gate.cpu())
+        np.testing.assert_array_equal(offs.cpu().numpy(), roffs)
+        close(ck, rk, 1e-2)
+        close(cv, rv, 1e-2)
+
+
+def test_compress_paged_matches_tnd():
+    q, kc, vc, bt, cl = _paged_case(5, 8, 2, 128, 16, 300, 120, torch.bfloat16, 33, [0, 17, 300, 64, 1])
+    ck, cv, offs, lens, _ = T.compress_paged(kc, vc, bt, cl, 16, 4, 8)
+    kt, cut = O.gather_paged_to_tnd(npy(kc), bt.cpu(), cl.cpu(), 16)
+    vt, _ = O.gather_paged_to_tnd(npy(vc), bt.cpu(), cl.cpu(), 16)
+    rk, rv, roffs = O.compress_kv(kt, vt, cut, 4, 8)
+    np.testing.assert_array_equal(offs.cpu().numpy(), roffs)
+    close(ck, rk, 1e-2)
+    close(cv, rv, 1e-2)
+
+
+def test_index_builders_bit_exact():
+    lens = [0, 1, 37, 300, 0, 129]
+    Tn = sum(lens)
+    cuq = _cu_t(lens)
+    assert SA.build_token_to_seq(cuq, Tn + 2, DEV).cpu().tolist() == O.build_token_to_seq(cuq.cpu(), Tn + 2).tolist()
+    offs = torch.tensor(O.comp_offsets_for(lens, 128), dtype=torch.int32, device=DEV)
+    got = HCA.build_hca_topk_idxs(cuq, offs, Tn, 16, 128)
+    np.testing.assert_array_equal(got.cpu().numpy(), O.build_hca_topk_idxs(cuq.cpu(), offs.cpu(), Tn, 16, 128))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_csa_indexer_bit_exact(dtype):
+    """Lightning indexer on 4 sequences, 512-dim compressed keys; ties and
+    fewer-than-k causal slots included (short sequences)."""
+    lens = [3, 40, 200, 513]
+    Tn = sum(lens)
+    g = torch.Generator().manual_seed(41)
+    q = torch.randn(Tn, 4, 512, generator=g).to(DEV, dtype)
+    k = torch.randn(Tn, 1, 512, generator=g).to(DEV, dtype)
+    cuq = _cu_t(lens)
+    ck, cv, offs = CSA.compress_kv_overlap(k, k, cuq, 4)
+    got = CSA.build_csa_topk_idxs(q, ck, cuq, offs, 8, 16, 4)
+    name = "bfloat16" if dtype == torch.bfloat16 else "float16"
+    ref = O.build_csa_topk_idxs(npy(q), npy(ck), cuq.cpu(), offs.cpu(), 8, 16, 4, name)
+    assert_topk_match(got.cpu().numpy(), ref, npy(q), npy(ck), lambda t: Tn, 8,
+                      2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10)
+
+
+def test_csa_hca_forward_bf16():
+    lens = [50, 200]
+    Tn = sum(lens)
+    g = torch.Generator().manual_seed(51)
+    q = torch.randn(Tn, 8, 128, generator=g).to(DEV, torch.bfloat16)
+    k = torch.randn(Tn, 2, 128, generator=g).to(DEV, torch.bfloat16)
+    v = torch.randn(Tn, 2, 128, generator=g).to(DEV, torch.bfloat16)
+    sink = torch.randn(8, generator=g).to(DEV)
+    cuq = _cu_t(lens)
+    out = CSA.csa_prefill_forward(q, k, v, cuq, 16, 8, 4, sink)
+    ref, _, _ = O.csa_prefill_forward(npy(q), npy(k), npy(v), cuq.cpu(), 16, 8, 4, sink.cpu(), "bfloat16")
+    close(out, ref, TOL16)
+    out = HCA.hca_prefill_forward(q, k, v, cuq, 16, 32, sink)
+    ref, _, _ = O.hca_prefill_forward(npy(q), npy(k), npy(v), cuq.cpu(), 16, 32, sink.cpu(), "bfloat16")
+    close(out, ref, TOL16)

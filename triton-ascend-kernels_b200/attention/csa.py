@@ -1,0 +1,100 @@
+"""CSA: overlapping KV compression + Lightning-indexer top-k sparse attention on B200.
+
+Drop-in for attention/csa.py of suluner/triton-ascend-kernels: the public
+functions keep the reference's names, arguments, defaults and return values
+(CSA:9-306).  Compression, index building and attention run as sm_100a kernels
+of libtak_b200.so; the host only sizes outputs (one small device->host copy of
+the sequence lengths, as the reference).
+
+Index rows follow the reference exactly except where it is itself undefined:
+among exactly equal indexer scores (and among the masked slots it picks when a
+query has fewer than top_k causal slots) torch.topk's order is backend-defined;
+here ties go to the lower slot and masked picks come in ascending slot order.
+"""
+
+import _tak_b200 as _t
+from sparse_attn_fwd import sparse_attn_prefill, sparse_attn_decode
+
+torch = _t.torch
+
+
+def compress_kv_overlap(k, v, cu_seqlens, m, *, gate=None):
+    """CSA-style overlapping pooling: kernel_size = 2*m, stride = m.
+
+    Args:
+        k, v: [total_tokens, num_kv_heads, head_dim]
+        cu_seqlens: [num_seqs + 1]
+        m: compression stride
+        gate: (keyword-only addition) optional [total_tokens] float32 logits;
+            each slot is then the softmax(gate)-weighted sum of its window
+            instead of the mean
+
+    Returns:
+        compressed_k, compressed_v: [total_compressed, num_kv_heads, head_dim]
+        comp_offsets: [num_seqs + 1] int32 cumulative offsets
+    """
+    return _t.compress_tnd(k, v, cu_seqlens, m, 2 * m, gate)
+
+
+def build_csa_topk_idxs(q, compressed_k, cu_seqlens, comp_offsets, n_win, top_k, m):
+    """topk_idxs [total_tokens, n_win + top_k] int32, -1 for padding:
+    [n_win sliding-window positions] + [top_k compressed indices + total_tokens]."""
+    _t.require_cuda(q, compressed_k)
+    dev = q.device
+    total_tokens, num_q_heads, head_dim = q.shape
+    num_kv_heads = compressed_k.shape[1]
+    cu = _t.as_i32(cu_seqlens, dev)
+    offs = _t.as_i32(comp_offsets, dev)
+    num_seqs = cu.numel() - 1
+    K = n_win + top_k
+    out = torch.full((total_tokens, K), -1, dtype=torch.int32, device=dev)
+    L = _t.lib()
+    st = _t.stream_of(q)
+    if total_tokens and n_win:
+        _t.check(L.tak_build_window_idxs(_t.ptr(cu), num_seqs, total_tokens, n_win, _t.ptr(out), K, st))
+    mc = _t.max_comp_per_seq(offs, compressed_k.shape[0])
+    if total_tokens and top_k and mc:
+        _t.check(L.tak_csa_indexer_topk(
+            _t.ptr(q), _t.strides(q), _t.ptr(compressed_k), _t.strides(compressed_k), _t.ptr(cu), None, _t.ptr(offs),
+            num_seqs, total_tokens, num_q_heads, num_kv_heads, head_dim, n_win, top_k, m, mc, _t.ptr(out), K,
+            _t.dtype_code(q), st))
+    return out
+
+
+def csa_prefill_forward(q, k, v, cu_seqlens, n_win, top_k, m, attn_sink=None, *, gate=None, return_lse=False):
+    """CSA prefill forward (TND layout): compress (kernel 2m, stride m), build
+    topk_idxs with the Lightning indexer, sparse attention over [K | compressed K]."""
+    compressed_k, compressed_v, comp_offsets = compress_kv_overlap(k, v, cu_seqlens, m, gate=gate)
+    topk_idxs = build_csa_topk_idxs(q, compressed_k, cu_seqlens, comp_offsets, n_win, top_k, m)
+    k_full = torch.cat([k, compressed_k], dim=0)
+    v_full = torch.cat([v, compressed_v], dim=0)
+    return sparse_attn_prefill(q, k_full, v_full, topk_idxs, cu_seqlens, attn_sink=attn_sink, return_lse=return_lse)
+
+
+def csa_decode_forward(q, k_cache, v_cache, block_tables, context_lens,
+                       n_win, top_k, m, block_size=16, attn_sink=None, *, return_lse=False):
+    """CSA decode forward (paged layout): compress each sequence's context
+    straight from the pages, index with the Lightning indexer, sparse decode."""
+    _t.require_cuda(q, k_cache, v_cache)
+    dev = q.device
+    num_seqs, num_q_heads, head_dim = q.shape
+    num_kv_heads = k_cache.shape[1]
+    ck, cv, offs, lens, offs_h = _t.compress_paged(k_cache, v_cache, block_tables, context_lens, block_size, m, 2 * m)
+    if sum(lens) == 0:
+        out = torch.zeros_like(q)
+        if return_lse:
+            return out, torch.full((num_seqs, num_q_heads), float("-inf"), device=dev)
+        return out
+    cl = _t.as_i32(context_lens, dev)
+    K = n_win + top_k
+    idx = torch.empty((num_seqs, K), dtype=torch.int32, device=dev)
+    L = _t.lib()
+    st = _t.stream_of(q)
+    _t.check(L.tak_build_decode_topk_idxs(_t.ptr(cl), _t.ptr(offs), num_seqs, n_win, top_k, 0, _t.ptr(idx), K, st))
+    mc = max((offs_h[i + 1] - offs_h[i] for i in range(num_seqs)), default=0)
+    if top_k and mc:
+        _t.check(L.tak_csa_indexer_topk(
+            _t.ptr(q), _t.strides(q), _t.ptr(ck), _t.strides(ck), None, _t.ptr(cl), _t.ptr(offs), num_seqs,
+            num_seqs, num_q_heads, num_kv_heads, head_dim, n_win, top_k, m, mc, _t.ptr(idx), K, _t.dtype_code(q), st))
+    return sparse_attn_decode(q, k_cache, v_cache, ck, cv, block_tables, idx, cl, num_win=n_win,
+                              block_size=block_size, attn_sink=attn_sink, return_lse=return_lse)

@@ -1,0 +1,393 @@
+// KV compression (CSA overlapping / HCA non-overlapping window pooling) and the
+// index-row builders of the CSA/HCA sparse paths.
+//
+// compress: slot i of sequence s pools rows [i*stride, min(i*stride + window,
+//   L_s)) of K and V (CSA:49-55 with window = 2m, stride = m; HCA:49-55 with
+//   window = stride = m').  Plain mean (the reference), or -- when a gate
+//   vector is given -- the softmax(gate)-weighted sum over the window's rows.
+//   Rows come from a TND tensor (cu_seqlens) or directly from a paged cache
+//   (block tables), which fuses the reference decode wrappers' page gather
+//   (CSA:225-253, HCA:204-230) into the pooling.  One CTA per (slot, KV head);
+//   each thread owns one 16-byte vector (8 elements) of the [K | V] row and
+//   accumulates in fp32.
+// index builders: window part (CSA:108-117, decode CSA:270-273), HCA
+//   compressed part (HCA:139-144, decode HCA:256-259), token -> sequence map
+//   (SA:253-260).
+// CSA indexer: Lightning-indexer scores q.k~ of the last query head against the
+//   last KV head (the reference's per-head writes leave the last head's choice,
+//   CSA:136-162), rounded to the input dtype like the reference's matmul
+//   output, causal iff slot*m < position, top-k in descending score order with
+//   ties to the lower slot, masked slots appended in ascending order when fewer
+//   than k are causal.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tak {
+
+__device__ __forceinline__ int find_slot_seq(const int32_t* offs, int num_seqs, int64_t slot) {
+  int lo = 0, hi = num_seqs - 1, ans = 0;
+  while (lo <= hi) {
+    const int mid = (lo + hi) >> 1;
+    if (offs[mid] <= slot) {
+      ans = mid;
+      lo = mid + 1;
+    } else {
+      hi = mid - 1;
+    }
+  }
+  // skip empty sequences that share the same offset
+  while (ans + 1 < num_seqs && offs[ans + 1] <= slot) ++ans;
+  return ans;
+}
+
+template <typename T, int VEC>
+__global__ void compress_kernel(const CompressArgs a) {
+  const int64_t slot = blockIdx.x;
+  const int h = blockIdx.y;
+  const int s = find_slot_seq(a.comp_offsets, a.num_seqs, slot);
+  const int i = static_cast<int>(slot - a.comp_offsets[s]);
+  const bool paged = a.cu_seqlens == nullptr;
+  const int L = paged ? a.context_lens[s] : (a.cu_seqlens[s + 1] - a.cu_seqlens[s]);
+  const int r0 = i * a.stride;
+  const int r1 = min(r0 + a.window, L);
+  const int nk = a.head_dim / VEC, nv = a.head_dim_v / VEC;
+  const int j = threadIdx.x;
+  if (j >= nk + nv) return;
+  const bool is_k = j < nk;
+  const int d0 = (is_k ? j : j - nk) * VEC;
+  const T* base = reinterpret_cast<const T*>(is_k ? a.k : a.v);
+  const int64_t* st = is_k ? a.sk : a.sv;
+  const int64_t sd = paged ? st[3] : st[2];
+
+  // window weights: plain mean, or softmax of the gate logits of the window
+  float gmax = 0.f, gsum = static_cast<float>(r1 - r0);
+  if (a.gate) {
+    gmax = -INFINITY;
+    for (int r = r0; r < r1; ++r) {
+      const float g = paged ? a.gate[a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]] * a.sg[0] +
+                                     (r % a.block_size) * a.sg[1]]
+                            : a.gate[(a.cu_seqlens[s] + r) * a.sg[0]];
+      gmax = fmaxf(gmax, g);
+    }
+    gsum = 0.f;
+    for (int r = r0; r < r1; ++r) {
+      const float g = paged ? a.gate[a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]] * a.sg[0] +
+                                     (r % a.block_size) * a.sg[1]]
+                            : a.gate[(a.cu_seqlens[s] + r) * a.sg[0]];
+      gsum += __expf(g - gmax);
+    }
+  }
+  float acc[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const T* row;
+    float w = 1.f;
+    if (paged) {
+      const int64_t page = a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]];
+      row = base + page * st[0] + h * st[1] + (r % a.block_size) * st[2];
+      if (a.gate) w = __expf(a.gate[page * a.sg[0] + (r % a.block_size) * a.sg[1]] - gmax);
+    } else {
+      const int64_t tok = a.cu_seqlens[s] + r;
+      row = base + tok * st[0] + h * st[1];
+      if (a.gate) w = __expf(a.gate[tok * a.sg[0]] - gmax);
+    }
+    if constexpr (VEC == 8) {
+      const uint4 u = *reinterpret_cast<const uint4*>(row + d0);
+      const uint32_t* pw = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = Elem<T>::unpack2(pw[e]);
+        acc[2 * e] += w * f.x;
+        acc[2 * e + 1] += w * f.y;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] += w * Elem<T>::to_f(row[(d0 + e) * sd]);
+    }
+  }
+  const float inv = gsum > 0.f ? 1.f / gsum : 0.f;
+  T* dst = reinterpret_cast<T*>(is_k ? a.ck : a.cv);
+  const int64_t* so = is_k ? a.sck : a.scv;
+  T* orow = dst + slot * so[0] + h * so[1];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) orow[(d0 + e) * so[2]] = Elem<T>::from_f(acc[e] * inv);
+}
+
+template <typename T>
+static int compress_typed(const CompressArgs& a, cudaStream_t st) {
+  const bool paged = a.cu_seqlens == nullptr;
+  const int64_t kd = paged ? a.sk[3] : a.sk[2];
+  const int64_t vd = paged ? a.sv[3] : a.sv[2];
+  bool vec = sizeof(T) == 2 && kd == 1 && vd == 1 && a.sck[2] == 1 && a.scv[2] == 1 && a.head_dim % 8 == 0 &&
+             a.head_dim_v % 8 == 0;
+  const int64_t* strides[] = {a.sk, a.sv};
+  for (const int64_t* s4 : strides)
+    for (int i = 0; i < (paged ? 3 : 2); ++i) vec = vec && (s4[i] % 8 == 0);
+  vec = vec && ((reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v)) & 15) == 0;
+  vec = vec && a.sck[0] % 8 == 0 && a.sck[1] % 8 == 0 && a.scv[0] % 8 == 0 && a.scv[1] % 8 == 0 &&
+        ((reinterpret_cast<uintptr_t>(a.ck) | reinterpret_cast<uintptr_t>(a.cv)) & 15) == 0;
+  dim3 grid(static_cast<unsigned>(a.num_compressed), a.num_kv_heads);
+  if constexpr (sizeof(T) == 2) {
+    if (vec) {
+      const int threads = (a.head_dim + a.head_dim_v) / 8;
+      if (threads > 1024) return set_error(2, "compress: head dim too large");
+      compress_kernel<T, 8><<<grid, threads, 0, st>>>(a);
+      return 0;
+    }
+  }
+  {
+    const int threads = a.head_dim + a.head_dim_v;
+    if (threads > 1024) return set_error(2, "compress: head dim too large");
+    compress_kernel<T, 1><<<grid, threads, 0, st>>>(a);
+  }
+  return 0;
+}
+
+int compress_launch(const CompressArgs& a, cudaStream_t st) {
+  if (a.num_compressed == 0 || a.num_kv_heads == 0) return 0;
+  if (a.dtype == kBF16) return compress_typed<__nv_bfloat16>(a, st);
+  if (a.dtype == kF16) return compress_typed<__half>(a, st);
+  return compress_typed<float>(a, st);
+}
+
+// ---------------------------------------------------------------------------
+// index builders
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int seq_of_token(const int32_t* cu, int num_seqs, int t) {
+  int lo = 0, hi = num_seqs - 1, ans = -1;
+  while (lo <= hi) {
+    const int mid = (lo + hi) >> 1;
+    if (cu[mid] <= t) {
+      ans = mid;
+      lo = mid + 1;
+    } else {
+      hi = mid - 1;
+    }
+  }
+  if (ans >= 0 && t >= cu[ans + 1]) ans = -1;
+  return ans;
+}
+
+__global__ void token_to_seq_kernel(const int32_t* cu, int num_seqs, int total_tokens, int32_t* out) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= total_tokens) return;
+  const int s = seq_of_token(cu, num_seqs, t);
+  out[t] = s < 0 ? 0 : s;
+}
+
+__global__ void window_idxs_kernel(const int32_t* cu, int num_seqs, int total_tokens, int n_win, int32_t* out,
+                                   int64_t ld) {
+  const int t = blockIdx.x;
+  if (t >= total_tokens) return;
+  const int s = seq_of_token(cu, num_seqs, t);
+  for (int wi = threadIdx.x; wi < n_win; wi += blockDim.x) {
+    int v = -1;
+    if (s >= 0) {
+      const int p = t - cu[s];
+      const int src = p - n_win + 1 + wi;
+      if (src >= 0) v = cu[s] + src;
+    }
+    out[t * ld + wi] = v;
+  }
+}
+
+__global__ void hca_idxs_kernel(const int32_t* cu, const int32_t* offs, int num_seqs, int total_tokens, int n_win,
+                                int max_n_comp, int m_prime, int32_t* out, int64_t ld) {
+  const int t = blockIdx.x;
+  const int s = seq_of_token(cu, num_seqs, t);
+  const int p = s >= 0 ? t - cu[s] : 0;
+  const int n_causal = s >= 0 ? min((p + m_prime - 1) / m_prime, max_n_comp) : 0;
+  for (int j = threadIdx.x; j < n_win + max_n_comp; j += blockDim.x) {
+    int v = -1;
+    if (s >= 0) {
+      if (j < n_win) {
+        const int src = p - n_win + 1 + j;
+        if (src >= 0) v = cu[s] + src;
+      } else if (j - n_win < n_causal) {
+        v = total_tokens + offs[s] + (j - n_win);
+      }
+    }
+    out[t * ld + j] = v;
+  }
+}
+
+// Decode rows: window = ctx - n_win + wi (>= 0); with m_prime > 0 the HCA
+// compressed part ctx + offs[s] + ci for ci < min(ceil(ctx/m'), n_c, cols),
+// with m_prime == 0 the compressed columns are set to -1 (the CSA indexer
+// fills them afterwards).
+__global__ void decode_idxs_kernel(const int32_t* context_lens, const int32_t* offs, int num_seqs, int n_win,
+                                   int n_comp_cols, int m_prime, int32_t* out, int64_t ld) {
+  const int s = blockIdx.x;
+  const int ctx = context_lens[s];
+  int n_causal = 0;
+  if (m_prime > 0) {
+    const int nc = offs[s + 1] - offs[s];
+    n_causal = min(min((ctx + m_prime - 1) / m_prime, nc), n_comp_cols);
+  }
+  for (int j = threadIdx.x; j < n_win + n_comp_cols; j += blockDim.x) {
+    int v = -1;
+    if (j < n_win) {
+      const int pos = ctx - n_win + j;
+      if (pos >= 0) v = pos;
+    } else if (j - n_win < n_causal) {
+      v = ctx + offs[s] + (j - n_win);
+    }
+    out[s * ld + j] = v;
+  }
+}
+
+int token_to_seq_launch(const int32_t* cu, int num_seqs, int total_tokens, int32_t* out, cudaStream_t st) {
+  if (total_tokens <= 0) return 0;
+  token_to_seq_kernel<<<(total_tokens + 255) / 256, 256, 0, st>>>(cu, num_seqs, total_tokens, out);
+  return 0;
+}
+
+int window_idxs_launch(const int32_t* cu, int num_seqs, int total_tokens, int n_win, int32_t* out, int64_t ld,
+                       cudaStream_t st) {
+  if (total_tokens <= 0 || n_win <= 0) return 0;
+  window_idxs_kernel<<<total_tokens, 64, 0, st>>>(cu, num_seqs, total_tokens, n_win, out, ld);
+  return 0;
+}
+
+int hca_idxs_launch(const int32_t* cu, const int32_t* offs, int num_seqs, int total_tokens, int n_win,
+                    int max_n_comp, int m_prime, int32_t* out, int64_t ld, cudaStream_t st) {
+  if (total_tokens <= 0 || n_win + max_n_comp <= 0) return 0;
+  hca_idxs_kernel<<<total_tokens, 128, 0, st>>>(cu, offs, num_seqs, total_tokens, n_win, max_n_comp, m_prime, out,
+                                                ld);
+  return 0;
+}
+
+int decode_idxs_launch(const int32_t* context_lens, const int32_t* offs, int num_seqs, int n_win, int n_comp_cols,
+                       int m_prime, int32_t* out, int64_t ld, cudaStream_t st) {
+  if (num_seqs <= 0 || n_win + n_comp_cols <= 0) return 0;
+  decode_idxs_kernel<<<num_seqs, 128, 0, st>>>(context_lens, offs, num_seqs, n_win, n_comp_cols, m_prime, out, ld);
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// CSA Lightning indexer: scores + top-k, one CTA per query row
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float round_to_t(float x) {
+  return Elem<T>::to_f(Elem<T>::from_f(x));
+}
+template <>
+__device__ __forceinline__ float round_to_t<float>(float x) {
+  return x;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
+  extern __shared__ float sc[];  // [max_comp_per_seq] scores, -inf once taken
+  __shared__ float red_v[8];
+  __shared__ int red_i[8];
+  const int row = blockIdx.x;
+  const bool decode = a.cu_seqlens == nullptr;
+  int s, pos;
+  if (decode) {
+    s = row;
+    pos = a.context_lens[s];
+  } else {
+    s = seq_of_token(a.cu_seqlens, a.num_seqs, row);
+    if (s < 0) return;
+    pos = row - a.cu_seqlens[s];
+  }
+  const int c0 = a.comp_offsets[s];
+  const int nc = a.comp_offsets[s + 1] - c0;
+  if (nc <= 0) return;
+  const int k_sel = min(a.top_k, nc);
+  // slot i is causal iff i*m < pos  <=>  i < ceil(pos/m)
+  const int n_valid = pos <= 0 ? 0 : min(nc, (pos + a.m - 1) / a.m);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const T* q = reinterpret_cast<const T*>(a.q) + row * a.sq[0] + (a.num_q_heads - 1) * a.sq[1];
+  const T* ck = reinterpret_cast<const T*>(a.ck) + static_cast<int64_t>(c0) * a.sck[0] + (a.num_kv_heads - 1) * a.sck[1];
+  float qr[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int d = lane + 32 * j;
+    qr[j] = d < a.head_dim ? Elem<T>::to_f(q[d * a.sq[2]]) : 0.f;
+  }
+  for (int i = warp; i < n_valid; i += nwarps) {
+    const T* kr = ck + static_cast<int64_t>(i) * a.sck[0];
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int d = lane + 32 * j;
+      if (d < a.head_dim) acc += qr[j] * Elem<T>::to_f(kr[d * a.sck[2]]);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) sc[i] = round_to_t<T>(acc);
+  }
+  __syncthreads();
+  const int64_t base = (decode ? static_cast<int64_t>(pos) : static_cast<int64_t>(a.total_tokens)) + c0;
+  int32_t* out = a.out + static_cast<int64_t>(row) * a.ld + a.n_win;
+  const int n_pick = min(k_sel, n_valid);
+  for (int r = 0; r < n_pick; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n_valid; i += blockDim.x) {
+      const float v = sc[i];
+      if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      red_v[warp] = bv;
+      red_i[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float v = red_v[0];
+      int ix = red_i[0];
+      for (int w = 1; w < nwarps; ++w)
+        if (red_v[w] > v || (red_v[w] == v && red_i[w] < ix)) {
+          v = red_v[w];
+          ix = red_i[w];
+        }
+      // a slot already taken is marked with NaN, which never wins a comparison
+      if (ix < n_valid) {
+        out[r] = static_cast<int32_t>(base + ix);
+        sc[ix] = __int_as_float(0x7fffffff);
+      } else {
+        out[r] = -1;
+      }
+    }
+    __syncthreads();
+  }
+  for (int r = n_pick + threadIdx.x; r < k_sel; r += blockDim.x) out[r] = static_cast<int32_t>(base + r);
+}
+
+int csa_indexer_launch(const IndexerArgs& a, cudaStream_t st) {
+  const int rows = a.cu_seqlens ? a.total_tokens : a.num_seqs;
+  if (rows <= 0) return 0;
+  if (a.head_dim > 512) return set_error(2, "csa indexer: head_dim > 512 is not supported");
+  const size_t smem = static_cast<size_t>(a.max_comp_per_seq > 0 ? a.max_comp_per_seq : 1) * sizeof(float);
+  if (smem > 200 * 1024) return set_error(2, "csa indexer: more than 51200 compressed slots in one sequence");
+  if (a.dtype == kBF16) {
+    cudaFuncSetAttribute(csa_indexer_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    csa_indexer_kernel<__nv_bfloat16><<<rows, 256, smem, st>>>(a);
+  } else if (a.dtype == kF16) {
+    cudaFuncSetAttribute(csa_indexer_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    csa_indexer_kernel<__half><<<rows, 256, smem, st>>>(a);
+  } else {
+    cudaFuncSetAttribute(csa_indexer_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    csa_indexer_kernel<float><<<rows, 256, smem, st>>>(a);
+  }
+  return 0;
+}
+
+}  // namespace tak

@@ -1,0 +1,126 @@
+// Internal host-side interface between the C-ABI layer (capi.cu) and the
+// kernel files.  Argument structs carry raw device pointers, sizes and element
+// strides exactly as the extern "C" entry points receive them.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace tak {
+
+// error reporting (capi.cu): stores a message for tak_last_error(), returns code
+int set_error(int code, const char* msg);
+int num_sms();
+// cuTensorMapEncodeTiled through the runtime's driver entry point
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides,
+                 CUtensorMapSwizzle swizzle);
+
+struct PagedDecodeArgs {
+  const void* q; int64_t sq[3];
+  const void* k_cache; int64_t sk[4];
+  const void* v_cache; int64_t sv[4];
+  const int32_t* block_tables; int64_t sbt[2];
+  const int32_t* context_lens;
+  void* out; int64_t so[3];
+  float* lse;
+  int num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks;
+  int64_t num_blocks, cache_rows;
+  float scale;
+  int dtype;
+  void* workspace; size_t workspace_bytes;
+  int split_pages;    // 0 = automatic
+  int force_generic;  // 1 = use the generic kernel (tests)
+};
+size_t paged_decode_workspace_bytes(const PagedDecodeArgs& a);
+int paged_decode_launch(const PagedDecodeArgs& a, cudaStream_t st);
+
+struct PrefillArgs {
+  const void* q; int64_t sq[3];
+  const void* k; int64_t sk[3];
+  const void* v; int64_t sv[3];
+  const int32_t* cu_seqlens;
+  void* out; int64_t so[3];
+  float* lse;
+  int num_seqs, total_tokens, num_q_heads, num_kv_heads, head_dim, head_dim_v;
+  float scale;
+  int causal;
+  int dtype;
+  int force_generic;
+};
+int prefill_launch(const PrefillArgs& a, cudaStream_t st);
+
+// Sparse attention, prefill (flat K/V rows) and decode (paged window + flat
+// compressed rows) forms share one argument struct.
+struct SparseArgs {
+  const void* q; int64_t sq[3];
+  // prefill: k/v rows [rows, H_kv, D]; decode: the paged caches
+  const void* k; int64_t sk[4];
+  const void* v; int64_t sv[4];
+  // decode only
+  const void* ck; int64_t sck[3];
+  const void* cv; int64_t scv[3];
+  const int32_t* block_tables; int64_t sbt[2];
+  const int32_t* context_lens;
+  int64_t num_compressed;
+  int num_win, block_size;
+  // both
+  const int32_t* topk; int64_t stk[2];
+  const float* sink;
+  void* out; int64_t so[3];
+  float* lse;
+  int num_tokens, num_q_heads, num_kv_heads, head_dim, head_dim_v, k_topk;
+  int64_t kv_rows;
+  float scale;
+  int dtype;
+  int decode;
+  int force_generic;
+};
+int sparse_launch(const SparseArgs& a, cudaStream_t st);
+
+struct CompressArgs {
+  const void* k; int64_t sk[4];
+  const void* v; int64_t sv[4];
+  const float* gate; int64_t sg[2];   // [T] (TND) or [num_blocks, P] (paged); may be null
+  // TND rows: row r of sequence s is token cu_seqlens[s] + r.
+  const int32_t* cu_seqlens;
+  // paged rows (cu_seqlens == null): page block_tables[s, r / P], offset r % P
+  const int32_t* block_tables; int64_t sbt[2];
+  const int32_t* context_lens;
+  int block_size;
+  const int32_t* comp_offsets;
+  int num_seqs;
+  int64_t num_compressed;
+  void* ck; int64_t sck[3];
+  void* cv; int64_t scv[3];
+  int num_kv_heads, head_dim, head_dim_v;
+  int stride, window;
+  int dtype;
+};
+int compress_launch(const CompressArgs& a, cudaStream_t st);
+
+int token_to_seq_launch(const int32_t* cu, int num_seqs, int total_tokens, int32_t* out, cudaStream_t st);
+int window_idxs_launch(const int32_t* cu, int num_seqs, int total_tokens, int n_win, int32_t* out, int64_t ld,
+                       cudaStream_t st);
+int hca_idxs_launch(const int32_t* cu, const int32_t* offs, int num_seqs, int total_tokens, int n_win,
+                    int max_n_comp, int m_prime, int32_t* out, int64_t ld, cudaStream_t st);
+int decode_idxs_launch(const int32_t* context_lens, const int32_t* offs, int num_seqs, int n_win, int n_comp_cols,
+                       int m_prime, int32_t* out, int64_t ld, cudaStream_t st);
+
+struct IndexerArgs {
+  const void* q; int64_t sq[3];
+  const void* ck; int64_t sck[3];
+  const int32_t* cu_seqlens;    // prefill: query rows per sequence
+  const int32_t* context_lens;  // decode (cu_seqlens == null): one query per sequence
+  const int32_t* comp_offsets;
+  int num_seqs, total_tokens, num_q_heads, num_kv_heads, head_dim;
+  int n_win, top_k, m;
+  int max_comp_per_seq;  // largest comp_offsets[s+1] - comp_offsets[s]
+  int32_t* out; int64_t ld;
+  int dtype;
+};
+int csa_indexer_launch(const IndexerArgs& a, cudaStream_t st);
+
+}  // namespace tak
