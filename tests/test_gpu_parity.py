@@ -227,19 +227,22 @@ def test_prefill_varlen_gqa(dtype, causal, kernel_path):
     assert out.dtype == dtype
 
 
-def test_prefill_edge_lengths(kernel_path):
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+def test_prefill_edge_lengths(D, causal, kernel_path):
     """Empty sequences, length-1 sequences, a 129-row sequence (one row past a
-    128-row tile), trailing tokens outside every sequence, strided q."""
-    lens = [0, 1, 129, 0, 64, 1]
+    128-row tile), sequences starting off the 128-row grid, trailing tokens
+    outside every sequence, strided q (last dim contiguous)."""
+    lens = [0, 1, 129, 0, 64, 1, 300, 127]
     Tn = sum(lens) + 3
     g = torch.Generator().manual_seed(1)
-    qb = torch.randn(Tn, 4, 2, 64, generator=g).to(DEV, torch.bfloat16)
+    qb = torch.randn(Tn, 4, 2, D, generator=g).to(DEV, torch.bfloat16)
     q = qb[:, :, 0, :]                                  # non-contiguous
-    k = torch.randn(Tn, 1, 64, generator=g).to(DEV, torch.bfloat16)
-    v = torch.randn(Tn, 1, 64, generator=g).to(DEV, torch.bfloat16)
+    k = torch.randn(Tn, 1, D, generator=g).to(DEV, torch.bfloat16)
+    v = torch.randn(Tn, 1, D, generator=g).to(DEV, torch.bfloat16)
     cuq = _cu_t(lens)
-    out, lse = FP.flash_attention_prefill(q, k, v, cuq, True, return_lse=True)
-    ref, ref_lse = O.prefill(npy(q), npy(k), npy(v), cuq.cpu(), True)
+    out, lse = FP.flash_attention_prefill(q, k, v, cuq, causal, return_lse=True)
+    ref, ref_lse = O.prefill(npy(q), npy(k), npy(v), cuq.cpu(), causal)
     close(out, ref, TOL16)
     close_lse(lse, ref_lse)
     assert (npy(out)[-3:] == 0).all()
@@ -251,6 +254,7 @@ def _paged_case(B, H, Hkv, D, P, max_ctx, pool, dtype, seed, ctx=None):
         ctx = torch.randint(1, max_ctx + 1, (B,), generator=g)
     ctx = torch.as_tensor(ctx, dtype=torch.int32)
     maxb = (max_ctx + P - 1) // P
+    pool = max(pool, int(((ctx + P - 1) // P).sum()) + 3)
     perm = torch.randperm(pool, generator=g).to(torch.int32)
     bt = torch.zeros(B, maxb, dtype=torch.int32)
     i = 0

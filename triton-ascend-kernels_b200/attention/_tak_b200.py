@@ -112,11 +112,13 @@ _ws = {}
 
 
 def workspace(device, stream_handle, nbytes):
-    """Per-(device, stream) scratch buffer, grown on demand (caching allocator)."""
+    """Per-(device, stream) scratch buffer, grown on demand.  Zero-filled when
+    allocated: the decode kernel keeps its arrival counters in it and leaves
+    them zero after every call."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), int(stream_handle.value or 0))
     buf = _ws.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _ws[key] = buf
     return buf
 

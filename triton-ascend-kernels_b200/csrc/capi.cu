@@ -129,7 +129,7 @@ int tak_flash_attention_prefill(const void* q, const int64_t* q_strides, const v
   TAK_REQUIRE(dtype >= 0 && dtype <= 2, "prefill: unknown dtype");
   TAK_REQUIRE(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
               "prefill: num_q_heads must be a multiple of num_kv_heads");
-  TAK_REQUIRE(head_dim > 0 && head_dim <= 512, "prefill: head_dim must be in [1, 512]");
+  TAK_REQUIRE(head_dim > 0 && head_dim <= 640, "prefill: head_dim must be in [1, 640]");
   TAK_REQUIRE(num_seqs >= 0 && total_tokens >= 0, "prefill: negative sizes");
   if (total_tokens == 0) return 0;
   TAK_REQUIRE(q && k && v && out && cu_seqlens && q_strides && k_strides && v_strides && out_strides,
@@ -179,7 +179,7 @@ int tak_paged_attention_decode(const void* q, const int64_t* q_strides, const vo
   TAK_REQUIRE(dtype >= 0 && dtype <= 2, "paged decode: unknown dtype");
   TAK_REQUIRE(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
               "paged decode: num_q_heads must be a multiple of num_kv_heads");
-  TAK_REQUIRE(head_dim > 0 && head_dim <= 512, "paged decode: head_dim must be in [1, 512]");
+  TAK_REQUIRE(head_dim > 0 && head_dim <= 640, "paged decode: head_dim must be in [1, 640]");
   TAK_REQUIRE(block_size > 0 && block_size <= cache_rows, "paged decode: block_size must be in [1, cache_rows]");
   TAK_REQUIRE(num_seqs >= 0 && max_blocks >= 0 && num_blocks >= 0, "paged decode: negative sizes");
   if (num_seqs == 0) return 0;
@@ -219,8 +219,8 @@ static int fill_sparse_common(SparseArgs& a, const void* q, const int64_t* q_str
   TAK_REQUIRE(dtype >= 0 && dtype <= 2, "sparse attention: unknown dtype");
   TAK_REQUIRE(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
               "sparse attention: num_q_heads must be a multiple of num_kv_heads");
-  TAK_REQUIRE(head_dim > 0 && head_dim <= 512 && head_dim_v > 0 && head_dim_v <= 512,
-              "sparse attention: head dims must be in [1, 512]");
+  TAK_REQUIRE(head_dim > 0 && head_dim <= 640 && head_dim_v > 0 && head_dim_v <= 640,
+              "sparse attention: head dims must be in [1, 640]");
   TAK_REQUIRE(k_topk >= 0, "sparse attention: negative k_topk");
   TAK_REQUIRE(q && out && q_strides && out_strides && (k_topk == 0 || (topk_idxs && topk_strides)),
               "sparse attention: null pointer");

@@ -12,7 +12,7 @@
 
 namespace tak {
 
-constexpr int kMaxDPerLane = 16;  // head dims up to 512
+constexpr int kMaxDPerLane = 20;  // head dims up to 640 (MLA: 576 + 64 spare)
 
 template <typename T>
 struct RowPair {

@@ -21,8 +21,10 @@
 //           mma.sync m16n8k16 (query heads padded to 16 rows), online softmax
 //           in registers, base-2 exponentials.
 //   epilogue: the 4 warps merge through shared memory; single-split sequences
-//           write the output directly, others write (O, max, sum) partials that
-//           paged_decode_combine merges with warp shuffles.
+//           write the output directly, others write (O, max, sum) partials to
+//           the workspace and bump an arrival counter; the last split CTA of a
+//           (sequence, KV head) merges all partials (no second launch) and
+//           resets the counter to zero.
 // Generic path (any dtype incl. fp32, any strides / block size / head dim):
 //   one CTA of 4 warps per (sequence, query head); each warp walks a strided
 //   subset of the keys (lanes split the head dim), then the warps merge.
@@ -42,6 +44,7 @@ struct DecodeParams {
   float* lse;    // [B, H] contiguous, may be null
   float* ws_o;   // [B, H, max_splits, D]
   float* ws_ml;  // [B, H, max_splits, 2]
+  int* ws_count; // [B, H_kv * head_chunks] arrival counters, zero between calls
   int B, H, Hkv, G, D, block_size, pages_per_split, max_splits, head_chunks;
   float scale_log2;
 };
@@ -285,34 +288,46 @@ __global__ void __launch_bounds__(160, 2)
       }
     }
   }
-}
+  if (n_splits == 1) return;
 
-// Merge the split partials of each (sequence, query head): one warp per pair.
-template <typename T>
-__global__ void paged_decode_combine_kernel(const DecodeParams p) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= p.B * p.H) return;
-  const int seq = w / p.H, h = w % p.H;
-  const int ctx = p.context_lens[seq];
-  const int split_tokens = p.pages_per_split * p.block_size;
-  const int n = (ctx + split_tokens - 1) / split_tokens;
-  if (ctx <= 0 || n <= 1) return;
-  const int64_t base = (static_cast<int64_t>(seq) * p.H + h) * p.max_splits;
-  float M = -INFINITY;
-  for (int i = lane; i < n; i += 32) M = fmaxf(M, p.ws_ml[(base + i) * 2]);
-  M = warp_max(M);
-  const float Mu = (M == -INFINITY) ? 0.f : M;
-  float L = 0.f;
-  for (int i = lane; i < n; i += 32) L += p.ws_ml[(base + i) * 2 + 1] * fast_exp2(p.ws_ml[(base + i) * 2] - Mu);
-  L = warp_sum(L);
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  for (int d = lane; d < p.D; d += 32) {
-    float acc = 0.f;
-    for (int i = 0; i < n; ++i) acc += p.ws_o[(base + i) * p.D + d] * fast_exp2(p.ws_ml[(base + i) * 2] - Mu);
-    reinterpret_cast<T*>(p.out)[seq * p.so_s + h * p.so_h + d * p.so_d] = Elem<T>::from_f(acc * inv);
+  // ---------------- split-KV merge by the last CTA of this (sequence, KV head) ----------------
+  __shared__ int s_last;
+  __threadfence();
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  int* counter = p.ws_count + static_cast<int64_t>(seq) * gridDim.y + blockIdx.y;
+  if (tid == 0) {
+    const int prev = atomicAdd(counter, 1);
+    s_last = prev == n_splits - 1;
   }
-  if (lane == 0 && p.lse) p.lse[seq * p.H + h] = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (!s_last) return;
+  __threadfence();
+  float* wts = obuf;                      // [16][n_splits] merge weights, then [16] 1/L
+  float* inv_l = obuf + 16 * n_splits;
+  if (tid < gcnt) {
+    const int64_t base = (static_cast<int64_t>(seq) * p.H + h0 + tid) * p.max_splits;
+    float M = -INFINITY;
+    for (int i = 0; i < n_splits; ++i) M = fmaxf(M, __ldcg(&p.ws_ml[(base + i) * 2]));
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float L = 0.f;
+    for (int i = 0; i < n_splits; ++i) {
+      const float w = fast_exp2(__ldcg(&p.ws_ml[(base + i) * 2]) - Mu);
+      wts[tid * n_splits + i] = w;
+      L += __ldcg(&p.ws_ml[(base + i) * 2 + 1]) * w;
+    }
+    inv_l[tid] = L > 0.f ? 1.f / L : 0.f;
+    if (p.lse) p.lse[seq * p.H + h0 + tid] = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  for (int i = tid; i < gcnt * D; i += 128) {
+    const int r = i / D, d = i % D;
+    const int64_t base = (static_cast<int64_t>(seq) * p.H + h0 + r) * p.max_splits;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < n_splits; ++j) acc += wts[r * n_splits + j] * __ldcg(&p.ws_o[(base + j) * D + d]);
+    reinterpret_cast<T*>(p.out)[seq * p.so_s + (h0 + r) * p.so_h + d * p.so_d] = Elem<T>::from_f(acc * inv_l[r]);
+  }
+  if (tid == 0) *counter = 0;  // leave the counter zero for the next call
 }
 
 // ---------------------------------------------------------------------------
@@ -335,7 +350,7 @@ struct DecodeGenericParams {
   float scale_log2;
 };
 
-constexpr int kGenMaxDPerLane = 16;  // head_dim <= 512
+constexpr int kGenMaxDPerLane = 20;  // head_dim <= 640
 
 template <typename T>
 __global__ void __launch_bounds__(128) paged_decode_generic_kernel(const DecodeGenericParams p) {
@@ -433,11 +448,23 @@ static bool decode_fast_path_ok(const PagedDecodeArgs& a, int* ch) {
   return true;
 }
 
+// Workspace layout (256-byte aligned regions): arrival counters [B, H_kv *
+// head_chunks] int32 (must be zero before the first call; every call leaves
+// them zero), then (max, sum) [B, H, splits, 2] and O partials [B, H, splits, D]
+// in fp32.
+static int64_t counters_bytes(const PagedDecodeArgs& a) {
+  const int hc = (a.num_q_heads / a.num_kv_heads + 15) / 16;
+  return ((static_cast<int64_t>(a.num_seqs) * a.num_kv_heads * hc * 4 + 255) / 256) * 256;
+}
+
 size_t paged_decode_workspace_bytes(const PagedDecodeArgs& a) {
   const int units = a.num_seqs * a.num_kv_heads * ((a.num_q_heads / a.num_kv_heads + 15) / 16);
   const int pps = pick_pages_per_split(a, units);
   const int64_t max_splits = (a.max_blocks + pps - 1) / pps;
-  return static_cast<size_t>(a.num_seqs) * a.num_q_heads * max_splits * (a.head_dim + 2) * sizeof(float) + 256;
+  if (max_splits <= 1) return 0;
+  return static_cast<size_t>(counters_bytes(a) +
+                             static_cast<int64_t>(a.num_seqs) * a.num_q_heads * max_splits * (a.head_dim + 2) * 4 +
+                             256);
 }
 
 static int encode_cache_map(CUtensorMap* map, const void* base, const int64_t* st, int64_t num_blocks,
@@ -470,7 +497,9 @@ static int launch_fast(const PagedDecodeArgs& a, int pps, int max_splits, int he
   p.out = a.out;
   p.so_s = a.so[0]; p.so_h = a.so[1]; p.so_d = a.so[2];
   p.lse = a.lse;
-  float* ws = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(a.workspace) + 255) & ~uintptr_t(255));
+  uint8_t* ws8 = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(a.workspace) + 255) & ~uintptr_t(255));
+  p.ws_count = reinterpret_cast<int*>(ws8);
+  float* ws = reinterpret_cast<float*>(ws8 + counters_bytes(a));
   p.ws_ml = ws;
   p.ws_o = ws + static_cast<int64_t>(a.num_seqs) * a.num_q_heads * max_splits * 2;
   p.B = a.num_seqs; p.H = a.num_q_heads; p.Hkv = a.num_kv_heads; p.G = a.num_q_heads / a.num_kv_heads;
@@ -481,10 +510,6 @@ static int launch_fast(const PagedDecodeArgs& a, int pps, int max_splits, int he
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   dim3 grid(max_splits, a.num_kv_heads * head_chunks, a.num_seqs);
   kern<<<grid, 160, SMEM, st>>>(mk, mv, p);
-  if (max_splits > 1) {
-    const int warps = a.num_seqs * a.num_q_heads;
-    paged_decode_combine_kernel<T><<<(warps + 3) / 4, 128, 0, st>>>(p);
-  }
   return 0;
 }
 
@@ -507,7 +532,7 @@ static int launch_generic(const PagedDecodeArgs& a, cudaStream_t st) {
 
 int paged_decode_launch(const PagedDecodeArgs& a, cudaStream_t st) {
   if (a.num_seqs == 0 || a.num_q_heads == 0) return 0;
-  if (a.head_dim > 32 * kGenMaxDPerLane) return set_error(2, "paged decode: head_dim > 512 is not supported");
+  if (a.head_dim > 32 * kGenMaxDPerLane) return set_error(2, "paged decode: head_dim > 640 is not supported");
   int ch = 0;
   const bool fast = !a.force_generic && decode_fast_path_ok(a, &ch);
   if (!fast) {
@@ -519,7 +544,7 @@ int paged_decode_launch(const PagedDecodeArgs& a, cudaStream_t st) {
   const int head_chunks = (G + 15) / 16;
   const int pps = pick_pages_per_split(a, a.num_seqs * a.num_kv_heads * head_chunks);
   const int max_splits = (a.max_blocks + pps - 1) / pps;
-  if (a.workspace_bytes < paged_decode_workspace_bytes(a) && max_splits > 1)
+  if (max_splits > 1 && (a.workspace == nullptr || a.workspace_bytes < paged_decode_workspace_bytes(a)))
     return set_error(2, "paged decode: workspace too small");
 #define TAK_DEC(T, D, CH) return launch_fast<T, D, CH>(a, pps, max_splits, head_chunks, st)
 #define TAK_DEC_CH(T, D)   \

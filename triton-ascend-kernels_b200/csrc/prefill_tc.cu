@@ -1,13 +1,371 @@
 // Varlen flash prefill on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Semantics: attention/flash_attention_prefill.py of the reference (kernel
+// FP:11-102): per sequence of cu_seqlens and query head h, softmax(scale *
+// Q K^T [+ causal mask]) V with KV head h / (H / H_kv), output acc / (l + 1e-6)
+// (FP:97), plus the natural-log LSE.
+//
+// One CTA = one tile of up to 128 query rows of one sequence x one query head.
+// Tiles are 128-row blocks aligned to global token positions (clipped to the
+// sequence that owns the block's first row) plus one "head piece" per sequence
+// for its rows before the first aligned boundary, so the schedule needs no
+// host-side table (the reference builds one with a host loop, FP:144-153).
+// Causal tiles stop at the diagonal block (the reference sweeps every block,
+// FP:60).  Aligned tiles are issued last-block-first (longest work first).
+//
+// Warp roles (192 threads):
+//   warp 4      TMA producer: Q tile once, then K and V blocks of 128 rows into
+//               2-stage rings (128-byte swizzle, one 64-column box per half).
+//   warp 5      TMEM allocator + single-thread tcgen05.mma issuer:
+//               S_j = Q K_j^T (SS, M=N=128, K=16 x 8) into one of 3 TMEM
+//               buffers, then O += P_j V_j (TS: P read from TMEM, V from smem,
+//               MN-major) -- QK of block j+1 is issued before PV of block j so
+//               the tensor core works while the softmax warps run.
+//   warps 0-3   softmax: thread i owns row i (TMEM lane i): loads S_j, masks,
+//               online max with lazy rescaling (O and l are rescaled only when
+//               the max grows by more than 2^8), P = exp2(s - m) packed to 16
+//               bits back into the S buffer's first 64 columns; epilogue reads
+//               O, normalises, stores the row and its LSE.
+// TMEM: O in columns [0,128), S/P buffers in [128,512).
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace tak {
 
+struct PrefillTcParams {
+  const int32_t* cu_seqlens;
+  int num_seqs, total_tokens, H, Hkv, G, n_aligned, causal;
+  void* out;
+  int64_t so_t, so_h;
+  float* lse;
+  float scale_log2;
+};
+
+namespace pf {
+constexpr int BM = 128, BN = 128, D = 128;
+constexpr int TILE = 128 * 128;                   // one 64-column block of 128 rows (bytes)
+constexpr int QOFF = 0, KOFF = 2 * TILE, VOFF = 6 * TILE;
+constexpr int BAROFF = 10 * TILE;                 // 160 KB of tiles, then barriers
+constexpr int NBAR = 19;
+constexpr int SMEM = BAROFF + NBAR * 8 + 16 + 1024;
+constexpr float kRescaleThreshold = 8.f;          // log2 units
+}  // namespace pf
+
+__device__ __forceinline__ int pf_find_seq(const int32_t* cu, int n, int t) {
+  int lo = 0, hi = n - 1, ans = -1;
+  while (lo <= hi) {
+    const int mid = (lo + hi) >> 1;
+    if (cu[mid] <= t) {
+      ans = mid;
+      lo = mid + 1;
+    } else {
+      hi = mid - 1;
+    }
+  }
+  return ans;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(192, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const PrefillTcParams p) {
+  using namespace pf;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAROFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [3]
+  uint64_t* p_full = bars + 12;  // [3]
+  uint64_t* s_free = bars + 15;  // [3]
+  uint64_t* o_done = bars + 18;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int h = blockIdx.x;
+  const int slot = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = p.num_seqs;
+  const int cu_end = p.cu_seqlens[S];
+
+  // ---------------- which rows does this CTA own (CTA-uniform) ----------------
+  int s, row0, row1;
+  if (slot < p.n_aligned) {
+    row0 = (p.n_aligned - 1 - slot) * BM;
+    if (row0 >= cu_end) return;
+    s = pf_find_seq(p.cu_seqlens, S, row0);
+    row1 = min(row0 + BM, static_cast<int>(p.cu_seqlens[s + 1]));
+  } else if (slot < p.n_aligned + S) {
+    s = slot - p.n_aligned;
+    const int st = p.cu_seqlens[s], en = p.cu_seqlens[s + 1];
+    if (st % BM == 0 || st >= en) return;
+    row0 = st;
+    row1 = min((st / BM + 1) * BM, en);
+  } else {
+    // rows past the last sequence: zeros (FP:189)
+    for (int t = cu_end + warp; t < p.total_tokens; t += 6) {
+      T* o = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(t) * p.so_t + static_cast<int64_t>(h) * p.so_h;
+      for (int d = lane; d < D; d += 32) o[d] = Elem<T>::from_f(0.f);
+      if (lane == 0 && p.lse) p.lse[static_cast<int64_t>(t) * p.H + h] = -INFINITY;
+    }
+    return;
+  }
+  const int seq_start = p.cu_seqlens[s];
+  const int seq_len = p.cu_seqlens[s + 1] - seq_start;
+  const int rows_valid = row1 - row0;
+  const int p0 = row0 - seq_start;
+  const int kv_keys = p.causal ? min(seq_len, p0 + rows_valid) : seq_len;
+  const int n_kv = (kv_keys + BN - 1) / BN;
+  const int kvh = h / p.G;
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&s_free[i], 1);
+    }
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t taddr = *tmem_holder;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, 2 * TILE);
+      tma_load_3d(smem + QOFF, &tmQ, q_full, 0, h, row0);
+      tma_load_3d(smem + QOFF + TILE, &tmQ, q_full, 64, h, row0);
+      for (int j = 0; j < n_kv && !*abort_flag; ++j) {
+        const int st = j & 1;
+        const int key0 = seq_start + j * BN;
+        if (j >= 2 && !mbar_wait(&k_empty[st], ((j >> 1) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], 2 * TILE);
+        tma_load_3d(smem + KOFF + st * 2 * TILE, &tmK, &k_full[st], 0, kvh, key0);
+        tma_load_3d(smem + KOFF + st * 2 * TILE + TILE, &tmK, &k_full[st], 64, kvh, key0);
+        if (j >= 2 && !mbar_wait(&v_empty[st], ((j >> 1) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], 2 * TILE);
+        tma_load_3d(smem + VOFF + st * 2 * TILE, &tmV, &v_full[st], 0, kvh, key0);
+        tma_load_3d(smem + VOFF + st * 2 * TILE + TILE, &tmV, &v_full[st], 64, kvh, key0);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr int AB = sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      const uint32_t idesc_qk = tc_idesc_f16(AB, BM, BN, 0);
+      const uint32_t idesc_pv = tc_idesc_f16(AB, BM, D, 1);
+      bool ok = mbar_wait(q_full, 0);
+      auto issue_qk = [&](int j) -> bool {
+        const int b = j % 3, st = j & 1;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
+        if (j >= 3 && !mbar_wait(&s_free[b], ((j / 3) - 1) & 1)) return false;
+        tc_fence_after();
+        const uint32_t d_tmem = taddr + 128 + b * 128;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t koff = (kk >> 2) * TILE + (kk & 3) * 32;
+          const uint64_t a = tc_sdesc_sw128(sbase + QOFF + koff, 16, 1024);
+          const uint64_t bd = tc_sdesc_sw128(sbase + KOFF + st * 2 * TILE + koff, 16, 1024);
+          tc_mma_ss(d_tmem, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[b]);
+        tc_commit(&k_empty[st]);
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (*abort_flag) break;
+        if (j + 1 < n_kv && !(ok = issue_qk(j + 1))) break;
+        const int b = j % 3, st = j & 1;
+        if (!(ok = mbar_wait(&p_full[b], (j / 3) & 1))) break;
+        if (!(ok = mbar_wait(&v_full[st], (j >> 1) & 1))) break;
+        tc_fence_after();
+        const uint32_t p_tmem = taddr + 128 + b * 128;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t bd = tc_sdesc_sw128(sbase + VOFF + st * 2 * TILE + kk * 2048, TILE, 1024);
+          tc_mma_ts(taddr, p_tmem + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(o_done);
+        tc_commit(&v_empty[st]);
+        tc_commit(&s_free[b]);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ---------------- softmax + epilogue: warps 0-3, thread = row ----------------
+    const int r = tid;
+    const bool row_ok = r < rows_valid;
+    const int lim = !row_ok ? 0 : (p.causal ? min(seq_len, p0 + r + 1) : seq_len);
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    float m_run = -INFINITY, m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int b = j % 3;
+      if (!(ok = mbar_wait(&s_full[b], (j / 3) & 1))) break;
+      tc_fence_after();
+      uint32_t sr[128];
+      const uint32_t s_tmem = taddr + lane_off + 128 + b * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + c * 32, sr + c * 32);
+      tmem_ld_wait();
+      const int nvalid = lim - j * BN;  // keys [0, nvalid) of this block are visible to the row
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float v = c < nvalid ? __uint_as_float(sr[c]) : -INFINITY;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m_run, mx * p.scale_log2);
+      const bool need = m_new != -INFINITY && m_new > m_used + kRescaleThreshold;
+      const bool rescale_o = need && m_used != -INFINITY;
+      if (__any_sync(0xffffffffu, rescale_o)) {
+        // O holds PV of blocks < j: wait for the last of them, then rescale rows in place
+        if (!(ok = mbar_wait(o_done, (j - 1) & 1))) break;
+        tc_fence_after();
+        const float f = rescale_o ? fast_exp2(m_used - m_new) : 1.f;
+        uint32_t orow[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(taddr + lane_off + c * 32, orow);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * f);
+          tmem_st32(taddr + lane_off + c * 32, orow);
+        }
+        tmem_st_wait();
+        l *= f;
+      }
+      if (need) m_used = m_new;
+      m_run = m_new;
+      const float mu = m_used == -INFINITY ? 0.f : m_used;
+      uint32_t pk[64];
+      float ls = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float a = (2 * c < nvalid) ? fast_exp2(__uint_as_float(sr[2 * c]) * p.scale_log2 - mu) : 0.f;
+        const float bb = (2 * c + 1 < nvalid) ? fast_exp2(__uint_as_float(sr[2 * c + 1]) * p.scale_log2 - mu) : 0.f;
+        ls += a + bb;
+        pk[c] = Elem<T>::pack2(a, bb);
+      }
+      l += ls;
+      tmem_st32(s_tmem, pk);
+      tmem_st32(s_tmem + 32, pk + 32);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[b]);
+    }
+    if (ok && n_kv > 0) ok = mbar_wait(o_done, (n_kv - 1) & 1);
+    if (!ok) *abort_flag = 1;
+    tc_fence_after();
+    float o[128];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) tmem_ld32(taddr + lane_off + c * 32, reinterpret_cast<uint32_t*>(o) + c * 32);
+    tmem_ld_wait();
+    if (row_ok) {
+      const float f = (m_used == -INFINITY || n_kv == 0) ? 0.f : fast_exp2(m_used - m_run);
+      const float inv = (l > 0.f && ok) ? f / (l * f + 1e-6f) : 0.f;
+      T* orow = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(row0 + r) * p.so_t +
+                static_cast<int64_t>(h) * p.so_h;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint4 u;
+        u.x = Elem<T>::pack2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
+        u.y = Elem<T>::pack2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+        u.z = Elem<T>::pack2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+        u.w = Elem<T>::pack2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+        *reinterpret_cast<uint4*>(orow + 8 * c) = u;
+      }
+      if (p.lse)
+        p.lse[static_cast<int64_t>(row0 + r) * p.H + h] = (l > 0.f && ok) ? (m_used + __log2f(l)) * kLn2 : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(taddr, 512);
+  }
+}
+
+static int encode_tnd_map(CUtensorMap* m, const void* base, const int64_t* st, int64_t T, int64_t heads) {
+  const uint64_t dims[3] = {128, static_cast<uint64_t>(heads), static_cast<uint64_t>(T)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(st[1] * 2), static_cast<uint64_t>(st[0] * 2)};
+  const uint32_t box[3] = {64, 1, 128};
+  const uint32_t es[3] = {1, 1, 1};
+  return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, base, dims, strides, box, es, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+static bool tma_ok(const void* ptr, const int64_t* st) {
+  if (reinterpret_cast<uintptr_t>(ptr) & 15) return false;
+  if (st[2] != 1) return false;
+  return st[0] > 0 && st[1] > 0 && (st[0] * 2) % 16 == 0 && (st[1] * 2) % 16 == 0;
+}
+
 int prefill_tc_launch(const PrefillArgs& a, cudaStream_t st, bool* handled) {
-  (void)a;
-  (void)st;
   *handled = false;
+  if (a.dtype == kF32 || a.head_dim != 128 || a.head_dim_v != 128) return 0;
+  if (!tma_ok(a.q, a.sq) || !tma_ok(a.k, a.sk) || !tma_ok(a.v, a.sv)) return 0;
+  if (a.so[2] != 1 || (a.so[0] % 8) || (a.so[1] % 8) || (reinterpret_cast<uintptr_t>(a.out) & 15)) return 0;
+  const int n_aligned = (a.total_tokens + pf::BM - 1) / pf::BM;
+  if (static_cast<int64_t>(n_aligned) + a.num_seqs + 1 > 65535) return 0;
+  CUtensorMap mq, mk, mv;
+  if (int r = encode_tnd_map(&mq, a.q, a.sq, a.total_tokens, a.num_q_heads)) return r;
+  if (int r = encode_tnd_map(&mk, a.k, a.sk, a.total_tokens, a.num_kv_heads)) return r;
+  if (int r = encode_tnd_map(&mv, a.v, a.sv, a.total_tokens, a.num_kv_heads)) return r;
+  PrefillTcParams p{};
+  p.cu_seqlens = a.cu_seqlens;
+  p.num_seqs = a.num_seqs;
+  p.total_tokens = a.total_tokens;
+  p.H = a.num_q_heads;
+  p.Hkv = a.num_kv_heads;
+  p.G = a.num_q_heads / a.num_kv_heads;
+  p.n_aligned = n_aligned;
+  p.causal = a.causal;
+  p.out = a.out;
+  p.so_t = a.so[0];
+  p.so_h = a.so[1];
+  p.lse = a.lse;
+  p.scale_log2 = a.scale * kLog2e;
+  dim3 grid(a.num_q_heads, n_aligned + a.num_seqs + 1);
+  if (a.dtype == kBF16) {
+    cudaFuncSetAttribute(prefill_tc_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
+    prefill_tc_kernel<__nv_bfloat16><<<grid, 192, pf::SMEM, st>>>(mq, mk, mv, p);
+  } else {
+    cudaFuncSetAttribute(prefill_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
+    prefill_tc_kernel<__half><<<grid, 192, pf::SMEM, st>>>(mq, mk, mv, p);
+  }
+  *handled = true;
   return 0;
 }
 
