@@ -71,10 +71,10 @@ int tak_flash_attention_prefill(const void* q, const int64_t* q_strides, const v
  * q [B,H,D], k_cache/v_cache [num_blocks,H_kv,cache_rows,D],
  * block_tables [B,max_blocks], context_lens [B], out [B,H,D].
  * workspace: device scratch of at least tak_paged_attention_decode_workspace_size()
- * bytes for the split-KV partials and arrival counters (may be NULL if that
- * size is 0).  It must be zero-filled before its first use; every call leaves
- * the counters zero again.  Calls that share a workspace must not overlap on
- * the GPU (issue them on one stream).
+ * bytes for the split-KV partials (may be NULL if that size is 0); no
+ * initialisation needed.  Calls that share a workspace must not overlap on the
+ * GPU (issue them on one stream).  Context rows past the block table
+ * (ctx > max_blocks * block_size) are ignored.
  * split_pages: pages per split-KV work unit, 0 = automatic.
  */
 size_t tak_paged_attention_decode_workspace_size(int64_t num_seqs, int64_t num_q_heads, int64_t num_kv_heads,

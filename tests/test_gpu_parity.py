@@ -347,6 +347,27 @@ def test_sparse_prefill_mla_shape(with_sink, kernel_path):
     close_lse(lse, ref_lse)
 
 
+def test_sparse_prefill_cfg3_index_width():
+    """cfg3 index width: 2048 sorted unique indices per token drawn causally
+    from a 32768-row latent KV (MQA, 64 heads, 576/512), -1 padding for early
+    positions; 16 tokens checked against the oracle."""
+    g = torch.Generator().manual_seed(23)
+    rows, K, Tn = 32768, 2048, 16
+    q = torch.randn(Tn, 64, 576, generator=g).to(DEV, torch.bfloat16)
+    k = torch.randn(rows, 1, 576, generator=g).to(DEV, torch.bfloat16)
+    pos = torch.tensor([100, 2047, 2048, 5000] + list(range(28000, 28012)))
+    idx = torch.full((Tn, K), -1, dtype=torch.int32)
+    for t in range(Tn):
+        n = min(K, int(pos[t]) + 1)
+        idx[t, :n] = torch.randperm(int(pos[t]) + 1, generator=g)[:n].sort().values.to(torch.int32)
+    idx = idx.to(DEV)
+    sink = torch.randn(64, generator=g).to(DEV)
+    out, lse = SA.sparse_attn_prefill(q, k, k[..., :512], idx, None, sink, return_lse=True)
+    ref, ref_lse = O.sparse_prefill(npy(q), npy(k), npy(k[..., :512]), idx.cpu(), None, sink.cpu(), acc=np.float32)
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+
+
 def test_sparse_prefill_gqa_fp32_and_oob():
     q, k, v, idx, sink = _sparse_case(40, 8, 2, 128, 128, 300, 64, torch.float32, 22)
     idx[5, 3] = 10_000            # past the last row: masked

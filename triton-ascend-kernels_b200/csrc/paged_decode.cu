@@ -21,10 +21,9 @@
 //           mma.sync m16n8k16 (query heads padded to 16 rows), online softmax
 //           in registers, base-2 exponentials.
 //   epilogue: the 4 warps merge through shared memory; single-split sequences
-//           write the output directly, others write (O, max, sum) partials to
-//           the workspace and bump an arrival counter; the last split CTA of a
-//           (sequence, KV head) merges all partials (no second launch) and
-//           resets the counter to zero.
+//           write the output directly, others write (O, max, sum) partials
+//           that paged_decode_combine_kernel merges (one CTA per sequence and
+//           KV head; all splits' loads in flight at once).
 // Generic path (any dtype incl. fp32, any strides / block size / head dim):
 //   one CTA of 4 warps per (sequence, query head); each warp walks a strided
 //   subset of the keys (lanes split the head dim), then the warps merge.
@@ -44,8 +43,8 @@ struct DecodeParams {
   float* lse;    // [B, H] contiguous, may be null
   float* ws_o;   // [B, H, max_splits, D]
   float* ws_ml;  // [B, H, max_splits, 2]
-  int* ws_count; // [B, H_kv * head_chunks] arrival counters, zero between calls
   int B, H, Hkv, G, D, block_size, pages_per_split, max_splits, head_chunks;
+  int max_ctx;  // max_blocks * block_size: rows past the block table are ignored
   float scale_log2;
 };
 
@@ -73,7 +72,7 @@ __global__ void __launch_bounds__(160, 2)
   const int seq = blockIdx.z;
   const int h0 = kvh * p.G + hc * 16;
   const int gcnt = min(16, p.G - hc * 16);
-  const int ctx = p.context_lens[seq];
+  const int ctx = min(p.context_lens[seq], p.max_ctx);
   const int split_tokens = p.pages_per_split * p.block_size;
   const int tok0 = split * split_tokens;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -288,46 +287,59 @@ __global__ void __launch_bounds__(160, 2)
       }
     }
   }
-  if (n_splits == 1) return;
+}
 
-  // ---------------- split-KV merge by the last CTA of this (sequence, KV head) ----------------
-  __shared__ int s_last;
-  __threadfence();
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  int* counter = p.ws_count + static_cast<int64_t>(seq) * gridDim.y + blockIdx.y;
-  if (tid == 0) {
-    const int prev = atomicAdd(counter, 1);
-    s_last = prev == n_splits - 1;
+// Merge the split partials of one (sequence, KV head, head chunk): weights of
+// every split first (shared memory), then one output element per thread and
+// iteration with all splits' loads independent (no serial latency chain).
+template <typename T>
+__global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeParams p) {
+  __shared__ float wts[16 * 64];
+  __shared__ float inv_l[16];
+  const int kvh = blockIdx.y / p.head_chunks, hc = blockIdx.y % p.head_chunks, seq = blockIdx.x;
+  const int ctx = min(p.context_lens[seq], p.max_ctx);
+  const int split_tokens = p.pages_per_split * p.block_size;
+  const int n = (ctx + split_tokens - 1) / split_tokens;
+  if (ctx <= 0 || n <= 1) return;
+  const int h0 = kvh * p.G + hc * 16;
+  const int gcnt = min(16, p.G - hc * 16);
+  const int tid = threadIdx.x;
+  for (int i = tid; i < gcnt * n; i += 128) {
+    const int r = i / n, j = i % n;
+    wts[r * n + j] = p.ws_ml[((static_cast<int64_t>(seq) * p.H + h0 + r) * p.max_splits + j) * 2];
   }
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  if (!s_last) return;
-  __threadfence();
-  float* wts = obuf;                      // [16][n_splits] merge weights, then [16] 1/L
-  float* inv_l = obuf + 16 * n_splits;
+  __syncthreads();
   if (tid < gcnt) {
     const int64_t base = (static_cast<int64_t>(seq) * p.H + h0 + tid) * p.max_splits;
     float M = -INFINITY;
-    for (int i = 0; i < n_splits; ++i) M = fmaxf(M, __ldcg(&p.ws_ml[(base + i) * 2]));
+    for (int j = 0; j < n; ++j) M = fmaxf(M, wts[tid * n + j]);
     const float Mu = (M == -INFINITY) ? 0.f : M;
     float L = 0.f;
-    for (int i = 0; i < n_splits; ++i) {
-      const float w = fast_exp2(__ldcg(&p.ws_ml[(base + i) * 2]) - Mu);
-      wts[tid * n_splits + i] = w;
-      L += __ldcg(&p.ws_ml[(base + i) * 2 + 1]) * w;
+    for (int j = 0; j < n; ++j) {
+      const float w = fast_exp2(wts[tid * n + j] - Mu);
+      wts[tid * n + j] = w;
+      L += p.ws_ml[(base + j) * 2 + 1] * w;
     }
     inv_l[tid] = L > 0.f ? 1.f / L : 0.f;
     if (p.lse) p.lse[seq * p.H + h0 + tid] = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
   }
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-  for (int i = tid; i < gcnt * D; i += 128) {
-    const int r = i / D, d = i % D;
-    const int64_t base = (static_cast<int64_t>(seq) * p.H + h0 + r) * p.max_splits;
-    float acc = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < n_splits; ++j) acc += wts[r * n_splits + j] * __ldcg(&p.ws_o[(base + j) * D + d]);
-    reinterpret_cast<T*>(p.out)[seq * p.so_s + (h0 + r) * p.so_h + d * p.so_d] = Elem<T>::from_f(acc * inv_l[r]);
+  __syncthreads();
+  for (int i = tid; i < gcnt * p.D; i += 128) {
+    const int r = i / p.D, d = i % p.D;
+    const float* src = p.ws_o + ((static_cast<int64_t>(seq) * p.H + h0 + r) * p.max_splits) * p.D + d;
+    const float* w = wts + r * n;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int j = 0;
+    for (; j + 4 <= n; j += 4) {
+      a0 += w[j] * src[(j + 0) * p.D];
+      a1 += w[j + 1] * src[(j + 1) * p.D];
+      a2 += w[j + 2] * src[(j + 2) * p.D];
+      a3 += w[j + 3] * src[(j + 3) * p.D];
+    }
+    for (; j < n; ++j) a0 += w[j] * src[j * p.D];
+    reinterpret_cast<T*>(p.out)[seq * p.so_s + (h0 + r) * p.so_h + d * p.so_d] =
+        Elem<T>::from_f((a0 + a1 + a2 + a3) * inv_l[r]);
   }
-  if (tid == 0) *counter = 0;  // leave the counter zero for the next call
 }
 
 // ---------------------------------------------------------------------------
@@ -346,7 +358,7 @@ struct DecodeGenericParams {
   void* out;
   int64_t so_s, so_h, so_d;
   float* lse;
-  int H, G, D, block_size;
+  int H, G, D, block_size, max_ctx;
   float scale_log2;
 };
 
@@ -356,7 +368,7 @@ template <typename T>
 __global__ void __launch_bounds__(128) paged_decode_generic_kernel(const DecodeGenericParams p) {
   const int seq = blockIdx.y, h = blockIdx.x, kvh = h / p.G;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ctx = p.context_lens[seq];
+  const int ctx = min(p.context_lens[seq], p.max_ctx);
   const T* q = reinterpret_cast<const T*>(p.q) + seq * p.sq_s + h * p.sq_h;
   const T* kc = reinterpret_cast<const T*>(p.kc);
   const T* vc = reinterpret_cast<const T*>(p.vc);
@@ -421,7 +433,9 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(const DecodeG
 // host side
 // ---------------------------------------------------------------------------
 static int pick_pages_per_split(const PagedDecodeArgs& a, int units) {
-  if (a.split_pages > 0) return a.split_pages;
+  // at most 64 splits per sequence (the combine kernel's weight table)
+  const int min_pps = a.max_blocks > 64 ? (a.max_blocks + 63) / 64 : 1;
+  if (a.split_pages > 0) return a.split_pages > min_pps ? a.split_pages : min_pps;
   // Aim for ~16 waves of 2 CTAs/SM assuming contexts fill half the table on
   // average, with at most 1024 tokens per split.
   const int64_t target_ctas = static_cast<int64_t>(num_sms()) * 2 * 16;
@@ -430,6 +444,7 @@ static int pick_pages_per_split(const PagedDecodeArgs& a, int units) {
   if (pps < 1) pps = 1;
   if (pps > cap) pps = cap;
   if (pps > a.max_blocks) pps = a.max_blocks > 0 ? a.max_blocks : 1;
+  if (pps < min_pps) pps = min_pps;
   return static_cast<int>(pps);
 }
 
@@ -448,22 +463,14 @@ static bool decode_fast_path_ok(const PagedDecodeArgs& a, int* ch) {
   return true;
 }
 
-// Workspace layout (256-byte aligned regions): arrival counters [B, H_kv *
-// head_chunks] int32 (must be zero before the first call; every call leaves
-// them zero), then (max, sum) [B, H, splits, 2] and O partials [B, H, splits, D]
-// in fp32.
-static int64_t counters_bytes(const PagedDecodeArgs& a) {
-  const int hc = (a.num_q_heads / a.num_kv_heads + 15) / 16;
-  return ((static_cast<int64_t>(a.num_seqs) * a.num_kv_heads * hc * 4 + 255) / 256) * 256;
-}
-
+// Workspace layout (256-byte aligned): (max, sum) [B, H, splits, 2], then O
+// partials [B, H, splits, D], fp32.  Nothing in it needs initialising.
 size_t paged_decode_workspace_bytes(const PagedDecodeArgs& a) {
   const int units = a.num_seqs * a.num_kv_heads * ((a.num_q_heads / a.num_kv_heads + 15) / 16);
   const int pps = pick_pages_per_split(a, units);
   const int64_t max_splits = (a.max_blocks + pps - 1) / pps;
   if (max_splits <= 1) return 0;
-  return static_cast<size_t>(counters_bytes(a) +
-                             static_cast<int64_t>(a.num_seqs) * a.num_q_heads * max_splits * (a.head_dim + 2) * 4 +
+  return static_cast<size_t>(static_cast<int64_t>(a.num_seqs) * a.num_q_heads * max_splits * (a.head_dim + 2) * 4 +
                              256);
 }
 
@@ -497,19 +504,19 @@ static int launch_fast(const PagedDecodeArgs& a, int pps, int max_splits, int he
   p.out = a.out;
   p.so_s = a.so[0]; p.so_h = a.so[1]; p.so_d = a.so[2];
   p.lse = a.lse;
-  uint8_t* ws8 = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(a.workspace) + 255) & ~uintptr_t(255));
-  p.ws_count = reinterpret_cast<int*>(ws8);
-  float* ws = reinterpret_cast<float*>(ws8 + counters_bytes(a));
+  float* ws = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(a.workspace) + 255) & ~uintptr_t(255));
   p.ws_ml = ws;
   p.ws_o = ws + static_cast<int64_t>(a.num_seqs) * a.num_q_heads * max_splits * 2;
   p.B = a.num_seqs; p.H = a.num_q_heads; p.Hkv = a.num_kv_heads; p.G = a.num_q_heads / a.num_kv_heads;
   p.D = D; p.block_size = a.block_size; p.pages_per_split = pps; p.max_splits = max_splits;
   p.head_chunks = head_chunks;
+  p.max_ctx = a.max_blocks * a.block_size;
   p.scale_log2 = a.scale * kLog2e;
   auto kern = paged_decode_tc_kernel<T, D, CH, NS>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
   dim3 grid(max_splits, a.num_kv_heads * head_chunks, a.num_seqs);
   kern<<<grid, 160, SMEM, st>>>(mk, mv, p);
+  if (max_splits > 1) paged_decode_combine_kernel<T><<<dim3(a.num_seqs, a.num_kv_heads * head_chunks), 128, 0, st>>>(p);
   return 0;
 }
 
@@ -524,6 +531,7 @@ static int launch_generic(const PagedDecodeArgs& a, cudaStream_t st) {
   p.out = a.out; p.so_s = a.so[0]; p.so_h = a.so[1]; p.so_d = a.so[2];
   p.lse = a.lse;
   p.H = a.num_q_heads; p.G = a.num_q_heads / a.num_kv_heads; p.D = a.head_dim; p.block_size = a.block_size;
+  p.max_ctx = a.max_blocks * a.block_size;
   p.scale_log2 = a.scale * kLog2e;
   dim3 grid(a.num_q_heads, a.num_seqs);
   paged_decode_generic_kernel<T><<<grid, 128, 0, st>>>(p);

@@ -1,14 +1,459 @@
-// Top-k sparse attention on the 5th-generation tensor cores (tcgen05 + TMEM).
+// Top-k sparse attention (prefill form) on the 5th-generation tensor cores.
+//
+// Semantics: attention/sparse_attn_fwd.py of the reference (kernel SA:10-98):
+// token t, query head h attends to rows topk_idxs[t, :] of K/V (negative =
+// masked; past the last row = masked here), softmax with an optional per-head
+// sink logit that enters only the denominator (SA:86-92), l = 0 -> output 0
+// (SA:94-95); plus the natural-log LSE.  Also covers the MLA-style latent
+// layout the reference cannot express (Dqk = 576 = 512 latent + 64 rope,
+// Dv = 512, V a view of K's first 512 columns).
+//
+// One CTA = one query token x one group of up to 64 query heads sharing a KV
+// head (MQA: all 64 heads of the token).  The 64 head rows are the MMA's
+// M = 64 dimension, so every gathered K/V row is read once for all heads.
+//
+// Warp roles (192 threads):
+//   warp 4   gather producer: Q rows once (TMA), then for each tile of 64
+//            indices lanes 0-15 issue TMA gather4 loads (4 arbitrary rows x 64
+//            columns each, 128-byte swizzle) into a 2-stage ring; masked
+//            indices use row -1, which TMA fills with zeros; a 64-bit validity
+//            mask per stage goes to shared memory.
+//   warp 5   TMEM allocator + single-thread tcgen05.mma issuer:
+//            S_j = Q K_j^T (M=64, N=64, K=16 x Dqk/16) into TMEM lanes 16-31
+//            of each quadrant (two buffers), O += P_j V_j (M=64, N<=256 per
+//            instruction, V from the same gathered rows when it is a view of
+//            K) into TMEM lanes 0-15.  QK of tile j+1 is issued before PV of
+//            tile j.
+//   warps 0-3 softmax: TMEM loads of shape 16x32bx2 let all 32 threads of a
+//            warp work on its 16 head rows (two threads per row, 32 columns
+//            each); lazy rescaling of O (only when the max grows by > 2^8);
+//            P written to shared memory (K-major, swizzled) for the PV MMA;
+//            epilogue folds the sink, normalises and stores the rows.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace tak {
 
-int sparse_tc_launch(const SparseArgs& a, cudaStream_t st, bool* handled) {
-  (void)a;
-  (void)st;
-  *handled = false;
+struct SparseTcParams {
+  const int32_t* topk;
+  int64_t stk0, stk1;
+  int k_topk;
+  int64_t kv_rows;
+  const float* sink;
+  void* out;
+  int64_t so_t, so_h;
+  float* lse;
+  int H, Hkv, G, head_chunks;
+  float scale_log2;
+};
+
+__device__ __forceinline__ void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int col, int r0, int r1,
+                                            int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// 16 TMEM lanes x 32 columns per half-warp: threads 0-15 read columns
+// [c, c+32) of lanes base+t, threads 16-31 columns [c+32, c+64) of lanes base+t-16.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32], 32;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16x2(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x32.b32 [%0], 32, {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+template <int DQK, int DV, bool SHARED>
+struct SpLayout {
+  static constexpr int BLK = 64 * 128;  // 64 rows x 128 B: one 64-column block of a 64-row tile
+  static constexpr int NQB = DQK / 64, NVB = DV / 64;
+  static constexpr int QOFF = 0;
+  static constexpr int STAGE = (NQB + (SHARED ? 0 : NVB)) * BLK;
+  static constexpr int KVOFF = NQB * BLK;
+  static constexpr int POFF = KVOFF + 2 * STAGE;
+  static constexpr int MASKOFF = POFF + BLK;
+  static constexpr int BAROFF = MASKOFF + 16;
+  static constexpr int NBAR = 10;
+  static constexpr int SMEM = BAROFF + NBAR * 8 + 16 + 1024;
+  static constexpr int TMEM_COLS = DV <= 128 ? 128 : (DV <= 256 ? 256 : 512);
+};
+
+template <typename T, int DQK, int DV, bool SHARED>
+__global__ void __launch_bounds__(192, 1)
+    sparse_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const SparseTcParams p) {
+  using L = SpLayout<DQK, DV, SHARED>;
+  constexpr int BN = 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* masks = reinterpret_cast<uint64_t*>(smem + L::MASKOFF);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAROFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* p_full = bars + 7;
+  uint64_t* p_free = bars + 8;
+  uint64_t* o_done = bars + 9;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int t = blockIdx.x;
+  const int kvh = blockIdx.y / p.head_chunks;
+  const int hc = blockIdx.y % p.head_chunks;
+  const int h0 = kvh * p.G + hc * 64;
+  const int nrows = min(64, p.G - hc * 64);
+  const int n_tiles = (p.k_topk + BN - 1) / BN;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(p_free, 1);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_holder, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t taddr = *tmem_holder;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == 4) {
+    // ---------------- gather producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      if (!SHARED) tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, L::NQB * L::BLK);
+#pragma unroll 1
+      for (int cb = 0; cb < L::NQB; ++cb)
+        tma_load_2d(smem + L::QOFF + cb * L::BLK, &tmQ, q_full, cb * 64, t * p.H + h0);
+    }
+    const int32_t* idx_row = p.topk + static_cast<int64_t>(t) * p.stk0;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int st = j & 1;
+      // warp-uniform: lane 0 waits for the stage, every lane follows its verdict
+      int go = 1;
+      if (lane == 0) {
+        go = (j < 2 || mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1)) && !*abort_flag;
+        if (!go) *abort_flag = 1;
+      }
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      int coord[4];
+      uint32_t vb = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = j * BN + 4 * (lane & 15) + i;
+        int64_t r = c < p.k_topk ? idx_row[c * p.stk1] : -1;
+        const bool ok = r >= 0 && r < p.kv_rows;
+        coord[i] = ok ? static_cast<int>(r * p.Hkv + kvh) : -1;
+        vb |= (ok && lane < 16) ? (1u << i) : 0u;
+      }
+      // validity of the tile's 64 rows: row 4l+i <- bit i of lane l
+      uint64_t mask = 0;
+#pragma unroll
+      for (int l = 0; l < 16; ++l) mask |= static_cast<uint64_t>(__shfl_sync(0xffffffffu, vb, l)) << (4 * l);
+      if (lane == 0) {
+        masks[st] = mask;
+        mbar_arrive_expect_tx(&kv_full[st], L::STAGE);
+      }
+      __syncwarp();
+      if (lane < 16) {
+        uint8_t* kst = smem + L::KVOFF + st * L::STAGE;
+#pragma unroll 1
+        for (int cb = 0; cb < L::NQB; ++cb)
+          tma_gather4(kst + cb * L::BLK + lane * 512, &tmK, &kv_full[st], cb * 64, coord[0], coord[1], coord[2],
+                      coord[3]);
+        if (!SHARED) {
+#pragma unroll 1
+          for (int cb = 0; cb < L::NVB; ++cb)
+            tma_gather4(kst + (L::NQB + cb) * L::BLK + lane * 512, &tmV, &kv_full[st], cb * 64, coord[0], coord[1],
+                        coord[2], coord[3]);
+        }
+      }
+      __syncwarp();
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && n_tiles > 0) {
+      constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      constexpr int NPV = DV < 256 ? DV : 256;
+      const uint32_t idesc_qk = tc_idesc_f16(AB, 64, BN, 0);
+      const uint32_t idesc_pv = tc_idesc_f16(AB, 64, NPV, 1);
+      bool ok = mbar_wait(q_full, 0);
+      auto issue_qk = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) return false;
+        tc_fence_after();
+        const uint32_t d_tmem = taddr + (16u << 16) + st * 64;
+        const uint32_t kbase = sbase + L::KVOFF + st * L::STAGE;
+#pragma unroll 1
+        for (int kk = 0; kk < DQK / 16; ++kk) {
+          const uint32_t koff = (kk >> 2) * L::BLK + (kk & 3) * 32;
+          tc_mma_ss(d_tmem, tc_sdesc_sw128(sbase + L::QOFF + koff, 16, 1024), tc_sdesc_sw128(kbase + koff, 16, 1024),
+                    idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[st]);
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (*abort_flag) break;
+        if (j + 1 < n_tiles && !(ok = issue_qk(j + 1))) break;
+        const int st = j & 1;
+        if (!(ok = mbar_wait(p_full, j & 1))) break;
+        tc_fence_after();
+        const uint32_t vbase = sbase + L::KVOFF + st * L::STAGE + (SHARED ? 0 : L::NQB * L::BLK);
+#pragma unroll
+        for (int half = 0; half < (DV + 255) / 256; ++half) {
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t a = tc_sdesc_sw128(sbase + L::POFF + kk * 32, 16, 1024);
+            const uint64_t b = tc_sdesc_sw128(vbase + half * 4 * L::BLK + kk * 2048, L::BLK, 1024);
+            tc_mma_ss(taddr + half * 256, a, b, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        tc_commit(o_done);
+        tc_commit(&kv_empty[st]);
+        tc_commit(p_free);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ---------------- softmax + epilogue: warps 0-3, 16 head rows per warp ----------------
+    const int t16 = lane & 15, hi = lane >> 4;
+    const int row = 16 * warp + t16;
+    const bool row_ok = row < nrows;
+    const int head = h0 + row;
+    const bool has_sink = p.sink != nullptr;
+    const float sink_log2 = (has_sink && row_ok) ? p.sink[head] * kLog2e : -INFINITY;
+    const uint32_t s_lane = static_cast<uint32_t>(32 * warp + 16) << 16;
+    const uint32_t o_lane = static_cast<uint32_t>(32 * warp) << 16;
+    float m_run = -INFINITY, m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      if (!(ok = mbar_wait(&s_full[b], (j >> 1) & 1))) break;
+      if (!(ok = mbar_wait(&kv_full[b], (j >> 1) & 1))) break;  // orders the producer's mask write
+      tc_fence_after();
+      uint32_t sr[32];
+      tmem_ld16x2(taddr + s_lane + b * 64, sr);
+      tmem_ld_wait();
+      const uint32_t vbits = static_cast<uint32_t>(masks[b] >> (32 * hi));
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 32; ++c)
+        if ((vbits >> c) & 1u) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float m_new = fmaxf(m_run, mx * p.scale_log2);
+      const bool need = m_new != -INFINITY && m_new > m_used + 8.f;
+      const bool resc = need && m_used != -INFINITY;
+      if (__any_sync(0xffffffffu, resc)) {
+        if (!(ok = mbar_wait(o_done, (j - 1) & 1))) break;
+        tc_fence_after();
+        const float f = resc ? fast_exp2(m_used - m_new) : 1.f;
+        uint32_t orow[32];
+#pragma unroll 1
+        for (int c = 0; c < DV / 64; ++c) {
+          tmem_ld16x2(taddr + o_lane + c * 64, orow);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * f);
+          tmem_st16x2(taddr + o_lane + c * 64, orow);
+        }
+        tmem_st_wait();
+        l *= f;
+      }
+      if (need) m_used = m_new;
+      m_run = m_new;
+      const float mu = m_used == -INFINITY ? 0.f : m_used;
+      uint32_t pk[16];
+      float ls = 0.f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float a = ((vbits >> (2 * c)) & 1u) ? fast_exp2(__uint_as_float(sr[2 * c]) * p.scale_log2 - mu) : 0.f;
+        const float bb =
+            ((vbits >> (2 * c + 1)) & 1u) ? fast_exp2(__uint_as_float(sr[2 * c + 1]) * p.scale_log2 - mu) : 0.f;
+        ls += a + bb;
+        pk[c] = Elem<T>::pack2(a, bb);
+      }
+      l += ls;
+      if (j >= 1 && !(ok = mbar_wait(p_free, (j - 1) & 1))) break;
+      uint8_t* prow = smem + L::POFF + row * 128;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int chunk = (hi * 4 + k) ^ (row & 7);
+        *reinterpret_cast<uint4*>(prow + chunk * 16) = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_tiles > 0) ok = mbar_wait(o_done, (n_tiles - 1) & 1);
+    if (!ok) *abort_flag = 1;
+    tc_fence_after();
+    const float l_tot = l + __shfl_xor_sync(0xffffffffu, l, 16);
+    const float M = fmaxf(m_run, sink_log2);
+    const float f = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - M);
+    const float Lsum = l_tot * f + (has_sink && row_ok ? fast_exp2(sink_log2 - M) : 0.f);
+    const float inv = (Lsum > 0.f && ok) ? f / Lsum : 0.f;
+    T* orow_g = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(t) * p.so_t + static_cast<int64_t>(head) * p.so_h;
+#pragma unroll 1
+    for (int c = 0; c < DV / 64; ++c) {
+      uint32_t o[32];
+      if (n_tiles > 0) {
+        tmem_ld16x2(taddr + o_lane + c * 64, o);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0u;
+      }
+      if (row_ok) {
+        T* dst = orow_g + c * 64 + hi * 32;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint4 u;
+          u.x = Elem<T>::pack2(__uint_as_float(o[8 * k + 0]) * inv, __uint_as_float(o[8 * k + 1]) * inv);
+          u.y = Elem<T>::pack2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv);
+          u.z = Elem<T>::pack2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
+          u.w = Elem<T>::pack2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + 8 * k) = u;
+        }
+      }
+    }
+    if (row_ok && hi == 0 && p.lse)
+      p.lse[static_cast<int64_t>(t) * p.H + head] = (Lsum > 0.f && ok) ? (M + __log2f(Lsum)) * kLn2 : -INFINITY;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(taddr, L::TMEM_COLS);
+  }
+}
+
+// 2-D view [rows, cols] of a 16-bit tensor, box {64 columns, box_rows rows}, 128-byte swizzle.
+static int encode_rows_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t row_stride,
+                           int box_rows) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(row_stride * 2)};
+  const uint32_t box[2] = {64, static_cast<uint32_t>(box_rows)};
+  const uint32_t es[2] = {1, 1};
+  return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base, dims, strides, box, es, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <typename T, int DQK, int DV, bool SHARED>
+static int launch_sparse_tc(const SparseArgs& a, cudaStream_t st) {
+  using L = SpLayout<DQK, DV, SHARED>;
+  const int G = a.num_q_heads / a.num_kv_heads;
+  CUtensorMap mq, mk, mv;
+  // q as [T * H, Dqk] rows, k (and v) as [rows * H_kv, D] rows
+  if (int r = encode_rows_map(&mq, a.q, static_cast<int64_t>(a.num_tokens) * a.num_q_heads, DQK, a.sq[1], 64)) return r;
+  const int64_t krow = a.num_kv_heads == 1 ? a.sk[0] : a.sk[1];
+  if (int r = encode_rows_map(&mk, a.k, a.kv_rows * a.num_kv_heads, DQK, krow, 1)) return r;
+  if (SHARED) {
+    mv = mk;
+  } else {
+    const int64_t vrow = a.num_kv_heads == 1 ? a.sv[0] : a.sv[1];
+    if (int r = encode_rows_map(&mv, a.v, a.kv_rows * a.num_kv_heads, DV, vrow, 1)) return r;
+  }
+  SparseTcParams p{};
+  p.topk = a.topk;
+  p.stk0 = a.stk[0];
+  p.stk1 = a.stk[1];
+  p.k_topk = a.k_topk;
+  p.kv_rows = a.kv_rows;
+  p.sink = a.sink;
+  p.out = a.out;
+  p.so_t = a.so[0];
+  p.so_h = a.so[1];
+  p.lse = a.lse;
+  p.H = a.num_q_heads;
+  p.Hkv = a.num_kv_heads;
+  p.G = G;
+  p.head_chunks = (G + 63) / 64;
+  p.scale_log2 = a.scale * kLog2e;
+  auto kern = sparse_tc_kernel<T, DQK, DV, SHARED>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+  dim3 grid(a.num_tokens, a.num_kv_heads * p.head_chunks);
+  kern<<<grid, 192, L::SMEM, st>>>(mq, mk, mv, p);
   return 0;
+}
+
+static bool rows_ok(const void* ptr, const int64_t* s, int hkv) {
+  if (reinterpret_cast<uintptr_t>(ptr) & 15) return false;
+  if (s[2] != 1) return false;
+  const int64_t row = hkv == 1 ? s[0] : s[1];
+  if (hkv > 1 && s[0] != hkv * s[1]) return false;
+  return row > 0 && (row * 2) % 16 == 0;
+}
+
+int sparse_tc_launch(const SparseArgs& a, cudaStream_t st, bool* handled) {
+  *handled = false;
+  if (a.decode || a.dtype == kF32) return 0;
+  const int G = a.num_q_heads / a.num_kv_heads;
+  if (G > 64 && G % 64 != 0) return 0;
+  if (a.num_tokens > 2147483647 / 64 || a.kv_rows * a.num_kv_heads > 2147483647) return 0;
+  // q rows [T * H, Dqk] must be dense over heads
+  if ((reinterpret_cast<uintptr_t>(a.q) & 15) || a.sq[2] != 1 || a.sq[0] != static_cast<int64_t>(a.num_q_heads) * a.sq[1] ||
+      (a.sq[1] * 2) % 16 != 0)
+    return 0;
+  if (!rows_ok(a.k, a.sk, a.num_kv_heads) || !rows_ok(a.v, a.sv, a.num_kv_heads)) return 0;
+  if (a.so[2] != 1 || (a.so[0] % 8) || (a.so[1] % 8) || (reinterpret_cast<uintptr_t>(a.out) & 15)) return 0;
+  const bool shared = a.v == a.k && a.sv[0] == a.sk[0] && a.sv[1] == a.sk[1] && a.sv[2] == a.sk[2] &&
+                      a.head_dim_v <= a.head_dim;
+  const int dq = a.head_dim, dv = a.head_dim_v;
+  int r = -1;
+  if (a.dtype == kBF16) {
+    if (shared && dq == 576 && dv == 512) r = launch_sparse_tc<__nv_bfloat16, 576, 512, true>(a, st);
+    else if (dq == 128 && dv == 128) r = launch_sparse_tc<__nv_bfloat16, 128, 128, false>(a, st);
+    else if (dq == 64 && dv == 64) r = launch_sparse_tc<__nv_bfloat16, 64, 64, false>(a, st);
+    else if (dq == 256 && dv == 256) r = launch_sparse_tc<__nv_bfloat16, 256, 256, false>(a, st);
+  } else {
+    if (shared && dq == 576 && dv == 512) r = launch_sparse_tc<__half, 576, 512, true>(a, st);
+    else if (dq == 128 && dv == 128) r = launch_sparse_tc<__half, 128, 128, false>(a, st);
+    else if (dq == 64 && dv == 64) r = launch_sparse_tc<__half, 64, 64, false>(a, st);
+    else if (dq == 256 && dv == 256) r = launch_sparse_tc<__half, 256, 256, false>(a, st);
+  }
+  if (r < 0) return 0;
+  *handled = true;
+  return r;
 }
 
 }  // namespace tak
