@@ -295,6 +295,7 @@ __global__ void __launch_bounds__(160, 2)
 template <typename T>
 __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeParams p) {
   __shared__ float wts[16 * 64];
+  __shared__ float lsum[16 * 64];
   __shared__ float inv_l[16];
   const int kvh = blockIdx.y / p.head_chunks, hc = blockIdx.y % p.head_chunks, seq = blockIdx.x;
   const int ctx = min(p.context_lens[seq], p.max_ctx);
@@ -304,13 +305,16 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeP
   const int h0 = kvh * p.G + hc * 16;
   const int gcnt = min(16, p.G - hc * 16);
   const int tid = threadIdx.x;
+  // every (head, split) max and sum in one parallel round of loads
   for (int i = tid; i < gcnt * n; i += 128) {
     const int r = i / n, j = i % n;
-    wts[r * n + j] = p.ws_ml[((static_cast<int64_t>(seq) * p.H + h0 + r) * p.max_splits + j) * 2];
+    const float2 ml = *reinterpret_cast<const float2*>(
+        &p.ws_ml[((static_cast<int64_t>(seq) * p.H + h0 + r) * p.max_splits + j) * 2]);
+    wts[r * n + j] = ml.x;
+    lsum[r * n + j] = ml.y;
   }
   __syncthreads();
   if (tid < gcnt) {
-    const int64_t base = (static_cast<int64_t>(seq) * p.H + h0 + tid) * p.max_splits;
     float M = -INFINITY;
     for (int j = 0; j < n; ++j) M = fmaxf(M, wts[tid * n + j]);
     const float Mu = (M == -INFINITY) ? 0.f : M;
@@ -318,7 +322,7 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeP
     for (int j = 0; j < n; ++j) {
       const float w = fast_exp2(wts[tid * n + j] - Mu);
       wts[tid * n + j] = w;
-      L += p.ws_ml[(base + j) * 2 + 1] * w;
+      L += lsum[tid * n + j] * w;
     }
     inv_l[tid] = L > 0.f ? 1.f / L : 0.f;
     if (p.lse) p.lse[seq * p.H + h0 + tid] = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
