@@ -89,6 +89,30 @@ int tak_paged_attention_decode(const void* q, const int64_t* q_strides, const vo
                                void* workspace, size_t workspace_bytes, int split_pages, void* stream);
 
 /*
+ * Paged decode that allocates nothing.  No counterpart in the reference: it
+ * exists for callers that cannot provide the workspace above -- code where a
+ * cudaMalloc is not allowed or would stall the device, hosts whose device
+ * memory is owned by a framework allocator, bindings without a device
+ * allocator.  Same arguments and results as tak_paged_attention_decode minus
+ * the workspace: the split-KV scratch is a 32 MiB array inside the library
+ * (held by every GPU that loads the library until exit).  Sizes whose scratch
+ * would exceed 32 MiB are rejected with status 2 (a larger split_pages lowers
+ * the need).  All calls on a GPU share the array: calls that overlap on the
+ * GPU race; nothing in it needs clearing between calls.  The first call with
+ * a given GPU current looks up the array's device address; make it before any
+ * stream capture.
+ */
+int tak_paged_attention_decode_static_scratch(const void* q, const int64_t* q_strides, const void* k_cache,
+                                              const int64_t* k_strides, const void* v_cache,
+                                              const int64_t* v_strides, const int32_t* block_tables,
+                                              const int64_t* bt_strides, const int32_t* context_lens, void* out,
+                                              const int64_t* out_strides, float* lse, int64_t num_seqs,
+                                              int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                              int64_t block_size, int64_t max_blocks, int64_t num_blocks,
+                                              int64_t cache_rows, float scale, int dtype, int split_pages,
+                                              void* stream);
+
+/*
  * Top-k sparse prefill with per-head sink logits.  Replaces
  * sparse_attn_prefill(q, k, v, topk_idxs, cu_seqlens, attn_sink) of
  * attention/sparse_attn_fwd.py:263-314 (Triton launch at :298).
