@@ -114,6 +114,159 @@ __global__ void compress_kernel(const CompressArgs a) {
   for (int e = 0; e < VEC; ++e) orow[(d0 + e) * so[2]] = Elem<T>::from_f(acc[e] * inv);
 }
 
+// Streaming pooling for windows of one or two strides (the reference's CSA and
+// HCA shapes): a CTA owns a run of consecutive slots, reads every row of that
+// run exactly once (rows are summed into stride-sized blocks; a CSA slot is
+// block i + block i+1), with 8 independent 16-byte loads in flight per thread.
+// Thread j owns 8 consecutive elements of the [K | V] row.  With a gate the
+// blocks carry (max logit, sum of weights, weighted sum) and slots merge them
+// like an online softmax.
+template <typename T, int WIN_BLOCKS>
+__global__ void __launch_bounds__(128) compress_stream_kernel(const CompressArgs a, int slots_per_cta) {
+  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * slots_per_cta;
+  const int h = blockIdx.y;
+  const int nk = a.head_dim / 8, nv = a.head_dim_v / 8;
+  const int j = threadIdx.x;
+  const bool active = j < nk + nv;
+  const bool is_k = j < nk;
+  const int d0 = (is_k ? j : j - nk) * 8;
+  const T* base = reinterpret_cast<const T*>(is_k ? a.k : a.v);
+  const int64_t* st = is_k ? a.sk : a.sv;
+  T* dst = reinterpret_cast<T*>(is_k ? a.ck : a.cv);
+  const int64_t* so = is_k ? a.sck : a.scv;
+  const bool paged = a.cu_seqlens == nullptr;
+  const int m = a.stride;
+  const int64_t gend = min(g0 + slots_per_cta, a.num_compressed);
+  int64_t slot = g0;
+  int s = find_slot_seq(a.comp_offsets, a.num_seqs, slot);
+  while (slot < gend) {
+    while (s + 1 < a.num_seqs && a.comp_offsets[s + 1] <= slot) ++s;
+    const int64_t seg_end = min(gend, static_cast<int64_t>(a.comp_offsets[s + 1]));
+    const int i0 = static_cast<int>(slot - a.comp_offsets[s]);
+    const int i1 = static_cast<int>(seg_end - a.comp_offsets[s]);
+    const int L = paged ? a.context_lens[s] : (a.cu_seqlens[s + 1] - a.cu_seqlens[s]);
+    const int64_t tok0 = paged ? 0 : a.cu_seqlens[s];
+    // blocks [i0, i1 + WIN_BLOCKS - 1) cover the segment's windows
+    const int r_begin = i0 * m;
+    const int r_end = min((i1 + WIN_BLOCKS - 1) * m, L);
+    float prev[8], cur[8];
+    float pm = -INFINITY, ps = 0.f, cm = -INFINITY, cs = 0.f;  // gate block (max, sum)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) prev[e] = cur[e] = 0.f;
+    int blk = i0;  // block being accumulated
+    for (int r0 = r_begin; r0 < r_end; r0 += 8) {
+      uint4 u[8];
+      float gv[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int r = r0 + k;
+        u[k] = make_uint4(0, 0, 0, 0);
+        gv[k] = -INFINITY;
+        if (r < r_end) {
+          int64_t roff, goff;
+          if (paged) {
+            const int64_t page = a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]];
+            roff = page * st[0] + h * st[1] + (r % a.block_size) * st[2];
+            goff = page * a.sg[0] + (r % a.block_size) * a.sg[1];
+          } else {
+            roff = (tok0 + r) * st[0] + h * st[1];
+            goff = (tok0 + r) * a.sg[0];
+          }
+          if (active) u[k] = __ldg(reinterpret_cast<const uint4*>(base + roff + d0));
+          if (a.gate) gv[k] = __ldg(a.gate + goff);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int r = r0 + k;
+        if (r >= r_end) break;
+        float w = 1.f;
+        if (a.gate) {
+          if (gv[k] > cm) {  // new block max: rescale the block's running sums
+            const float f = __expf(cm - gv[k]);
+            cs *= f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) cur[e] *= f;
+            cm = gv[k];
+          }
+          w = __expf(gv[k] - cm);
+          cs += w;
+        }
+        const uint32_t* pw = reinterpret_cast<const uint32_t*>(&u[k]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f2 = Elem<T>::unpack2(pw[e]);
+          cur[2 * e] += w * f2.x;
+          cur[2 * e + 1] += w * f2.y;
+        }
+        if (r + 1 == min((blk + 1) * m, r_end)) {
+          // block `blk` is complete: emit the slot(s) it finishes
+          const int emit = WIN_BLOCKS == 1 ? blk : blk - 1;
+          if (emit >= i0 && emit < i1) {
+            float o[8];
+            if (a.gate) {
+              float M = cm, S = cs;
+              if (WIN_BLOCKS == 2) M = fmaxf(pm, cm);
+              const float fc = __expf(cm - M), fp = WIN_BLOCKS == 2 ? __expf(pm - M) : 0.f;
+              S = cs * fc + (WIN_BLOCKS == 2 ? ps * fp : 0.f);
+              const float inv = S > 0.f ? 1.f / S : 0.f;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] = (cur[e] * fc + (WIN_BLOCKS == 2 ? prev[e] * fp : 0.f)) * inv;
+            } else {
+              const int wr0 = emit * m;
+              const int cnt = min(wr0 + WIN_BLOCKS * m, L) - wr0;
+              const float inv = 1.f / static_cast<float>(cnt);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] = (cur[e] + (WIN_BLOCKS == 2 ? prev[e] : 0.f)) * inv;
+            }
+            if (active) {
+              uint4 q;
+              q.x = Elem<T>::pack2(o[0], o[1]);
+              q.y = Elem<T>::pack2(o[2], o[3]);
+              q.z = Elem<T>::pack2(o[4], o[5]);
+              q.w = Elem<T>::pack2(o[6], o[7]);
+              *reinterpret_cast<uint4*>(dst + (a.comp_offsets[s] + emit) * so[0] + h * so[1] + d0) = q;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            prev[e] = cur[e];
+            cur[e] = 0.f;
+          }
+          pm = cm;
+          ps = cs;
+          cm = -INFINITY;
+          cs = 0.f;
+          ++blk;
+        }
+      }
+    }
+    // CSA: the last slot's window ends at the sequence end (block i1 may not exist)
+    if (WIN_BLOCKS == 2 && i1 * m >= L && i1 - 1 >= i0 && i1 - 1 == blk - 1) {
+      const int emit = i1 - 1;
+      float o[8];
+      if (a.gate) {
+        const float inv = ps > 0.f ? 1.f / ps : 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = prev[e] * inv;
+      } else {
+        const float inv = 1.f / static_cast<float>(L - emit * m);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = prev[e] * inv;
+      }
+      if (active) {
+        uint4 q;
+        q.x = Elem<T>::pack2(o[0], o[1]);
+        q.y = Elem<T>::pack2(o[2], o[3]);
+        q.z = Elem<T>::pack2(o[4], o[5]);
+        q.w = Elem<T>::pack2(o[6], o[7]);
+        *reinterpret_cast<uint4*>(dst + (a.comp_offsets[s] + emit) * so[0] + h * so[1] + d0) = q;
+      }
+    }
+    slot = seg_end;
+  }
+}
+
 template <typename T>
 static int compress_typed(const CompressArgs& a, cudaStream_t st) {
   const bool paged = a.cu_seqlens == nullptr;
@@ -129,6 +282,17 @@ static int compress_typed(const CompressArgs& a, cudaStream_t st) {
         ((reinterpret_cast<uintptr_t>(a.ck) | reinterpret_cast<uintptr_t>(a.cv)) & 15) == 0;
   dim3 grid(static_cast<unsigned>(a.num_compressed), a.num_kv_heads);
   if constexpr (sizeof(T) == 2) {
+    const int threads = (a.head_dim + a.head_dim_v) / 8;
+    if (vec && threads <= 128 && (a.window == a.stride || a.window == 2 * a.stride)) {
+      // ~64 rows per CTA: enough CTAs to fill the GPU, small halo for CSA
+      const int spc = a.stride >= 64 ? 1 : 64 / a.stride;
+      const unsigned ctas = static_cast<unsigned>((a.num_compressed + spc - 1) / spc);
+      if (a.window == a.stride)
+        compress_stream_kernel<T, 1><<<dim3(ctas, a.num_kv_heads), 128, 0, st>>>(a, spc);
+      else
+        compress_stream_kernel<T, 2><<<dim3(ctas, a.num_kv_heads), 128, 0, st>>>(a, spc);
+      return 0;
+    }
     if (vec) {
       const int threads = (a.head_dim + a.head_dim_v) / 8;
       if (threads > 1024) return set_error(2, "compress: head dim too large");

@@ -12,18 +12,20 @@
 // head (MQA: all 64 heads of the token).  The 64 head rows are the MMA's
 // M = 64 dimension, so every gathered K/V row is read once for all heads.
 //
-// Warp roles (192 threads):
-//   warp 4   gather producer: Q rows once (TMA), then for each tile of 64
-//            indices lanes 0-15 issue TMA gather4 loads (4 arbitrary rows x 64
-//            columns each, 128-byte swizzle) into a 2-stage ring; masked
-//            indices use row -1, which TMA fills with zeros; a 64-bit validity
-//            mask per stage goes to shared memory.
-//   warp 5   TMEM allocator + single-thread tcgen05.mma issuer:
+// Warp roles (288 threads):
+//   warps 4-7 gather producers: Q rows once (one TMA), then for each tile of
+//            64 indices, cp.async 16-byte copies of the gathered rows (8 lanes
+//            per 128-byte line, so every warp instruction moves 4 full lines)
+//            written straight into the 128-byte-swizzled layout the MMA reads,
+//            2-stage ring; masked rows are zero-filled; the next tile's
+//            indices are loaded while the current tile is in flight.
+//   warp 8   TMEM allocator + single-thread tcgen05.mma issuer:
 //            S_j = Q K_j^T (M=64, N=64, K=16 x Dqk/16) into TMEM lanes 16-31
 //            of each quadrant (two buffers), O += P_j V_j (M=64, N<=256 per
 //            instruction, V from the same gathered rows when it is a view of
-//            K) into TMEM lanes 0-15.  QK of tile j+1 is issued before PV of
-//            tile j.
+//            K) into TMEM lanes 0-15.  Issue order is greedy: whichever of
+//            "QK of the next loaded tile" and "PV of the next softmaxed tile"
+//            is ready goes first.
 //   warps 0-3 softmax: TMEM loads of shape 16x32bx2 let all 32 threads of a
 //            warp work on its 16 head rows (two threads per row, 32 columns
 //            each); lazy rescaling of O (only when the max grows by > 2^8);
@@ -48,15 +50,6 @@ struct SparseTcParams {
   int H, Hkv, G, head_chunks;
   float scale_log2;
 };
-
-__device__ __forceinline__ void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int col, int r0, int r1,
-                                            int r2, int r3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
-      : "memory");
-}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1) {
   asm volatile(
@@ -105,14 +98,14 @@ struct SpLayout {
 };
 
 template <typename T, int DQK, int DV, bool SHARED>
-__global__ void __launch_bounds__(192, 1)
-    sparse_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, const SparseTcParams p) {
+__global__ void __launch_bounds__(288, 1)
+    sparse_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const SparseTcParams p, const void* kbase_ptr,
+                     int64_t krow_stride, const void* vbase_ptr, int64_t vrow_stride) {
   using L = SpLayout<DQK, DV, SHARED>;
   constexpr int BN = 64;
+  constexpr int NPROD = 128;  // producer threads
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* masks = reinterpret_cast<uint64_t*>(smem + L::MASKOFF);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAROFF);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;   // [2]
@@ -131,11 +124,12 @@ __global__ void __launch_bounds__(192, 1)
   const int nrows = min(64, p.G - hc * 64);
   const int n_tiles = (p.k_topk + BN - 1) / BN;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int32_t* idx_row = p.topk + static_cast<int64_t>(t) * p.stk0;
 
   if (tid == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_full[i], NPROD);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
     }
@@ -145,7 +139,7 @@ __global__ void __launch_bounds__(192, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 8) {
     tmem_alloc(tmem_holder, L::TMEM_COLS);
     tmem_relinquish();
   }
@@ -155,104 +149,113 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t taddr = *tmem_holder;
   const uint32_t sbase = smem_u32(smem);
 
-  if (warp == 4) {
-    // ---------------- gather producer ----------------
-    if (lane == 0) {
+  if (warp >= 4 && warp < 8) {
+    // ---------------- gather producers ----------------
+    const int pt = tid - 128;                 // 0..127
+    const int rsub = pt >> 3, chunk = pt & 7;  // row within a 16-row group, 16-byte chunk within a line
+    if (pt == 0) {
       tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      if (!SHARED) tma_prefetch_desc(&tmV);
       mbar_arrive_expect_tx(q_full, L::NQB * L::BLK);
 #pragma unroll 1
       for (int cb = 0; cb < L::NQB; ++cb)
         tma_load_2d(smem + L::QOFF + cb * L::BLK, &tmQ, q_full, cb * 64, t * p.H + h0);
     }
-    const int32_t* idx_row = p.topk + static_cast<int64_t>(t) * p.stk0;
+    const T* kb = reinterpret_cast<const T*>(kbase_ptr);
+    const T* vb = reinterpret_cast<const T*>(vbase_ptr);
+    auto load_rows = [&](int j, int64_t* rows) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int c = j * BN + g * 16 + rsub;
+        const int64_t r = (j < n_tiles && c < p.k_topk) ? static_cast<int64_t>(idx_row[c * p.stk1]) : -1;
+        rows[g] = (r >= 0 && r < p.kv_rows) ? r * p.Hkv + kvh : -1;
+      }
+    };
+    int64_t cur[4], nxt[4];
+    load_rows(0, cur);
     for (int j = 0; j < n_tiles; ++j) {
       const int st = j & 1;
-      // warp-uniform: lane 0 waits for the stage, every lane follows its verdict
-      int go = 1;
-      if (lane == 0) {
-        go = (j < 2 || mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1)) && !*abort_flag;
-        if (!go) *abort_flag = 1;
+      load_rows(j + 1, nxt);  // in flight while this tile's stage frees up
+      if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1)) {
+        *abort_flag = 1;
+        break;
       }
-      if (!__shfl_sync(0xffffffffu, go, 0)) break;
-      int coord[4];
-      uint32_t vb = 0;
+      uint8_t* kst = smem + L::KVOFF + st * L::STAGE;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int c = j * BN + 4 * (lane & 15) + i;
-        int64_t r = c < p.k_topk ? idx_row[c * p.stk1] : -1;
-        const bool ok = r >= 0 && r < p.kv_rows;
-        coord[i] = ok ? static_cast<int>(r * p.Hkv + kvh) : -1;
-        vb |= (ok && lane < 16) ? (1u << i) : 0u;
-      }
-      // validity of the tile's 64 rows: row 4l+i <- bit i of lane l
-      uint64_t mask = 0;
+      for (int g = 0; g < 4; ++g) {
+        const int row = g * 16 + rsub;
+        const bool ok = cur[g] >= 0;
+        const T* src = kb + (ok ? cur[g] : 0) * krow_stride + chunk * 8;
+        const uint32_t dst_off = row * 128 + ((chunk ^ (row & 7)) << 4);
 #pragma unroll
-      for (int l = 0; l < 16; ++l) mask |= static_cast<uint64_t>(__shfl_sync(0xffffffffu, vb, l)) << (4 * l);
-      if (lane == 0) {
-        masks[st] = mask;
-        mbar_arrive_expect_tx(&kv_full[st], L::STAGE);
-      }
-      __syncwarp();
-      if (lane < 16) {
-        uint8_t* kst = smem + L::KVOFF + st * L::STAGE;
-#pragma unroll 1
-        for (int cb = 0; cb < L::NQB; ++cb)
-          tma_gather4(kst + cb * L::BLK + lane * 512, &tmK, &kv_full[st], cb * 64, coord[0], coord[1], coord[2],
-                      coord[3]);
+        for (int cb = 0; cb < L::NQB; ++cb) cp_async_16(kst + cb * L::BLK + dst_off, src + cb * 64, ok);
         if (!SHARED) {
-#pragma unroll 1
+          const T* vsrc = vb + (ok ? cur[g] : 0) * vrow_stride + chunk * 8;
+#pragma unroll
           for (int cb = 0; cb < L::NVB; ++cb)
-            tma_gather4(kst + (L::NQB + cb) * L::BLK + lane * 512, &tmV, &kv_full[st], cb * 64, coord[0], coord[1],
-                        coord[2], coord[3]);
+            cp_async_16(kst + (L::NQB + cb) * L::BLK + dst_off, vsrc + cb * 64, ok);
         }
       }
-      __syncwarp();
+      cp_async_mbar_arrive(&kv_full[st]);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) cur[g] = nxt[g];
     }
-  } else if (warp == 5) {
-    // ---------------- MMA issuer ----------------
+    cp_async_wait_all();
+  } else if (warp == 8) {
+    // ---------------- MMA issuer (greedy order) ----------------
     if (lane == 0 && n_tiles > 0) {
       constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       constexpr int NPV = DV < 256 ? DV : 256;
       const uint32_t idesc_qk = tc_idesc_f16(AB, 64, BN, 0);
       const uint32_t idesc_pv = tc_idesc_f16(AB, 64, NPV, 1);
       bool ok = mbar_wait(q_full, 0);
-      auto issue_qk = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) return false;
-        tc_fence_after();
-        const uint32_t d_tmem = taddr + (16u << 16) + st * 64;
-        const uint32_t kbase = sbase + L::KVOFF + st * L::STAGE;
+      int nq = 0, np = 0;  // next QK / PV to issue
+      const uint64_t t0 = globaltimer();
+      uint32_t spins = 0;
+      while (ok && np < n_tiles) {
+        bool did = false;
+        // QK of tile nq: its stage must be loaded and its S buffer consumed (nq <= np + 1)
+        if (nq < n_tiles && nq <= np + 1 && mbar_try_wait(smem_u32(&kv_full[nq & 1]), (nq >> 1) & 1)) {
+          fence_proxy_async_smem();
+          tc_fence_after();
+          const int st = nq & 1;
+          const uint32_t d_tmem = taddr + (16u << 16) + st * 64;
+          const uint32_t kbase = sbase + L::KVOFF + st * L::STAGE;
 #pragma unroll 1
-        for (int kk = 0; kk < DQK / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * L::BLK + (kk & 3) * 32;
-          tc_mma_ss(d_tmem, tc_sdesc_sw128(sbase + L::QOFF + koff, 16, 1024), tc_sdesc_sw128(kbase + koff, 16, 1024),
-                    idesc_qk, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < DQK / 16; ++kk) {
+            const uint32_t koff = (kk >> 2) * L::BLK + (kk & 3) * 32;
+            tc_mma_ss(d_tmem, tc_sdesc_sw128(sbase + L::QOFF + koff, 16, 1024),
+                      tc_sdesc_sw128(kbase + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&s_full[st]);
+          ++nq;
+          did = true;
         }
-        tc_commit(&s_full[st]);
-        return true;
-      };
-      if (ok) ok = issue_qk(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (*abort_flag) break;
-        if (j + 1 < n_tiles && !(ok = issue_qk(j + 1))) break;
-        const int st = j & 1;
-        if (!(ok = mbar_wait(p_full, j & 1))) break;
-        tc_fence_after();
-        const uint32_t vbase = sbase + L::KVOFF + st * L::STAGE + (SHARED ? 0 : L::NQB * L::BLK);
+        // PV of tile np once its P is in shared memory
+        if (np < nq && mbar_try_wait(smem_u32(p_full), np & 1)) {
+          tc_fence_after();
+          const int st = np & 1;
+          const uint32_t vbase = sbase + L::KVOFF + st * L::STAGE + (SHARED ? 0 : L::NQB * L::BLK);
 #pragma unroll
-        for (int half = 0; half < (DV + 255) / 256; ++half) {
+          for (int half = 0; half < (DV + 255) / 256; ++half) {
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint64_t a = tc_sdesc_sw128(sbase + L::POFF + kk * 32, 16, 1024);
-            const uint64_t b = tc_sdesc_sw128(vbase + half * 4 * L::BLK + kk * 2048, L::BLK, 1024);
-            tc_mma_ss(taddr + half * 256, a, b, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              const uint64_t a = tc_sdesc_sw128(sbase + L::POFF + kk * 32, 16, 1024);
+              const uint64_t b = tc_sdesc_sw128(vbase + half * 4 * L::BLK + kk * 2048, L::BLK, 1024);
+              tc_mma_ss(taddr + half * 256, a, b, idesc_pv, (np > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          tc_commit(o_done);
+          tc_commit(&kv_empty[st]);
+          tc_commit(p_free);
+          ++np;
+          did = true;
+        }
+        if (!did && (++spins & 255u) == 0u) {
+          if (globaltimer() - t0 > TAK_WAIT_LIMIT_NS * 4 || *abort_flag) {
+            record_error(1);
+            ok = false;
           }
         }
-        tc_commit(o_done);
-        tc_commit(&kv_empty[st]);
-        tc_commit(p_free);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -268,15 +271,25 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t o_lane = static_cast<uint32_t>(32 * warp) << 16;
     float m_run = -INFINITY, m_used = -INFINITY, l = 0.f;
     bool ok = true;
+    auto tile_mask = [&](int j) -> uint32_t {
+      // validity of this thread's 32 columns of tile j (lane l: columns l and l+32)
+      const int c0 = j * BN + lane, c1 = c0 + 32;
+      const int64_t r0 = c0 < p.k_topk ? static_cast<int64_t>(idx_row[c0 * p.stk1]) : -1;
+      const int64_t r1 = c1 < p.k_topk ? static_cast<int64_t>(idx_row[c1 * p.stk1]) : -1;
+      const uint32_t lo = __ballot_sync(0xffffffffu, r0 >= 0 && r0 < p.kv_rows);
+      const uint32_t hi_m = __ballot_sync(0xffffffffu, r1 >= 0 && r1 < p.kv_rows);
+      return hi ? hi_m : lo;
+    };
+    uint32_t vnext = n_tiles > 0 ? tile_mask(0) : 0u;
     for (int j = 0; j < n_tiles; ++j) {
       const int b = j & 1;
+      const uint32_t vbits = vnext;
+      if (j + 1 < n_tiles) vnext = tile_mask(j + 1);
       if (!(ok = mbar_wait(&s_full[b], (j >> 1) & 1))) break;
-      if (!(ok = mbar_wait(&kv_full[b], (j >> 1) & 1))) break;  // orders the producer's mask write
       tc_fence_after();
       uint32_t sr[32];
       tmem_ld16x2(taddr + s_lane + b * 64, sr);
       tmem_ld_wait();
-      const uint32_t vbits = static_cast<uint32_t>(masks[b] >> (32 * hi));
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 32; ++c)
@@ -362,7 +375,7 @@ __global__ void __launch_bounds__(192, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(taddr, L::TMEM_COLS);
   }
@@ -382,17 +395,11 @@ template <typename T, int DQK, int DV, bool SHARED>
 static int launch_sparse_tc(const SparseArgs& a, cudaStream_t st) {
   using L = SpLayout<DQK, DV, SHARED>;
   const int G = a.num_q_heads / a.num_kv_heads;
-  CUtensorMap mq, mk, mv;
-  // q as [T * H, Dqk] rows, k (and v) as [rows * H_kv, D] rows
+  CUtensorMap mq;
+  // q as [T * H, Dqk] rows (TMA); gathered K/V rows by cp.async from row bases
   if (int r = encode_rows_map(&mq, a.q, static_cast<int64_t>(a.num_tokens) * a.num_q_heads, DQK, a.sq[1], 64)) return r;
   const int64_t krow = a.num_kv_heads == 1 ? a.sk[0] : a.sk[1];
-  if (int r = encode_rows_map(&mk, a.k, a.kv_rows * a.num_kv_heads, DQK, krow, 1)) return r;
-  if (SHARED) {
-    mv = mk;
-  } else {
-    const int64_t vrow = a.num_kv_heads == 1 ? a.sv[0] : a.sv[1];
-    if (int r = encode_rows_map(&mv, a.v, a.kv_rows * a.num_kv_heads, DV, vrow, 1)) return r;
-  }
+  const int64_t vrow = a.num_kv_heads == 1 ? a.sv[0] : a.sv[1];
   SparseTcParams p{};
   p.topk = a.topk;
   p.stk0 = a.stk[0];
@@ -412,7 +419,7 @@ static int launch_sparse_tc(const SparseArgs& a, cudaStream_t st) {
   auto kern = sparse_tc_kernel<T, DQK, DV, SHARED>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
   dim3 grid(a.num_tokens, a.num_kv_heads * p.head_chunks);
-  kern<<<grid, 192, L::SMEM, st>>>(mq, mk, mv, p);
+  kern<<<grid, 288, L::SMEM, st>>>(mq, p, a.k, krow, a.v, vrow);
   return 0;
 }
 
