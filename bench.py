@@ -384,16 +384,290 @@ def run_decode_reference(args):
     }
 
 
+# ---------------------------------------------------------------------------
+# other workloads of the metric (prefill / sparse TFLOP/s, compression GB/s)
+# ---------------------------------------------------------------------------
+
+class Workload:
+    """One hot-path workload: device-resident step, end-to-end step through the
+    public API with host buffers, algorithmic work per step, CPU baseline."""
+    name = unit = bound = peak_key = kernel = desc = ""
+
+    def timed(self, fn, steps, warmup, device):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        st = torch.cuda.current_stream(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / steps
+
+
+def _loguniform_lengths(n, lo, hi, g):
+    u = torch.rand(n, generator=g, dtype=torch.float64)
+    return [int(round(math.exp(math.log(lo) + float(x) * (math.log(hi) - math.log(lo))))) for x in u]
+
+
+class PrefillWL(Workload):
+    name, unit, bound, peak_key, kernel = "prefill", "TFLOP/s", "tensor", "bf16_tflops", "prefill_tc_kernel"
+    desc = ("varlen causal prefill: 32 sequences (one GPU's share of 256), lengths log-uniform in [512, 32768], "
+            "64 q heads / 8 KV heads, head_dim 128, bf16")
+
+    def setup(self, rank, device):
+        import flash_attention_prefill as FP
+        self.FP = FP
+        g = torch.Generator().manual_seed(4321 + rank)
+        self.lens = _loguniform_lengths(4 if SMALL else 32, 512, 32768, g)
+        T = sum(self.lens)
+        cu = [0]
+        for L in self.lens:
+            cu.append(cu[-1] + L)
+        self.cu_h = torch.tensor(cu, dtype=torch.int32)
+        gd = torch.Generator(device=device).manual_seed(99 + rank)
+        self.q = torch.empty(T, 64, 128, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.k = torch.empty(T, 8, 128, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.v = torch.empty(T, 8, 128, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.cu = self.cu_h.to(device)
+        self.work = 4.0 * 128 * 64 * sum(L * (L + 1) / 2 for L in self.lens)
+        self.launches = 1
+        self.config = {"sequences": len(self.lens), "total_tokens": T, "max_len": max(self.lens),
+                       "l2_policy": f"inputs larger than L2 ({(T * 80 * 128 * 2) / 1e9:.2f} GB of q/k/v)"}
+
+    def step(self):
+        return self.FP.flash_attention_prefill(self.q, self.k, self.v, self.cu, True)
+
+    def e2e_setup(self):
+        self.hq, self.hk, self.hv = (t.cpu().pin_memory() for t in (self.q, self.k, self.v))
+        self.hcu = self.cu_h.pin_memory()
+        self.hout = torch.empty(self.q.shape, dtype=self.q.dtype).pin_memory()
+        self.dq, self.dk, self.dv = (torch.empty_like(t) for t in (self.q, self.k, self.v))
+        self.dcu = torch.empty_like(self.cu)
+        return (sum(t.numel() * t.element_size() for t in (self.hq, self.hk, self.hv, self.hcu)),
+                self.hout.numel() * self.hout.element_size())
+
+    def e2e_step(self):
+        for d, h in ((self.dq, self.hq), (self.dk, self.hk), (self.dv, self.hv), (self.dcu, self.hcu)):
+            d.copy_(h, non_blocking=True)
+        o = self.FP.flash_attention_prefill(self.dq, self.dk, self.dv, self.dcu, True)
+        self.hout.copy_(o, non_blocking=True)
+
+    def cpu_baseline(self, seconds, threads):
+        from oracle import attention_oracle as O
+        L = 1024
+        g = np.random.default_rng(1)
+        q = g.standard_normal((L, 64, 128), dtype=np.float32)
+        k = g.standard_normal((L, 8, 128), dtype=np.float32)
+        v = g.standard_normal((L, 8, 128), dtype=np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds or n == 0:
+            O.prefill(q, k, v, [0, L], True, acc=np.float32)
+            n += 1
+        dt = time.perf_counter() - t0
+        flop = n * 4.0 * 128 * 64 * L * (L + 1) / 2
+        return flop / dt / 1e12, f"{n} causal 1024-token sequences (64/8 heads, d 128) through the numpy oracle, " \
+                                 f"fp32, {dt:.1f} s, BLAS threads {threads}"
+
+
+class SparseWL(Workload):
+    name, unit, bound, peak_key, kernel = "sparse", "TFLOP/s", "tensor", "bf16_tflops", "sparse_tc_kernel"
+    desc = ("top-k sparse attention with sinks: 16 sequences x 4096 query tokens over a 32768-token latent KV, "
+            "MQA 64 heads, QK dim 576 (512 + 64 rope), V dim 512 (view of the latent), bf16, 2048 sorted unique "
+            "causal indices per query, per-head sink logits")
+
+    def setup(self, rank, device):
+        import sparse_attn_fwd as SA
+        self.SA = SA
+        S, QT, KVL, K = (1 if SMALL else 16), 4096, 32768, 2048
+        gd = torch.Generator(device=device).manual_seed(77 + rank)
+        T = S * QT
+        self.q = torch.empty(T, 64, 576, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.kv = torch.empty(S * KVL, 1, 576, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.sink = torch.empty(64, device=device).normal_(generator=gd)
+        idx = torch.empty(T, K, dtype=torch.int32, device=device)
+        pos_all = torch.arange(KVL - QT, KVL, device=device)
+        ar = torch.arange(KVL, device=device)
+        for s in range(S):
+            for c0 in range(0, QT, 512):
+                pos = pos_all[c0:c0 + 512]
+                r = torch.rand(pos.numel(), KVL, device=device, generator=gd)
+                r = torch.where(ar[None, :] <= pos[:, None], r, torch.full_like(r, 2.0))
+                sel = torch.topk(r, K, dim=1, largest=False).indices.sort(dim=1).values
+                idx[s * QT + c0:s * QT + c0 + pos.numel()] = (sel + s * KVL).to(torch.int32)
+        self.idx = idx
+        self.cu = torch.arange(0, T + 1, QT, dtype=torch.int32, device=device)
+        self.work = 2.0 * 64 * (576 + 512) * T * K
+        self.launches = 1
+        self.config = {"tokens": T, "kv_rows": S * KVL, "top_k": K,
+                       "l2_policy": "per-sequence latent KV (37.7 MB) fits L2 by design; q/out 9 GB stream"}
+
+    def step(self):
+        return self.SA.sparse_attn_prefill(self.q, self.kv, self.kv[..., :512], self.idx, self.cu, self.sink)
+
+    def e2e_setup(self):
+        self.hq, self.hkv, self.hidx = (t.cpu().pin_memory() for t in (self.q, self.kv, self.idx))
+        self.hout = torch.empty(self.q.shape[0], 64, 512, dtype=self.q.dtype).pin_memory()
+        self.dq, self.dkv, self.didx = (torch.empty_like(t) for t in (self.q, self.kv, self.idx))
+        return (sum(t.numel() * t.element_size() for t in (self.hq, self.hkv, self.hidx)),
+                self.hout.numel() * self.hout.element_size())
+
+    def e2e_step(self):
+        for d, h in ((self.dq, self.hq), (self.dkv, self.hkv), (self.didx, self.hidx)):
+            d.copy_(h, non_blocking=True)
+        o = self.SA.sparse_attn_prefill(self.dq, self.dkv, self.dkv[..., :512], self.didx, self.cu, self.sink)
+        self.hout.copy_(o, non_blocking=True)
+
+    def cpu_baseline(self, seconds, threads):
+        from oracle import attention_oracle as O
+        n_tok = 4
+        q = self.q[:n_tok].float().cpu().numpy()
+        kv = self.kv[:32768].float().cpu().numpy()
+        idx = self.idx[:n_tok].cpu().numpy()
+        sink = self.sink.cpu().numpy()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds or n == 0:
+            O.sparse_prefill(q, kv, kv[..., :512], idx, None, sink, acc=np.float32)
+            n += 1
+        dt = time.perf_counter() - t0
+        return n * n_tok * 2.0 * 64 * 1088 * 2048 / dt / 1e12, \
+            f"{n}x{n_tok} query tokens (64 heads, 2048 indices, 576/512) through the numpy oracle, fp32, {dt:.1f} s"
+
+
+class CompressWL(Workload):
+    name, unit, bound, peak_key, kernel = "compress", "GB/s", "hbm", "hbm_gbs", "compress_stream_kernel"
+    desc = ("CSA + HCA KV compression: 65536 tokens (16 sequences x 4096) x 512 dims bf16 K and V plus per-token "
+            "fp32 gate logits; CSA stride 4 (8-token windows, as the reference's csa.py) and HCA 128-token "
+            "windows, gate-softmax-weighted sums")
+
+    def setup(self, rank, device):
+        import csa as CSA
+        import hca as HCA
+        self.CSA, self.HCA = CSA, HCA
+        gd = torch.Generator(device=device).manual_seed(55 + rank)
+        T = 65536
+        self.k = torch.empty(T, 1, 512, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.v = torch.empty(T, 1, 512, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.gate = torch.empty(T, device=device).normal_(generator=gd)
+        self.cu_h = torch.arange(0, T + 1, 4096, dtype=torch.int32)
+        # algorithmic bytes: read K, V and the gates once, write both compressed outputs
+        self.work = 2 * T * 512 * 2 + T * 4 + 2 * (T // 4) * 512 * 2 + 2 * (T // 128) * 512 * 2
+        self.launches = 2
+        self.config = {"tokens": T, "csa_slots": T // 4, "hca_slots": T // 128,
+                       "l2_policy": "inputs (268 MB of K/V) larger than L2"}
+
+    def step(self):
+        a = self.CSA.compress_kv_overlap(self.k, self.v, self.cu_h, 4, gate=self.gate)
+        b = self.HCA.compress_kv_simple(self.k, self.v, self.cu_h, 128, gate=self.gate)
+        return a[0]
+
+    def e2e_setup(self):
+        self.hk, self.hv, self.hg = (t.cpu().pin_memory() for t in (self.k, self.v, self.gate))
+        self.hck = torch.empty(65536 // 4, 1, 512, dtype=torch.bfloat16).pin_memory()
+        self.hhk = torch.empty(65536 // 128, 1, 512, dtype=torch.bfloat16).pin_memory()
+        self.dk, self.dv, self.dg = (torch.empty_like(t) for t in (self.k, self.v, self.gate))
+        return (sum(t.numel() * t.element_size() for t in (self.hk, self.hv, self.hg)),
+                2 * (self.hck.numel() + self.hhk.numel()) * 2)
+
+    def e2e_step(self):
+        for d, h in ((self.dk, self.hk), (self.dv, self.hv), (self.dg, self.hg)):
+            d.copy_(h, non_blocking=True)
+        ck, cv, _ = self.CSA.compress_kv_overlap(self.dk, self.dv, self.cu_h, 4, gate=self.dg)
+        hk, hv, _ = self.HCA.compress_kv_simple(self.dk, self.dv, self.cu_h, 128, gate=self.dg)
+        self.hck.copy_(ck, non_blocking=True)
+        self.hhk.copy_(hk, non_blocking=True)
+
+    def cpu_baseline(self, seconds, threads):
+        from oracle import attention_oracle as O
+        T = 4096
+        k = self.k[:T].float().cpu().numpy()
+        v = self.v[:T].float().cpu().numpy()
+        g = self.gate[:T].cpu().numpy()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds or n == 0:
+            O.compress_kv(k, v, [0, T], 4, 8, g, acc=np.float32)
+            O.compress_kv(k, v, [0, T], 128, 128, g, acc=np.float32)
+            n += 1
+        dt = time.perf_counter() - t0
+        b = n * (2 * T * 512 * 2 + T * 4 + 2 * (T // 4) * 512 * 2 + 2 * (T // 128) * 512 * 2)
+        return b / dt / 1e9, f"{n} x one 4096-token sequence, CSA + HCA gated, numpy oracle, fp32, {dt:.1f} s"
+
+
+WORKLOADS = {"prefill": PrefillWL, "sparse": SparseWL, "compress": CompressWL}
+SMALL = False  # --small: a reduced instance of the workload (for ncu captures)
+
+
+def run_workload_ours(args, rank, world, device, W):
+    pk, pk_kind = peaks()
+    w = W()
+    w.setup(rank, device)
+    if world > 1:
+        torch.distributed.barrier()
+    with Clocks(device.index) as clk:
+        ms = w.timed(w.step, args.steps, args.warmup, device)
+    if args.no_e2e:
+        h2d = d2h = 0
+        e2e_ms = float("nan")
+    else:
+        h2d, d2h = w.e2e_setup()
+        if world > 1:
+            torch.distributed.barrier()
+        e2e_ms = w.timed(w.e2e_step, max(2, args.steps // 4), 1, device)
+    work_all = float(w.work)
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, float(w.work)], dtype=torch.float64, device=device)
+        mx, tot = t.clone(), t.clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(tot, op=torch.distributed.ReduceOp.SUM)
+        ms, e2e_ms, work_all = float(mx[0]), float(mx[1]), float(tot[2])
+    if rank != 0:
+        return None
+    scale = 1e12 if w.unit == "TFLOP/s" else 1e9
+    val = work_all / (ms * 1e-3) / scale
+    per_gpu = float(w.work) / (ms * 1e-3) / scale
+    peak = pk[w.peak_key]
+    res = {
+        "metric": METRIC, "workload": w.name, "value": round(val, 1), "unit": w.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": dict({"workload": w.desc, "parallelism": f"sequence sharding x{world} (weak scaling)"}, **w.config),
+        "roofline": {"bound": w.bound, "achieved": round(per_gpu, 1), "peak": peak, "unit": w.unit,
+                     "frac": round(per_gpu / peak, 4), "traffic": profile_traffic(f"{w.kernel}.md"),
+                     "peak_source": f"{pk_kind} {w.peak_key}", "algorithmic_work_per_step": w.work,
+                     "timed": f"{w.kernel} per step (public API, device-resident inputs), CUDA events"},
+        "e2e": {"value": round(work_all / (e2e_ms * 1e-3) / scale, 1), "unit": w.unit, "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps * w.launches,
+        "clocks": clk.summary(),
+    }
+    if args.no_e2e:
+        res["e2e"] = None
+    if not args.no_cpu_baseline:
+        from threadpoolctl import threadpool_limits
+        threads = os.cpu_count() or 1
+        with threadpool_limits(limits=threads):
+            v, sample = w.cpu_baseline(args.cpu_seconds, threads)
+        res["cpu_baseline"] = {"value": round(v, 4), "unit": w.unit, "cores": threads, "kind": "port",
+                               "sample": sample}
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode"], default="decode")
+    ap.add_argument("--workload", choices=["decode"] + sorted(WORKLOADS), default="decode")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling)")
+    ap.add_argument("--small", action="store_true", help="reduced workload instance (profiling captures)")
     args = ap.parse_args()
+    global SMALL
+    SMALL = args.small
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -402,7 +676,12 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_decode_reference(args)), flush=True)
+            if args.workload == "decode":
+                print(json.dumps(run_decode_reference(args)), flush=True)
+            else:
+                print(json.dumps({"impl": "reference", "workload": args.workload,
+                                  "unavailable": "reference arm implemented for the headline decode workload; "
+                                                 "this workload reports its CPU oracle as cpu_baseline"}), flush=True)
         return
 
     device = torch.device("cuda", local)
@@ -412,7 +691,10 @@ def main():
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
-    res = run_decode_ours(args, rank, world, device)
+    if args.workload == "decode":
+        res = run_decode_ours(args, rank, world, device)
+    else:
+        res = run_workload_ours(args, rank, world, device, WORKLOADS[args.workload])
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

@@ -156,8 +156,12 @@ def compress_tnd(k, v, cu_seqlens, stride, window, gate=None):
     """
     require_cuda(k, v)
     dev = k.device
-    cu = as_i32(cu_seqlens, dev)
-    cu_h = cu.cpu().tolist()
+    if isinstance(cu_seqlens, torch.Tensor) and cu_seqlens.is_cuda:
+        cu = as_i32(cu_seqlens, dev)
+        cu_h = cu.cpu().tolist()          # device -> host copy (sizes the outputs)
+    else:                                 # lengths already on the host: no device sync
+        cu_h = [int(x) for x in (cu_seqlens.tolist() if isinstance(cu_seqlens, torch.Tensor) else cu_seqlens)]
+        cu = torch.tensor(cu_h, dtype=torch.int32).to(dev, non_blocking=True)
     offs = comp_offsets_host([cu_h[i + 1] - cu_h[i] for i in range(len(cu_h) - 1)], stride)
     nc = offs[-1]
     hkv = k.shape[1]
