@@ -267,6 +267,126 @@ __global__ void __launch_bounds__(128) compress_stream_kernel(const CompressArgs
   }
 }
 
+// Non-overlapping windows of many rows (HCA, m' >= 64): one CTA per (slot,
+// KV head), 4 row groups of 128 threads each streaming a quarter of the window
+// with 8 independent 16-byte loads in flight per thread, merged through shared
+// memory (with a gate: per-group max / weight-sum / weighted sum, merged like an
+// online softmax).
+template <typename T>
+__global__ void __launch_bounds__(512) compress_split_kernel(const CompressArgs a) {
+  constexpr int RG = 4;
+  __shared__ float part[RG][128][8];
+  __shared__ float gpart[RG][2];
+  const int64_t slot = blockIdx.x;
+  const int h = blockIdx.y;
+  const int s = find_slot_seq(a.comp_offsets, a.num_seqs, slot);
+  const int i = static_cast<int>(slot - a.comp_offsets[s]);
+  const bool paged = a.cu_seqlens == nullptr;
+  const int L = paged ? a.context_lens[s] : (a.cu_seqlens[s + 1] - a.cu_seqlens[s]);
+  const int64_t tok0 = paged ? 0 : a.cu_seqlens[s];
+  const int r0 = i * a.stride, r1 = min(r0 + a.window, L);
+  const int grp = threadIdx.x >> 7, j = threadIdx.x & 127;
+  const int nk = a.head_dim / 8, nv = a.head_dim_v / 8;
+  const bool active = j < nk + nv;
+  const bool is_k = j < nk;
+  const int d0 = (is_k ? j : j - nk) * 8;
+  const T* base = reinterpret_cast<const T*>(is_k ? a.k : a.v);
+  const int64_t* st = is_k ? a.sk : a.sv;
+  const int rows = r1 - r0;
+  const int per = (rows + RG - 1) / RG;
+  const int ga = r0 + grp * per, gb = min(ga + per, r1);
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  float gm = -INFINITY, gs = 0.f;
+  for (int rr = ga; rr < gb; rr += 8) {
+    uint4 u[8];
+    float gv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = rr + k;
+      u[k] = make_uint4(0, 0, 0, 0);
+      gv[k] = -INFINITY;
+      if (r < gb) {
+        int64_t roff, goff;
+        if (paged) {
+          const int64_t page = a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]];
+          roff = page * st[0] + h * st[1] + (r % a.block_size) * st[2];
+          goff = page * a.sg[0] + (r % a.block_size) * a.sg[1];
+        } else {
+          roff = (tok0 + r) * st[0] + h * st[1];
+          goff = (tok0 + r) * a.sg[0];
+        }
+        if (active) u[k] = __ldg(reinterpret_cast<const uint4*>(base + roff + d0));
+        if (a.gate) gv[k] = __ldg(a.gate + goff);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (rr + k >= gb) break;
+      float w = 1.f;
+      if (a.gate) {
+        if (gv[k] > gm) {
+          const float f = __expf(gm - gv[k]);
+          gs *= f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] *= f;
+          gm = gv[k];
+        }
+        w = __expf(gv[k] - gm);
+        gs += w;
+      }
+      const uint32_t* pw = reinterpret_cast<const uint32_t*>(&u[k]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f2 = Elem<T>::unpack2(pw[e]);
+        acc[2 * e] += w * f2.x;
+        acc[2 * e + 1] += w * f2.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) part[grp][j][e] = acc[e];
+  if (j == 0) {
+    gpart[grp][0] = gm;
+    gpart[grp][1] = gs;
+  }
+  __syncthreads();
+  if (grp != 0 || !active) return;
+  float o[8];
+  if (a.gate) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < RG; ++g) M = fmaxf(M, gpart[g][0]);
+    float S = 0.f, f[RG];
+#pragma unroll
+    for (int g = 0; g < RG; ++g) {
+      f[g] = gpart[g][0] == -INFINITY ? 0.f : __expf(gpart[g][0] - M);
+      S += gpart[g][1] * f[g];
+    }
+    const float inv = S > 0.f ? 1.f / S : 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float v = 0.f;
+#pragma unroll
+      for (int g = 0; g < RG; ++g) v += part[g][j][e] * f[g];
+      o[e] = v * inv;
+    }
+  } else {
+    const float inv = rows > 0 ? 1.f / static_cast<float>(rows) : 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = (part[0][j][e] + part[1][j][e] + part[2][j][e] + part[3][j][e]) * inv;
+  }
+  T* dst = reinterpret_cast<T*>(is_k ? a.ck : a.cv);
+  const int64_t* so = is_k ? a.sck : a.scv;
+  uint4 q;
+  q.x = Elem<T>::pack2(o[0], o[1]);
+  q.y = Elem<T>::pack2(o[2], o[3]);
+  q.z = Elem<T>::pack2(o[4], o[5]);
+  q.w = Elem<T>::pack2(o[6], o[7]);
+  *reinterpret_cast<uint4*>(dst + slot * so[0] + h * so[1] + d0) = q;
+}
+
 template <typename T>
 static int compress_typed(const CompressArgs& a, cudaStream_t st) {
   const bool paged = a.cu_seqlens == nullptr;
@@ -283,9 +403,13 @@ static int compress_typed(const CompressArgs& a, cudaStream_t st) {
   dim3 grid(static_cast<unsigned>(a.num_compressed), a.num_kv_heads);
   if constexpr (sizeof(T) == 2) {
     const int threads = (a.head_dim + a.head_dim_v) / 8;
+    if (vec && threads <= 128 && a.window == a.stride && a.stride >= 64) {
+      compress_split_kernel<T><<<grid, 512, 0, st>>>(a);
+      return 0;
+    }
     if (vec && threads <= 128 && (a.window == a.stride || a.window == 2 * a.stride)) {
-      // ~64 rows per CTA: enough CTAs to fill the GPU, small halo for CSA
-      const int spc = a.stride >= 64 ? 1 : 64 / a.stride;
+      // ~32 rows per CTA: enough CTAs to fill the GPU, small halo for CSA
+      const int spc = a.stride >= 32 ? 1 : 32 / a.stride;
       const unsigned ctas = static_cast<unsigned>((a.num_compressed + spc - 1) / spc);
       if (a.window == a.stride)
         compress_stream_kernel<T, 1><<<dim3(ctas, a.num_kv_heads), 128, 0, st>>>(a, spc);

@@ -5,28 +5,33 @@
 // Q K^T [+ causal mask]) V with KV head h / (H / H_kv), output acc / (l + 1e-6)
 // (FP:97), plus the natural-log LSE.
 //
-// One CTA = one tile of up to 128 query rows of one sequence x one query head.
-// Tiles are 128-row blocks aligned to global token positions (clipped to the
-// sequence that owns the block's first row) plus one "head piece" per sequence
-// for its rows before the first aligned boundary, so the schedule needs no
-// host-side table (the reference builds one with a host loop, FP:144-153).
-// Causal tiles stop at the diagonal block (the reference sweeps every block,
-// FP:60).  Aligned tiles are issued last-block-first (longest work first).
+// One CTA = up to 256 query rows of one sequence x one query head, as two
+// 128-row tiles A and B that share every K/V block.  Row blocks are 256-row
+// blocks aligned to global token positions (clipped to the sequence owning the
+// block's first row) plus one "head piece" per sequence for its rows before
+// the first aligned boundary, so the schedule needs no host-side table (the
+// reference builds one with a host loop, FP:144-153).  Causal tiles stop at
+// their diagonal block (the reference sweeps every block, FP:60).  Aligned
+// blocks are issued last-first (longest work first).
 //
-// Warp roles (192 threads):
-//   warp 4      TMA producer: Q tile once, then K and V blocks of 128 rows into
-//               2-stage rings (128-byte swizzle, one 64-column box per half).
-//   warp 5      TMEM allocator + single-thread tcgen05.mma issuer:
-//               S_j = Q K_j^T (SS, M=N=128, K=16 x 8) into one of 3 TMEM
-//               buffers, then O += P_j V_j (TS: P read from TMEM, V from smem,
-//               MN-major) -- QK of block j+1 is issued before PV of block j so
-//               the tensor core works while the softmax warps run.
-//   warps 0-3   softmax: thread i owns row i (TMEM lane i): loads S_j, masks,
-//               online max with lazy rescaling (O and l are rescaled only when
-//               the max grows by more than 2^8), P = exp2(s - m) packed to 16
-//               bits back into the S buffer's first 64 columns; epilogue reads
-//               O, normalises, stores the row and its LSE.
-// TMEM: O in columns [0,128), S/P buffers in [128,512).
+// Warp roles (320 threads):
+//   warp 8      TMA producer: both Q tiles once, then K and V blocks of 128
+//               rows into 2-stage rings (128-byte swizzle, 64-column boxes).
+//   warp 9      TMEM allocator + single-thread tcgen05.mma issuer.  Per K/V
+//               block j: PV_A(j), PV_B(j) (TS-MMA: P read from TMEM, V from
+//               smem, MN-major), then S_A(j+1) = Q_A K^T, S_B(j+1) = Q_B K^T
+//               (SS-MMA, M=N=128).  Each tile's S is rewritten only after
+//               that tile's PV of the previous block has completed.
+//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B (thread = row =
+//               TMEM lane): load S, mask only on boundary blocks, online max
+//               with lazy rescaling (O and l rescaled only when the max grows
+//               by more than 2^8), P = 2^(s - m) -- half of the exponentials on
+//               the MUFU unit, half by a cubic polynomial on the FMA pipe --
+//               packed to 16 bits back into the tile's S columns; epilogue
+//               reads O, normalises, stores the row and its LSE.  While one
+//               warpgroup runs its softmax the tensor core works on the other
+//               tile.
+// TMEM: O_A [0,128), O_B [128,256), S/P_A [256,384), S/P_B [384,512).
 #include <type_traits>
 
 #include "common.cuh"
@@ -44,11 +49,11 @@ struct PrefillTcParams {
 };
 
 namespace pf {
-constexpr int BM = 128, BN = 128, D = 128;
+constexpr int BM = 128, BN = 128, D = 128, ROWS = 256;
 constexpr int TILE = 128 * 128;                   // one 64-column block of 128 rows (bytes)
-constexpr int QOFF = 0, KOFF = 2 * TILE, VOFF = 6 * TILE;
-constexpr int BAROFF = 10 * TILE;                 // 160 KB of tiles, then barriers
-constexpr int NBAR = 19;
+constexpr int QOFF = 0, KOFF = 4 * TILE, VOFF = 8 * TILE;
+constexpr int BAROFF = 12 * TILE;                 // 192 KB of tiles, then barriers
+constexpr int NBAR = 15;
 constexpr int SMEM = BAROFF + NBAR * 8 + 16 + 1024;
 constexpr float kRescaleThreshold = 8.f;          // log2 units
 }  // namespace pf
@@ -67,8 +72,20 @@ __device__ __forceinline__ int pf_find_seq(const int32_t* cu, int n, int t) {
   return ans;
 }
 
+// 2^x on the FMA pipe: x = n + f with n = round(x) (magic-number rounding),
+// f in [-0.5, 0.5], 2^f from a cubic least-squares fit (relative error below
+// 1.2e-4, far under the 16-bit rounding P is stored with), 2^n added to the
+// exponent field.  Valid for x >= -126.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.05459282547f, f, 0.24221783876f), f, 0.69336861372f), f, 1.0f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 template <typename T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const PrefillTcParams p) {
   using namespace pf;
@@ -80,10 +97,9 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* k_empty = bars + 3;  // [2]
   uint64_t* v_full = bars + 5;   // [2]
   uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [3]
-  uint64_t* p_full = bars + 12;  // [3]
-  uint64_t* s_free = bars + 15;  // [3]
-  uint64_t* o_done = bars + 18;
+  uint64_t* s_full = bars + 9;   // [2] per tile
+  uint64_t* p_full = bars + 11;  // [2] per tile
+  uint64_t* o_done = bars + 13;  // [2] per tile
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -96,19 +112,19 @@ __global__ void __launch_bounds__(192, 1)
   // ---------------- which rows does this CTA own (CTA-uniform) ----------------
   int s, row0, row1;
   if (slot < p.n_aligned) {
-    row0 = (p.n_aligned - 1 - slot) * BM;
+    row0 = (p.n_aligned - 1 - slot) * ROWS;
     if (row0 >= cu_end) return;
     s = pf_find_seq(p.cu_seqlens, S, row0);
-    row1 = min(row0 + BM, static_cast<int>(p.cu_seqlens[s + 1]));
+    row1 = min(row0 + ROWS, static_cast<int>(p.cu_seqlens[s + 1]));
   } else if (slot < p.n_aligned + S) {
     s = slot - p.n_aligned;
     const int st = p.cu_seqlens[s], en = p.cu_seqlens[s + 1];
-    if (st % BM == 0 || st >= en) return;
+    if (st % ROWS == 0 || st >= en) return;
     row0 = st;
-    row1 = min((st / BM + 1) * BM, en);
+    row1 = min((st / ROWS + 1) * ROWS, en);
   } else {
     // rows past the last sequence: zeros (FP:189)
-    for (int t = cu_end + warp; t < p.total_tokens; t += 6) {
+    for (int t = cu_end + warp; t < p.total_tokens; t += 10) {
       T* o = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(t) * p.so_t + static_cast<int64_t>(h) * p.so_h;
       for (int d = lane; d < D; d += 32) o[d] = Elem<T>::from_f(0.f);
       if (lane == 0 && p.lse) p.lse[static_cast<int64_t>(t) * p.H + h] = -INFINITY;
@@ -117,10 +133,15 @@ __global__ void __launch_bounds__(192, 1)
   }
   const int seq_start = p.cu_seqlens[s];
   const int seq_len = p.cu_seqlens[s + 1] - seq_start;
-  const int rows_valid = row1 - row0;
-  const int p0 = row0 - seq_start;
-  const int kv_keys = p.causal ? min(seq_len, p0 + rows_valid) : seq_len;
-  const int n_kv = (kv_keys + BN - 1) / BN;
+  const int rows_t[2] = {min(BM, row1 - row0), max(0, row1 - row0 - BM)};
+  const int p0_t[2] = {row0 - seq_start, row0 - seq_start + BM};
+  int n_t[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int keys = rows_t[t] <= 0 ? 0 : (p.causal ? min(seq_len, p0_t[t] + rows_t[t]) : seq_len);
+    n_t[t] = (keys + BN - 1) / BN;
+  }
+  const int n_kv = max(n_t[0], n_t[1]);
   const int kvh = h / p.G;
 
   if (tid == 0) {
@@ -130,17 +151,14 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
-    }
-    for (int i = 0; i < 3; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
-      mbar_init(&s_free[i], 1);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(o_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
   }
@@ -150,15 +168,18 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t taddr = *tmem_holder;
   const uint32_t sbase = smem_u32(smem);
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, 2 * TILE);
-      tma_load_3d(smem + QOFF, &tmQ, q_full, 0, h, row0);
-      tma_load_3d(smem + QOFF + TILE, &tmQ, q_full, 64, h, row0);
+      const int nq = rows_t[1] > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, nq * 2 * TILE);
+      for (int t = 0; t < nq; ++t) {
+        tma_load_3d(smem + QOFF + t * 2 * TILE, &tmQ, q_full, 0, h, row0 + t * BM);
+        tma_load_3d(smem + QOFF + t * 2 * TILE + TILE, &tmQ, q_full, 64, h, row0 + t * BM);
+      }
       for (int j = 0; j < n_kv && !*abort_flag; ++j) {
         const int st = j & 1;
         const int key0 = seq_start + j * BN;
@@ -178,90 +199,124 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_3d(smem + VOFF + st * 2 * TILE + TILE, &tmV, &v_full[st], 64, kvh, key0);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr int AB = sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t idesc_qk = tc_idesc_f16(AB, BM, BN, 0);
       const uint32_t idesc_pv = tc_idesc_f16(AB, BM, D, 1);
-      bool ok = mbar_wait(q_full, 0);
-      auto issue_qk = [&](int j) -> bool {
-        const int b = j % 3, st = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
-        if (j >= 3 && !mbar_wait(&s_free[b], ((j / 3) - 1) & 1)) return false;
-        tc_fence_after();
-        const uint32_t d_tmem = taddr + 128 + b * 128;
+      auto qk = [&](int t, int j) {
+        const int st = j & 1;
+        const uint32_t d_tmem = taddr + 256 + t * 128;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t koff = (kk >> 2) * TILE + (kk & 3) * 32;
-          const uint64_t a = tc_sdesc_sw128(sbase + QOFF + koff, 16, 1024);
-          const uint64_t bd = tc_sdesc_sw128(sbase + KOFF + st * 2 * TILE + koff, 16, 1024);
-          tc_mma_ss(d_tmem, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          tc_mma_ss(d_tmem, tc_sdesc_sw128(sbase + QOFF + t * 2 * TILE + koff, 16, 1024),
+                    tc_sdesc_sw128(sbase + KOFF + st * 2 * TILE + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[b]);
-        tc_commit(&k_empty[st]);
-        return true;
+        tc_commit(&s_full[t]);
       };
-      if (ok) ok = issue_qk(0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        if (*abort_flag) break;
-        if (j + 1 < n_kv && !(ok = issue_qk(j + 1))) break;
-        const int b = j % 3, st = j & 1;
-        if (!(ok = mbar_wait(&p_full[b], (j / 3) & 1))) break;
-        if (!(ok = mbar_wait(&v_full[st], (j >> 1) & 1))) break;
-        tc_fence_after();
-        const uint32_t p_tmem = taddr + 128 + b * 128;
+      auto pv = [&](int t, int j) {
+        const int st = j & 1;
+        const uint32_t p_tmem = taddr + 256 + t * 128;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bd = tc_sdesc_sw128(sbase + VOFF + st * 2 * TILE + kk * 2048, TILE, 1024);
-          tc_mma_ts(taddr, p_tmem + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(o_done);
-        tc_commit(&v_empty[st]);
-        tc_commit(&s_free[b]);
+        for (int kk = 0; kk < BN / 16; ++kk)
+          tc_mma_ts(taddr + t * 128, p_tmem + kk * 8,
+                    tc_sdesc_sw128(sbase + VOFF + st * 2 * TILE + kk * 2048, TILE, 1024), idesc_pv,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&o_done[t]);
+      };
+      bool ok = n_kv > 0 && mbar_wait(q_full, 0) && mbar_wait(&k_full[0], 0);
+      if (ok) {
+        tc_fence_after();
+        if (n_t[0] > 0) qk(0, 0);
+        if (n_t[1] > 0) qk(1, 0);
+        tc_commit(&k_empty[0]);
       }
-      if (!ok) *abort_flag = 1;
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (*abort_flag) {
+          ok = false;
+          break;
+        }
+        const int st = j & 1;
+        if (!(ok = mbar_wait(&v_full[st], (j >> 1) & 1))) break;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (j < n_t[t]) {
+            if (!(ok = mbar_wait(&p_full[t], j & 1))) break;
+            tc_fence_after();
+            pv(t, j);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&v_empty[st]);
+        if (j + 1 < n_kv) {
+          if (!(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) break;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (j + 1 < n_t[t]) {
+              // this tile's S/P columns are rewritten only after its PV of block j has read P
+              if (!(ok = mbar_wait(&o_done[t], j & 1))) break;
+              tc_fence_after();
+              qk(t, j + 1);
+            }
+          }
+          if (!ok) break;
+          tc_commit(&k_empty[(j + 1) & 1]);
+        }
+      }
+      if (!ok && n_kv > 0) *abort_flag = 1;
     }
-  } else {
-    // ---------------- softmax + epilogue: warps 0-3, thread = row ----------------
-    const int r = tid;
-    const bool row_ok = r < rows_valid;
-    const int lim = !row_ok ? 0 : (p.causal ? min(seq_len, p0 + r + 1) : seq_len);
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  } else if (warp < 8) {
+    // ---------------- softmax + epilogue: warps 0-3 tile A, warps 4-7 tile B ----------------
+    const int t = warp >> 2;
+    const int r = tid & 127;
+    const int nt = n_t[t];
+    const bool row_ok = r < rows_t[t];
+    const int lim = !row_ok ? 0 : (p.causal ? min(seq_len, p0_t[t] + r + 1) : seq_len);
+    // blocks below this bound need no mask for any row of the tile
+    const int lim_all = p.causal ? min(seq_len, p0_t[t] + 1) : seq_len;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t s_tmem = taddr + lane_off + 256 + t * 128;
+    const uint32_t o_tmem = taddr + lane_off + t * 128;
     float m_run = -INFINITY, m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int b = j % 3;
-      if (!(ok = mbar_wait(&s_full[b], (j / 3) & 1))) break;
+    for (int j = 0; j < nt; ++j) {
+      if (!(ok = mbar_wait(&s_full[t], j & 1))) break;
       tc_fence_after();
-      uint32_t sr[128];
-      const uint32_t s_tmem = taddr + lane_off + 128 + b * 128;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + c * 32, sr + c * 32);
-      tmem_ld_wait();
-      const int nvalid = lim - j * BN;  // keys [0, nvalid) of this block are visible to the row
+      const bool interior = (j + 1) * BN <= lim_all;
+      const int nvalid = lim - j * BN;
+      // pass 1: row max over the 128 scores (two 64-column loads)
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float v = c < nvalid ? __uint_as_float(sr[c]) : -INFINITY;
-        mx = fmaxf(mx, v);
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t sr[64];
+        tmem_ld32(s_tmem + hh * 64, sr);
+        tmem_ld32(s_tmem + hh * 64 + 32, sr + 32);
+        tmem_ld_wait();
+        if (interior) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, hh * 64 + c < nvalid ? __uint_as_float(sr[c]) : -INFINITY);
+        }
       }
       const float m_new = fmaxf(m_run, mx * p.scale_log2);
       const bool need = m_new != -INFINITY && m_new > m_used + kRescaleThreshold;
       const bool rescale_o = need && m_used != -INFINITY;
       if (__any_sync(0xffffffffu, rescale_o)) {
-        // O holds PV of blocks < j: wait for the last of them, then rescale rows in place
-        if (!(ok = mbar_wait(o_done, (j - 1) & 1))) break;
+        if (!(ok = mbar_wait(&o_done[t], (j - 1) & 1))) break;
         tc_fence_after();
         const float f = rescale_o ? fast_exp2(m_used - m_new) : 1.f;
         uint32_t orow[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          tmem_ld32(taddr + lane_off + c * 32, orow);
+          tmem_ld32(o_tmem + c * 32, orow);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * f);
-          tmem_st32(taddr + lane_off + c * 32, orow);
+          tmem_st32(o_tmem + c * 32, orow);
         }
         tmem_st_wait();
         l *= f;
@@ -269,50 +324,73 @@ __global__ void __launch_bounds__(192, 1)
       if (need) m_used = m_new;
       m_run = m_new;
       const float mu = m_used == -INFINITY ? 0.f : m_used;
-      uint32_t pk[64];
-      float ls = 0.f;
+      const float sl2 = p.scale_log2;
+      // pass 2: P = 2^(s*scale - m), 32 scores at a time; the 16 packed columns
+      // of chunk c land on S columns [16c, 16c+16), already consumed
+      float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float a = (2 * c < nvalid) ? fast_exp2(__uint_as_float(sr[2 * c]) * p.scale_log2 - mu) : 0.f;
-        const float bb = (2 * c + 1 < nvalid) ? fast_exp2(__uint_as_float(sr[2 * c + 1]) * p.scale_log2 - mu) : 0.f;
-        ls += a + bb;
-        pk[c] = Elem<T>::pack2(a, bb);
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t sr[32], pk[16];
+        tmem_ld32(s_tmem + c4 * 32, sr);
+        tmem_ld_wait();
+        if (interior) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float a = fast_exp2(fmaf(__uint_as_float(sr[2 * c]), sl2, -mu));
+            const float bb = exp2_fma(fmaf(__uint_as_float(sr[2 * c + 1]), sl2, -mu));
+            ls0 += a;
+            ls1 += bb;
+            pk[c] = Elem<T>::pack2(a, bb);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int e = 32 * c4 + 2 * c;
+            const float a = (e < nvalid) ? fast_exp2(fmaf(__uint_as_float(sr[2 * c]), sl2, -mu)) : 0.f;
+            const float bb = (e + 1 < nvalid) ? exp2_fma(fmaf(__uint_as_float(sr[2 * c + 1]), sl2, -mu)) : 0.f;
+            ls0 += a;
+            ls1 += bb;
+            pk[c] = Elem<T>::pack2(a, bb);
+          }
+        }
+        tmem_st16(s_tmem + 16 * c4, pk);
       }
-      l += ls;
-      tmem_st32(s_tmem, pk);
-      tmem_st32(s_tmem + 32, pk + 32);
+      l += ls0 + ls1;
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[b]);
+      mbar_arrive(&p_full[t]);
     }
-    if (ok && n_kv > 0) ok = mbar_wait(o_done, (n_kv - 1) & 1);
+    if (ok && nt > 0) ok = mbar_wait(&o_done[t], (nt - 1) & 1);
     if (!ok) *abort_flag = 1;
-    tc_fence_after();
-    float o[128];
+    if (nt > 0) {
+      tc_fence_after();
+      float o[128];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) tmem_ld32(taddr + lane_off + c * 32, reinterpret_cast<uint32_t*>(o) + c * 32);
-    tmem_ld_wait();
-    if (row_ok) {
-      const float f = (m_used == -INFINITY || n_kv == 0) ? 0.f : fast_exp2(m_used - m_run);
-      const float inv = (l > 0.f && ok) ? f / (l * f + 1e-6f) : 0.f;
-      T* orow = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(row0 + r) * p.so_t +
-                static_cast<int64_t>(h) * p.so_h;
+      for (int c = 0; c < 4; ++c) tmem_ld32(o_tmem + c * 32, reinterpret_cast<uint32_t*>(o) + c * 32);
+      tmem_ld_wait();
+      if (row_ok) {
+        const float f = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_run);
+        const float inv = (l > 0.f && ok) ? f / (l * f + 1e-6f) : 0.f;
+        T* orow = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(row0 + t * BM + r) * p.so_t +
+                  static_cast<int64_t>(h) * p.so_h;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 u;
-        u.x = Elem<T>::pack2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
-        u.y = Elem<T>::pack2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-        u.z = Elem<T>::pack2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-        u.w = Elem<T>::pack2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-        *reinterpret_cast<uint4*>(orow + 8 * c) = u;
+        for (int c = 0; c < 16; ++c) {
+          uint4 u;
+          u.x = Elem<T>::pack2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
+          u.y = Elem<T>::pack2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+          u.z = Elem<T>::pack2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+          u.w = Elem<T>::pack2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+          *reinterpret_cast<uint4*>(orow + 8 * c) = u;
+        }
+        if (p.lse)
+          p.lse[static_cast<int64_t>(row0 + t * BM + r) * p.H + h] =
+              (l > 0.f && ok) ? (m_used + __log2f(l)) * kLn2 : -INFINITY;
       }
-      if (p.lse)
-        p.lse[static_cast<int64_t>(row0 + r) * p.H + h] = (l > 0.f && ok) ? (m_used + __log2f(l)) * kLn2 : -INFINITY;
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(taddr, 512);
   }
@@ -337,7 +415,7 @@ int prefill_tc_launch(const PrefillArgs& a, cudaStream_t st, bool* handled) {
   if (a.dtype == kF32 || a.head_dim != 128 || a.head_dim_v != 128) return 0;
   if (!tma_ok(a.q, a.sq) || !tma_ok(a.k, a.sk) || !tma_ok(a.v, a.sv)) return 0;
   if (a.so[2] != 1 || (a.so[0] % 8) || (a.so[1] % 8) || (reinterpret_cast<uintptr_t>(a.out) & 15)) return 0;
-  const int n_aligned = (a.total_tokens + pf::BM - 1) / pf::BM;
+  const int n_aligned = (a.total_tokens + pf::ROWS - 1) / pf::ROWS;
   if (static_cast<int64_t>(n_aligned) + a.num_seqs + 1 > 65535) return 0;
   CUtensorMap mq, mk, mv;
   if (int r = encode_tnd_map(&mq, a.q, a.sq, a.total_tokens, a.num_q_heads)) return r;
@@ -360,10 +438,10 @@ int prefill_tc_launch(const PrefillArgs& a, cudaStream_t st, bool* handled) {
   dim3 grid(a.num_q_heads, n_aligned + a.num_seqs + 1);
   if (a.dtype == kBF16) {
     cudaFuncSetAttribute(prefill_tc_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
-    prefill_tc_kernel<__nv_bfloat16><<<grid, 192, pf::SMEM, st>>>(mq, mk, mv, p);
+    prefill_tc_kernel<__nv_bfloat16><<<grid, 320, pf::SMEM, st>>>(mq, mk, mv, p);
   } else {
     cudaFuncSetAttribute(prefill_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
-    prefill_tc_kernel<__half><<<grid, 192, pf::SMEM, st>>>(mq, mk, mv, p);
+    prefill_tc_kernel<__half><<<grid, 320, pf::SMEM, st>>>(mq, mk, mv, p);
   }
   *handled = true;
   return 0;
