@@ -183,6 +183,23 @@ int tak_compress_kv_paged(const void* k_cache, const int64_t* k_strides, const v
                           void* compressed_v, const int64_t* cv_strides, int64_t num_kv_heads, int64_t head_dim,
                           int64_t head_dim_v, int64_t stride, int64_t window, int dtype, void* stream);
 
+/* CSA and HCA pooling of the same TND K/V (and gate) in one pass: the CSA
+ * outputs of compress_kv_overlap (attention/csa.py:9-69, window 2m, stride m,
+ * offsets csa_offsets) and the HCA outputs of compress_kv_simple
+ * (attention/hca.py:9-69, window = stride = m_prime, offsets hca_offsets),
+ * which the reference computes with two separate passes over K/V.  Shapes the
+ * single-pass kernel does not take (fp32, m_prime not a multiple of m,
+ * m_prime + m > 256, head dims not multiples of 128, unaligned strides) run as
+ * two tak_compress_kv passes with the same results.  total_tokens = rows of
+ * K/V/gate. */
+int tak_compress_kv_csa_hca(const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                            const float* gate, int64_t gate_stride, const int32_t* cu_seqlens, int64_t num_seqs,
+                            int64_t total_tokens, const int32_t* csa_offsets, int64_t num_csa, void* csa_k,
+                            const int64_t* csa_k_strides, void* csa_v, const int64_t* csa_v_strides,
+                            const int32_t* hca_offsets, int64_t num_hca, void* hca_k, const int64_t* hca_k_strides,
+                            void* hca_v, const int64_t* hca_v_strides, int64_t num_kv_heads, int64_t head_dim,
+                            int64_t head_dim_v, int64_t m, int64_t m_prime, int dtype, void* stream);
+
 /* Sliding-window columns [0, n_win) of prefill index rows (row stride ld).
  * Replaces attention/csa.py:108-117 (same rule at hca.py:133-137). */
 int tak_build_window_idxs(const int32_t* cu_seqlens, int64_t num_seqs, int64_t total_tokens, int64_t n_win,

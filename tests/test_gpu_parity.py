@@ -395,6 +395,40 @@ def test_compress_csa_hca(dtype, gated):
         close(cv, rv, 1e-2)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("gated", [False, True])
+@pytest.mark.parametrize("shape", ["ragged", "latent512", "strided", "m3"])
+def test_compress_csa_hca_one_pass(dtype, gated, shape):
+    """CSA + HCA pooling of the same K/V in one launch vs the oracle's two
+    separate poolings: ragged lengths (empty, shorter than m, chunk-straddling
+    tails), 512-dim latent rows, a strided K/V view, and m = 3 (m' = 128 not a
+    multiple of m: the two-pass path)."""
+    g = torch.Generator().manual_seed(71)
+    m, mp, hkv, D, Dv = 4, 128, 2, 128, 256
+    if shape == "latent512":
+        lens, hkv, D, Dv = [4096, 77, 4096], 1, 512, 512
+    else:
+        lens = [0, 3, 4, 5, 130, 257, 1, 0, 132]
+    if shape == "m3":
+        m = 3
+    Tn = sum(lens)
+    if shape == "strided":
+        big = torch.randn(Tn, hkv, 2 * D + Dv, generator=g).to(DEV, dtype)
+        k, v = big[:, :, :D], big[:, :, 2 * D:]
+    else:
+        k = torch.randn(Tn, hkv, D, generator=g).to(DEV, dtype)
+        v = torch.randn(Tn, hkv, Dv, generator=g).to(DEV, dtype)
+    gate = torch.randn(Tn, generator=g).to(DEV) if gated else None
+    cuq = _cu_t(lens)
+    (ck, cv, co), (hk, hv, ho) = CSA.compress_kv_csa_hca(k, v, cuq, m, mp, gate=gate)
+    gnp = None if gate is None else gate.cpu()
+    for (gk, gv, go), (stride, window) in (((ck, cv, co), (m, 2 * m)), ((hk, hv, ho), (mp, mp))):
+        rk, rv, roffs = O.compress_kv(npy(k), npy(v), cuq.cpu(), stride, window, gnp)
+        np.testing.assert_array_equal(go.cpu().numpy(), roffs)
+        close(gk, rk, 1e-2)
+        close(gv, rv, 1e-2)
+
+
 def test_compress_paged_matches_tnd():
     q, kc, vc, bt, cl = _paged_case(5, 8, 2, 128, 16, 300, 120, torch.bfloat16, 33, [0, 17, 300, 64, 1])
     ck, cv, offs, lens, _ = T.compress_paged(kc, vc, bt, cl, 16, 4, 8)

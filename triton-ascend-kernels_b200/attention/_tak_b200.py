@@ -43,6 +43,8 @@ _SIGS = {
                          _I64, _I32, _P], _I32),
     "tak_compress_kv_paged": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _P, _P, _P, _P, _I64,
                                _I64, _I64, _I64, _I64, _I32, _P], _I32),
+    "tak_compress_kv_csa_hca": ([_P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _P,
+                                 _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I32, _P], _I32),
     "tak_build_window_idxs": ([_P, _I64, _I64, _I64, _P, _I64, _P], _I32),
     "tak_build_hca_topk_idxs": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P], _I32),
     "tak_build_decode_topk_idxs": ([_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P], _I32),
@@ -178,6 +180,39 @@ def compress_tnd(k, v, cu_seqlens, stride, window, gate=None):
             ptr(offs_t), len(cu_h) - 1, nc, ptr(ck), strides(ck), ptr(cv), strides(cv), hkv, k.shape[2],
             v.shape[2], stride, window, dtype_code(k), stream_of(k)))
     return ck, cv, offs_t
+
+
+def compress_csa_hca(k, v, cu_seqlens, m, m_prime, gate=None):
+    """CSA (window 2m, stride m) and HCA (window = stride = m_prime) pooling of
+    the same TND K/V in one pass.  Returns ((csa_k, csa_v, csa_offsets),
+    (hca_k, hca_v, hca_offsets)), offsets int32 on the device."""
+    require_cuda(k, v)
+    dev = k.device
+    if isinstance(cu_seqlens, torch.Tensor) and cu_seqlens.is_cuda:
+        cu = as_i32(cu_seqlens, dev)
+        cu_h = cu.cpu().tolist()          # device -> host copy (sizes the outputs)
+    else:
+        cu_h = [int(x) for x in (cu_seqlens.tolist() if isinstance(cu_seqlens, torch.Tensor) else cu_seqlens)]
+        cu = torch.tensor(cu_h, dtype=torch.int32).to(dev, non_blocking=True)
+    lens = [cu_h[i + 1] - cu_h[i] for i in range(len(cu_h) - 1)]
+    hkv = k.shape[1]
+    res = []
+    for stride in (m, m_prime):
+        offs = comp_offsets_host(lens, stride)
+        nc = offs[-1]
+        res.append((k.new_empty((nc, hkv, k.shape[2])), v.new_empty((nc, hkv, v.shape[2])),
+                    torch.tensor(offs, dtype=torch.int32).to(dev), nc))
+    (ck, cv, co, nc), (hk, hv, ho, nh) = res
+    if nc or nh:
+        g = None
+        if gate is not None:
+            g = gate.to(device=dev, dtype=torch.float32)
+            assert g.dim() == 1 and g.shape[0] == k.shape[0], "gate must be [total_tokens] logits"
+        check(lib().tak_compress_kv_csa_hca(
+            ptr(k), strides(k), ptr(v), strides(v), ptr(g), g.stride(0) if g is not None else 0, ptr(cu),
+            len(cu_h) - 1, k.shape[0], ptr(co), nc, ptr(ck), strides(ck), ptr(cv), strides(cv), ptr(ho), nh, ptr(hk),
+            strides(hk), ptr(hv), strides(hv), hkv, k.shape[2], v.shape[2], m, m_prime, dtype_code(k), stream_of(k)))
+    return (ck, cv, co), (hk, hv, ho)
 
 
 def compress_paged(k_cache, v_cache, block_tables, context_lens, block_size, stride, window):

@@ -36,6 +36,16 @@ def compress_kv_overlap(k, v, cu_seqlens, m, *, gate=None):
     return _t.compress_tnd(k, v, cu_seqlens, m, 2 * m, gate)
 
 
+def compress_kv_csa_hca(k, v, cu_seqlens, m, m_prime, *, gate=None):
+    """compress_kv_overlap(k, v, cu_seqlens, m) and hca.compress_kv_simple(k,
+    v, cu_seqlens, m_prime) of the same K/V (and gate) in one pass over K/V.
+
+    Returns ((csa_k, csa_v, csa_offsets), (hca_k, hca_v, hca_offsets)), each
+    triple as the single-stride function returns it.
+    """
+    return _t.compress_csa_hca(k, v, cu_seqlens, m, m_prime, gate)
+
+
 def build_csa_topk_idxs(q, compressed_k, cu_seqlens, comp_offsets, n_win, top_k, m):
     """topk_idxs [total_tokens, n_win + top_k] int32, -1 for padding:
     [n_win sliding-window positions] + [top_k compressed indices + total_tokens]."""

@@ -1,0 +1,116 @@
+"""Sequence / request sharding across ranks (one process per GPU) and the
+output gather.
+
+The reference is single-device (no torch.distributed anywhere in
+attention/*.py).  Attention over independent sequences (prefill, sparse
+prefill, compression) and independent requests (paged decode, sparse decode)
+needs no exchange between them, so the multi-GPU form is: give each rank whole
+sequences or whole requests, balance their cost with a greedy
+longest-processing-time rule, run each rank's share with the single-GPU
+functions, and gather the outputs once (NCCL all-gather on GPUs; any backend
+works, the tests use gloo).
+"""
+import heapq
+
+import torch
+import torch.distributed as dist
+
+
+def lpt_assign(costs, world):
+    """Owner rank of each item.  Items in decreasing cost (ties: lower index
+    first) go to the currently least-loaded rank (ties: lower rank)."""
+    assert world >= 1
+    heap = [(0.0, r) for r in range(world)]
+    owner = [0] * len(costs)
+    for i in sorted(range(len(costs)), key=lambda j: (-float(costs[j]), j)):
+        load, r = heapq.heappop(heap)
+        owner[i] = r
+        heapq.heappush(heap, (load + float(costs[i]), r))
+    return owner
+
+
+def _host_list(x):
+    if isinstance(x, torch.Tensor):
+        return [int(v) for v in x.cpu().tolist()]
+    return [int(v) for v in x]
+
+
+def prefill_costs(lengths, causal=True):
+    """Score-matrix entries per sequence: L(L+1)/2 causal, L^2 otherwise."""
+    return [L * (L + 1) // 2 if causal else L * L for L in lengths]
+
+
+class VarlenShard:
+    """One rank's share of a varlen (TND) batch.
+
+    seq_ids      global indices of the sequences this rank owns (ascending)
+    cu_seqlens   int32 [len(seq_ids) + 1] offsets of the local TND batch
+    token_index  int64 [local tokens] global token row of each local row
+    """
+
+    def __init__(self, seq_ids, cu_seqlens, token_index):
+        self.seq_ids = seq_ids
+        self.cu_seqlens = cu_seqlens
+        self.token_index = token_index
+
+    def take(self, x):
+        """Local rows of a global [T, ...] tensor."""
+        return x.index_select(0, self.token_index.to(x.device))
+
+
+def shard_varlen(cu_seqlens, world, rank, causal=True, costs=None):
+    """Sequences of a varlen batch for `rank`, balanced by attention cost."""
+    cu = _host_list(cu_seqlens)
+    lengths = [cu[i + 1] - cu[i] for i in range(len(cu) - 1)]
+    owner = lpt_assign(costs if costs is not None else prefill_costs(lengths, causal), world)
+    seq_ids = [s for s in range(len(lengths)) if owner[s] == rank]
+    local_cu, rows = [0], []
+    for s in seq_ids:
+        rows.append(torch.arange(cu[s], cu[s + 1], dtype=torch.int64))
+        local_cu.append(local_cu[-1] + lengths[s])
+    token_index = torch.cat(rows) if rows else torch.zeros(0, dtype=torch.int64)
+    return VarlenShard(seq_ids, torch.tensor(local_cu, dtype=torch.int32), token_index)
+
+
+def shard_requests(context_lens, world, rank):
+    """Decode requests for `rank` (int64 indices, ascending), balanced by
+    context length (the bytes each request streams)."""
+    ctx = _host_list(context_lens)
+    owner = lpt_assign([max(c, 1) for c in ctx], world)
+    return torch.tensor([b for b in range(len(ctx)) if owner[b] == rank], dtype=torch.int64)
+
+
+def gather_rows(local, index, total_rows, group=None, dst=None):
+    """Gather variable-sized row blocks: rank r holds rows `index` (global row
+    numbers, int64) of a [total_rows, ...] result.  With dst=None every rank
+    returns the whole result (all-gather); with dst=k only rank k does and the
+    others return None (gather, for results too large to replicate).  Blocks
+    are padded to the largest rank's row count for the collective."""
+    world = dist.get_world_size(group)
+    me = dist.get_rank(group)
+    dev = local.device
+    n = torch.tensor([local.shape[0]], dtype=torch.int64, device=dev)
+    counts = [torch.empty_like(n) for _ in range(world)]
+    dist.all_gather(counts, n, group=group)
+    counts = [int(c) for c in counts]
+    mx = max(counts) if counts else 0
+    pad = local.new_zeros((mx,) + tuple(local.shape[1:]))
+    pad[: local.shape[0]] = local
+    ipad = torch.full((mx,), -1, dtype=torch.int64, device=dev)
+    ipad[: local.shape[0]] = index.to(dev)
+    receive = dst is None or me == dst
+    blocks = [torch.empty_like(pad) for _ in range(world)] if receive else None
+    idxs = [torch.empty_like(ipad) for _ in range(world)] if receive else None
+    if dst is None:
+        dist.all_gather(blocks, pad, group=group)
+        dist.all_gather(idxs, ipad, group=group)
+    else:
+        dist.gather(pad, blocks, dst=dst, group=group)
+        dist.gather(ipad, idxs, dst=dst, group=group)
+    if not receive:
+        return None
+    full = local.new_zeros((total_rows,) + tuple(local.shape[1:]))
+    for blk, ix, c in zip(blocks, idxs, counts):
+        if c:
+            full[ix[:c]] = blk[:c]
+    return full

@@ -2,7 +2,9 @@
 // validation, error strings, tensor-map encoding, dispatch to the kernels.
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "../../include/tak_attention.h"
 #include "common.cuh"
@@ -34,6 +36,25 @@ int num_sms() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n > 0 ? n : 148;
+}
+
+int ensure_smem_attr(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = done[{func, dev}];
+  if (have >= bytes) return 0;
+  const cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    char buf[160];
+    std::snprintf(buf, sizeof(buf), "cudaFuncSetAttribute(max dynamic shared memory = %d) failed: %s", bytes,
+                  cudaGetErrorString(e));
+    return set_error(3, buf);
+  }
+  have = bytes;
+  return 0;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -372,6 +393,34 @@ int tak_compress_kv_paged(const void* k_cache, const int64_t* k_strides, const v
   if (gate) copy_strides(a.sg, gate_strides, 2);
   r = compress_launch(a, static_cast<cudaStream_t>(stream));
   return r ? r : check_launch("compress paged");
+}
+
+int tak_compress_kv_csa_hca(const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                            const float* gate, int64_t gate_stride, const int32_t* cu_seqlens, int64_t num_seqs,
+                            int64_t total_tokens, const int32_t* csa_offsets, int64_t num_csa, void* csa_k,
+                            const int64_t* csa_k_strides, void* csa_v, const int64_t* csa_v_strides,
+                            const int32_t* hca_offsets, int64_t num_hca, void* hca_k, const int64_t* hca_k_strides,
+                            void* hca_v, const int64_t* hca_v_strides, int64_t num_kv_heads, int64_t head_dim,
+                            int64_t head_dim_v, int64_t m, int64_t m_prime, int dtype, void* stream) {
+  if (num_csa == 0 && num_hca == 0) return 0;
+  TAK_REQUIRE(m > 0 && m_prime > 0, "compress csa+hca: m and m_prime must be positive");
+  TAK_REQUIRE(total_tokens > 0, "compress csa+hca: total_tokens must be positive when slots exist");
+  CompressArgs csa{}, hca{};
+  int r = compress_common(csa, k, k_strides, 3, v, v_strides, csa_offsets, num_seqs, num_csa, csa_k, csa_k_strides,
+                          csa_v, csa_v_strides, num_kv_heads, head_dim, head_dim_v, m, 2 * m, dtype);
+  if (r) return r;
+  r = compress_common(hca, k, k_strides, 3, v, v_strides, hca_offsets, num_seqs, num_hca, hca_k, hca_k_strides,
+                      hca_v, hca_v_strides, num_kv_heads, head_dim, head_dim_v, m_prime, m_prime, dtype);
+  if (r) return r;
+  TAK_REQUIRE(cu_seqlens, "compress csa+hca: null cu_seqlens");
+  for (CompressArgs* a : {&csa, &hca}) {
+    a->cu_seqlens = cu_seqlens;
+    a->gate = gate;
+    a->sg[0] = gate_stride;
+    a->total_rows = total_tokens;
+  }
+  r = compress_csa_hca_launch(csa, hca, static_cast<cudaStream_t>(stream));
+  return r ? r : check_launch("compress csa+hca");
 }
 
 int tak_build_window_idxs(const int32_t* cu_seqlens, int64_t num_seqs, int64_t total_tokens, int64_t n_win,

@@ -45,9 +45,10 @@ template <> struct Elem<__nv_bfloat16> {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+  // bf16 -> fp32 is exact bit placement (the bf16 bits become the high half
+  // of the fp32 word), done with integer shift / mask on the ALU pipes
   static __device__ __forceinline__ float2 unpack2(uint32_t u) {
-    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);
-    return __bfloat1622float2(h);
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
   }
 };
 template <> struct Elem<__half> {
@@ -112,6 +113,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(a, parity)) return true;
     if ((i & 255u) == 0u && globaltimer() - t0 > TAK_WAIT_LIMIT_NS) {
+      record_error(1);
+      return false;
+    }
+  }
+}
+
+// Like mbar_wait, but each probe may suspend the thread in hardware (until the
+// phase completes or suspend_ns elapse) instead of returning at once, so
+// waiting warps take no issue slots from working warps on the same SM
+// sub-partition.  Bounded by TAK_WAIT_LIMIT_NS like mbar_wait.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t suspend_ns = 20000) {
+  const uint32_t a = smem_u32(bar);
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity), "r"(suspend_ns)
+        : "memory");
+    if (ok) return true;
+    if (i == 0) {
+      t0 = globaltimer();
+    } else if (globaltimer() - t0 > TAK_WAIT_LIMIT_NS) {
       record_error(1);
       return false;
     }

@@ -663,16 +663,19 @@ int csa_indexer_launch(const IndexerArgs& a, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(a.max_comp_per_seq > 0 ? a.max_comp_per_seq : 1) * sizeof(float);
   if (smem > 200 * 1024) return set_error(2, "csa indexer: more than 51200 compressed slots in one sequence");
   if (a.dtype == kBF16) {
-    cudaFuncSetAttribute(csa_indexer_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
+    if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(csa_indexer_kernel<__nv_bfloat16>),
+                                       static_cast<int>(smem)))
+      return r;
     csa_indexer_kernel<__nv_bfloat16><<<rows, 256, smem, st>>>(a);
   } else if (a.dtype == kF16) {
-    cudaFuncSetAttribute(csa_indexer_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
+    if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(csa_indexer_kernel<__half>),
+                                       static_cast<int>(smem)))
+      return r;
     csa_indexer_kernel<__half><<<rows, 256, smem, st>>>(a);
   } else {
-    cudaFuncSetAttribute(csa_indexer_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
+    if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(csa_indexer_kernel<float>),
+                                       static_cast<int>(smem)))
+      return r;
     csa_indexer_kernel<float><<<rows, 256, smem, st>>>(a);
   }
   return 0;

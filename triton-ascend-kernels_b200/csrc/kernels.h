@@ -13,6 +13,9 @@ namespace tak {
 // error reporting (capi.cu): stores a message for tak_last_error(), returns code
 int set_error(int code, const char* msg);
 int num_sms();
+// cudaFuncAttributeMaxDynamicSharedMemorySize of `func` on the current device,
+// raised to at least `bytes` (set once per device and kernel, cached)
+int ensure_smem_attr(const void* func, int bytes);
 // cuTensorMapEncodeTiled through the runtime's driver entry point
 int encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
                  const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides,
@@ -98,8 +101,13 @@ struct CompressArgs {
   int num_kv_heads, head_dim, head_dim_v;
   int stride, window;
   int dtype;
+  int64_t total_rows;  // TND token count (only the fused CSA + HCA launch reads it)
 };
 int compress_launch(const CompressArgs& a, cudaStream_t st);
+// CSA (window 2m, stride m) and HCA (window = stride = m') pooling of the same
+// K/V/gate in one pass; falls back to two compress_launch calls for shapes the
+// fused kernel does not take.
+int compress_csa_hca_launch(const CompressArgs& csa, const CompressArgs& hca, cudaStream_t st);
 
 int token_to_seq_launch(const int32_t* cu, int num_seqs, int total_tokens, int32_t* out, cudaStream_t st);
 int window_idxs_launch(const int32_t* cu, int num_seqs, int total_tokens, int n_win, int32_t* out, int64_t ld,

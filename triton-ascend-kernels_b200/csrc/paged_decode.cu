@@ -517,7 +517,7 @@ static int launch_fast(const PagedDecodeArgs& a, int pps, int max_splits, int he
   p.max_ctx = a.max_blocks * a.block_size;
   p.scale_log2 = a.scale * kLog2e;
   auto kern = paged_decode_tc_kernel<T, D, CH, NS>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), SMEM)) return r;
   dim3 grid(max_splits, a.num_kv_heads * head_chunks, a.num_seqs);
   kern<<<grid, 160, SMEM, st>>>(mk, mv, p);
   if (max_splits > 1) paged_decode_combine_kernel<T><<<dim3(a.num_seqs, a.num_kv_heads * head_chunks), 128, 0, st>>>(p);

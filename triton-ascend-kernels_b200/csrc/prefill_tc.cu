@@ -14,24 +14,22 @@
 // their diagonal block (the reference sweeps every block, FP:60).  Aligned
 // blocks are issued last-first (longest work first).
 //
-// Warp roles (192 threads):
-//   warp 4      TMA producer: both Q tiles once, then K and V blocks of 128
+// Warp roles (320 threads):
+//   warp 8      TMA producer: both Q tiles once, then K and V blocks of 128
 //               rows into 2-stage rings (128-byte swizzle, 64-column boxes).
-//   warp 5      TMEM allocator + single-thread tcgen05.mma issuer.  Per K/V
-//               block j, tile by tile: PV_t(j) (TS-MMA: P read from TMEM, V
-//               from smem, MN-major), then S_t(j+1) = Q_t K^T (SS-MMA,
-//               M=N=128) once PV_t(j) has completed, so the two tiles run
-//               half a block apart and each softmax overlaps the other
-//               tile's MMAs.
-//   warps 0-3   softmax of both tiles, alternating A(j), B(j), A(j+1), ...
-//               (thread r = row r of each tile = TMEM lane r): load S (one
-//               TMEM round trip), mask only on boundary blocks, online max
+//   warp 9      TMEM allocator + single-thread tcgen05.mma issuer.  Per K/V
+//               block j: PV_A(j), PV_B(j) (TS-MMA: P read from TMEM, V from
+//               smem, MN-major), then S_A(j+1) = Q_A K^T, S_B(j+1) = Q_B K^T
+//               (SS-MMA, M=N=128).  Each tile's S is rewritten only after
+//               that tile's PV of the previous block has completed.
+//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B (thread = row =
+//               TMEM lane): load S, mask only on boundary blocks, online max
 //               with lazy rescaling (O and l rescaled only when the max grows
-//               by more than 2^8), P = 2^(s - m) -- half of the exponentials on
-//               the MUFU unit, half by a cubic polynomial on the FMA pipe --
-//               packed to 16 bits back into the tile's S columns; epilogue
-//               reads O, normalises, stores the row and its LSE.  While the
-//               warpgroup works on one tile the tensor core works on the other.
+//               by more than 2^8), P = 2^(s - m) on the MUFU unit, packed to
+//               16 bits back into the tile's S columns; epilogue
+//               reads O, normalises, stores the row and its LSE.  While one
+//               warpgroup runs its softmax the tensor core works on the other
+//               tile.
 // TMEM: O_A [0,128), O_B [128,256), S/P_A [256,384), S/P_B [384,512).
 #include <type_traits>
 
@@ -73,20 +71,8 @@ __device__ __forceinline__ int pf_find_seq(const int32_t* cu, int n, int t) {
   return ans;
 }
 
-// 2^x on the FMA pipe: x = n + f with n = round(x) (magic-number rounding),
-// f in [-0.5, 0.5], 2^f from a cubic least-squares fit (relative error below
-// 1.2e-4, far under the 16-bit rounding P is stored with), 2^n added to the
-// exponent field.  Valid for x >= -126.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.05459282547f, f, 0.24221783876f), f, 0.69336861372f), f, 1.0f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 template <typename T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const PrefillTcParams p) {
   using namespace pf;
@@ -125,7 +111,7 @@ __global__ void __launch_bounds__(192, 1)
     row1 = min((st / ROWS + 1) * ROWS, en);
   } else {
     // rows past the last sequence: zeros (FP:189)
-    for (int t = cu_end + warp; t < p.total_tokens; t += 6) {
+    for (int t = cu_end + warp; t < p.total_tokens; t += 10) {
       T* o = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(t) * p.so_t + static_cast<int64_t>(h) * p.so_h;
       for (int d = lane; d < D; d += 32) o[d] = Elem<T>::from_f(0.f);
       if (lane == 0 && p.lse) p.lse[static_cast<int64_t>(t) * p.H + h] = -INFINITY;
@@ -159,7 +145,7 @@ __global__ void __launch_bounds__(192, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
   }
@@ -169,7 +155,7 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t taddr = *tmem_holder;
   const uint32_t sbase = smem_u32(smem);
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -200,7 +186,7 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_3d(smem + VOFF + st * 2 * TILE + TILE, &tmV, &v_full[st], 64, kvh, key0);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
@@ -234,9 +220,6 @@ __global__ void __launch_bounds__(192, 1)
         if (n_t[1] > 0) qk(1, 0);
         tc_commit(&k_empty[0]);
       }
-      // Per block j, tile by tile: PV_t(j) as soon as P_t(j) is ready, then
-      // S_t(j+1) once PV_t(j) has consumed P_t(j) -- so one tile's softmax
-      // overlaps the other tile's MMAs (the two tiles run half a block apart).
       for (int j = 0; ok && j < n_kv; ++j) {
         if (*abort_flag) {
           ok = false;
@@ -250,128 +233,130 @@ __global__ void __launch_bounds__(192, 1)
             if (!(ok = mbar_wait(&p_full[t], j & 1))) break;
             tc_fence_after();
             pv(t, j);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&v_empty[st]);
+        if (j + 1 < n_kv) {
+          if (!(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) break;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
             if (j + 1 < n_t[t]) {
-              if (!(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) break;
-              // this tile's S/P columns are rewritten only after PV_t(j) has read P
+              // this tile's S/P columns are rewritten only after its PV of block j has read P
               if (!(ok = mbar_wait(&o_done[t], j & 1))) break;
               tc_fence_after();
               qk(t, j + 1);
             }
           }
+          if (!ok) break;
+          tc_commit(&k_empty[(j + 1) & 1]);
         }
-        if (!ok) break;
-        tc_commit(&v_empty[st]);
-        if (j + 1 < n_kv) tc_commit(&k_empty[(j + 1) & 1]);
       }
       if (!ok && n_kv > 0) *abort_flag = 1;
     }
-  } else {
-    // ---------------- softmax + epilogue: warps 0-3, thread r = row r of both tiles ----------------
-    const int r = tid;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    float m_run[2] = {-INFINITY, -INFINITY}, m_used[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
-    int lim[2], lim_all[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const bool row_ok = r < rows_t[t];
-      lim[t] = !row_ok ? 0 : (p.causal ? min(seq_len, p0_t[t] + r + 1) : seq_len);
-      // blocks below this bound need no mask for any row of the tile
-      lim_all[t] = p.causal ? min(seq_len, p0_t[t] + 1) : seq_len;
-    }
+  } else if (warp < 8) {
+    // ---------------- softmax + epilogue: warps 0-3 tile A, warps 4-7 tile B ----------------
+    const int t = warp >> 2;
+    const int r = tid & 127;
+    const int nt = n_t[t];
+    const bool row_ok = r < rows_t[t];
+    const int lim = !row_ok ? 0 : (p.causal ? min(seq_len, p0_t[t] + r + 1) : seq_len);
+    // blocks below this bound need no mask for any row of the tile
+    const int lim_all = p.causal ? min(seq_len, p0_t[t] + 1) : seq_len;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t s_tmem = taddr + lane_off + 256 + t * 128;
+    const uint32_t o_tmem = taddr + lane_off + t * 128;
+    float m_run = -INFINITY, m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    const float sl2 = p.scale_log2;
-    for (int j = 0; ok && j < n_kv; ++j) {
+    for (int j = 0; j < nt; ++j) {
+      if (!(ok = mbar_wait(&s_full[t], j & 1))) break;
+      tc_fence_after();
+      const bool interior = (j + 1) * BN <= lim_all;
+      const int nvalid = lim - j * BN;
+      // pass 1: row max over the 128 scores (two 64-column loads)
+      float mx = -INFINITY;
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        if (j >= n_t[t]) continue;
-        const uint32_t s_tmem = taddr + lane_off + 256 + t * 128;
-        const uint32_t o_tmem = taddr + lane_off + t * 128;
-        if (!(ok = mbar_wait(&s_full[t], j & 1))) break;
-        tc_fence_after();
-        uint32_t sr[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + c * 32, sr + c * 32);
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t sr[64];
+        tmem_ld32(s_tmem + hh * 64, sr);
+        tmem_ld32(s_tmem + hh * 64 + 32, sr + 32);
         tmem_ld_wait();
-        const bool interior = (j + 1) * BN <= lim_all[t];
-        const int nvalid = lim[t] - j * BN;
-        float mx = -INFINITY;
         if (interior) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
         } else {
 #pragma unroll
-          for (int c = 0; c < 128; ++c) mx = fmaxf(mx, c < nvalid ? __uint_as_float(sr[c]) : -INFINITY);
+          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, hh * 64 + c < nvalid ? __uint_as_float(sr[c]) : -INFINITY);
         }
-        const float m_new = fmaxf(m_run[t], mx * sl2);
-        const bool need = m_new != -INFINITY && m_new > m_used[t] + kRescaleThreshold;
-        const bool rescale_o = need && m_used[t] != -INFINITY;
-        if (__any_sync(0xffffffffu, rescale_o)) {
-          if (!(ok = mbar_wait(&o_done[t], (j - 1) & 1))) break;
-          tc_fence_after();
-          const float f = rescale_o ? fast_exp2(m_used[t] - m_new) : 1.f;
-          uint32_t orow[32];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            tmem_ld32(o_tmem + c * 32, orow);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * f);
-            tmem_st32(o_tmem + c * 32, orow);
-          }
-          tmem_st_wait();
-          lsum[t] *= f;
-        }
-        if (need) m_used[t] = m_new;
-        m_run[t] = m_new;
-        const float mu = m_used[t] == -INFINITY ? 0.f : m_used[t];
-        float ls0 = 0.f, ls1 = 0.f;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
-          if (interior) {
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const int e = 64 * half + 2 * c;
-              const float a = fast_exp2(fmaf(__uint_as_float(sr[e]), sl2, -mu));
-              const float bb = exp2_fma(fmaf(__uint_as_float(sr[e + 1]), sl2, -mu));
-              ls0 += a;
-              ls1 += bb;
-              pk[c] = Elem<T>::pack2(a, bb);
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const int e = 64 * half + 2 * c;
-              const float a = (e < nvalid) ? fast_exp2(fmaf(__uint_as_float(sr[e]), sl2, -mu)) : 0.f;
-              const float bb = (e + 1 < nvalid) ? exp2_fma(fmaf(__uint_as_float(sr[e + 1]), sl2, -mu)) : 0.f;
-              ls0 += a;
-              ls1 += bb;
-              pk[c] = Elem<T>::pack2(a, bb);
-            }
-          }
-          tmem_st32(s_tmem + 32 * half, pk);  // P half over S columns already in registers
-        }
-        lsum[t] += ls0 + ls1;
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(&p_full[t]);
       }
-    }
+      const float m_new = fmaxf(m_run, mx * p.scale_log2);
+      const bool need = m_new != -INFINITY && m_new > m_used + kRescaleThreshold;
+      const bool rescale_o = need && m_used != -INFINITY;
+      if (__any_sync(0xffffffffu, rescale_o)) {
+        if (!(ok = mbar_wait(&o_done[t], (j - 1) & 1))) break;
+        tc_fence_after();
+        const float f = rescale_o ? fast_exp2(m_used - m_new) : 1.f;
+        uint32_t orow[32];
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const int nt = n_t[t];
-      if (nt == 0) continue;
-      if (ok) ok = mbar_wait(&o_done[t], (nt - 1) & 1);
-      if (!ok) *abort_flag = 1;
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(o_tmem + c * 32, orow);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * f);
+          tmem_st32(o_tmem + c * 32, orow);
+        }
+        tmem_st_wait();
+        l *= f;
+      }
+      if (need) m_used = m_new;
+      m_run = m_new;
+      const float mu = m_used == -INFINITY ? 0.f : m_used;
+      const float sl2 = p.scale_log2;
+      // pass 2: P = 2^(s*scale - m), 32 scores at a time; the 16 packed columns
+      // of chunk c land on S columns [16c, 16c+16), already consumed
+      float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t sr[32], pk[16];
+        tmem_ld32(s_tmem + c4 * 32, sr);
+        tmem_ld_wait();
+        if (interior) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float a = fast_exp2(fmaf(__uint_as_float(sr[2 * c]), sl2, -mu));
+            const float bb = fast_exp2(fmaf(__uint_as_float(sr[2 * c + 1]), sl2, -mu));
+            ls0 += a;
+            ls1 += bb;
+            pk[c] = Elem<T>::pack2(a, bb);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int e = 32 * c4 + 2 * c;
+            const float a = (e < nvalid) ? fast_exp2(fmaf(__uint_as_float(sr[2 * c]), sl2, -mu)) : 0.f;
+            const float bb = (e + 1 < nvalid) ? fast_exp2(fmaf(__uint_as_float(sr[2 * c + 1]), sl2, -mu)) : 0.f;
+            ls0 += a;
+            ls1 += bb;
+            pk[c] = Elem<T>::pack2(a, bb);
+          }
+        }
+        tmem_st16(s_tmem + 16 * c4, pk);
+      }
+      l += ls0 + ls1;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    if (ok && nt > 0) ok = mbar_wait(&o_done[t], (nt - 1) & 1);
+    if (!ok) *abort_flag = 1;
+    if (nt > 0) {
       tc_fence_after();
-      const uint32_t o_tmem = taddr + lane_off + t * 128;
       float o[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(o_tmem + c * 32, reinterpret_cast<uint32_t*>(o) + c * 32);
       tmem_ld_wait();
-      if (r < rows_t[t]) {
-        const float l = lsum[t];
-        const float f = (m_used[t] == -INFINITY) ? 0.f : fast_exp2(m_used[t] - m_run[t]);
+      if (row_ok) {
+        const float f = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_run);
         const float inv = (l > 0.f && ok) ? f / (l * f + 1e-6f) : 0.f;
         T* orow = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(row0 + t * BM + r) * p.so_t +
                   static_cast<int64_t>(h) * p.so_h;
@@ -386,13 +371,13 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (p.lse)
           p.lse[static_cast<int64_t>(row0 + t * BM + r) * p.H + h] =
-              (l > 0.f && ok) ? (m_used[t] + __log2f(l)) * kLn2 : -INFINITY;
+              (l > 0.f && ok) ? (m_used + __log2f(l)) * kLn2 : -INFINITY;
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(taddr, 512);
   }
@@ -439,11 +424,12 @@ int prefill_tc_launch(const PrefillArgs& a, cudaStream_t st, bool* handled) {
   p.scale_log2 = a.scale * kLog2e;
   dim3 grid(a.num_q_heads, n_aligned + a.num_seqs + 1);
   if (a.dtype == kBF16) {
-    cudaFuncSetAttribute(prefill_tc_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
-    prefill_tc_kernel<__nv_bfloat16><<<grid, 192, pf::SMEM, st>>>(mq, mk, mv, p);
+    if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(prefill_tc_kernel<__nv_bfloat16>), pf::SMEM))
+      return r;
+    prefill_tc_kernel<__nv_bfloat16><<<grid, 320, pf::SMEM, st>>>(mq, mk, mv, p);
   } else {
-    cudaFuncSetAttribute(prefill_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
-    prefill_tc_kernel<__half><<<grid, 192, pf::SMEM, st>>>(mq, mk, mv, p);
+    if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(prefill_tc_kernel<__half>), pf::SMEM)) return r;
+    prefill_tc_kernel<__half><<<grid, 320, pf::SMEM, st>>>(mq, mk, mv, p);
   }
   *handled = true;
   return 0;

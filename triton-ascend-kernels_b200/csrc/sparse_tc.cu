@@ -417,7 +417,7 @@ static int launch_sparse_tc(const SparseArgs& a, cudaStream_t st) {
   p.head_chunks = (G + 63) / 64;
   p.scale_log2 = a.scale * kLog2e;
   auto kern = sparse_tc_kernel<T, DQK, DV, SHARED>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+  if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::SMEM)) return r;
   dim3 grid(a.num_tokens, a.num_kv_heads * p.head_chunks);
   kern<<<grid, 288, L::SMEM, st>>>(mq, p, a.k, krow, a.v, vrow);
   return 0;
