@@ -65,6 +65,24 @@ def profile_traffic(name):
     return None
 
 
+def capture_graph(fn, device, warm=3):
+    """CUDA graph of one step.  The step is first run on the capture stream so
+    that everything it caches per stream (the decode workspace, for one) exists
+    before capture; replays then launch exactly the step's kernels."""
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream(device).wait_stream(s)
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        out = fn()
+    torch.cuda.synchronize(device)
+    return g, out
+
+
 class Clocks:
     """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
 
@@ -213,8 +231,12 @@ def run_decode_ours(args, rank, world, device):
     def step():
         return PD.paged_attention_decode(qd, kc, vc, btd, ctxd, DEC["page"], DEC["page"])
 
+    run, graph = step, None
+    if not args.no_graph:
+        graph, out = capture_graph(step, device)
+        run = graph.replay
     for _ in range(args.warmup):
-        step()
+        run()
     torch.cuda.synchronize(device)
     # launches per step: main kernel (+ split-KV combine when there are splits)
     L = T.lib()
@@ -229,7 +251,10 @@ def run_decode_ours(args, rank, world, device):
     with Clocks(device.index) as clk:
         ev0.record(stream)
         for _ in range(args.steps):
-            out = step()
+            if graph is None:
+                out = step()
+            else:
+                run()
         ev1.record(stream)
         torch.cuda.synchronize(device)
     ms = ev0.elapsed_time(ev1) / args.steps
@@ -290,7 +315,7 @@ def run_decode_ours(args, rank, world, device):
     gbs = nbytes_all / (ms * 1e-3) / 1e9
     per_launch_gbs = nbytes / (ms * 1e-3) / 1e9
     hbm = pk["hbm_gbs"]
-    traffic = profile_traffic("paged_decode_cfg2.md")
+    traffic = profile_traffic("paged_decode_tc_kernel.md")
     res = {
         "metric": METRIC,
         "value": round(gbs, 1),
@@ -315,7 +340,9 @@ def run_decode_ours(args, rank, world, device):
         "roofline": {"bound": "hbm", "achieved": round(per_launch_gbs, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(per_launch_gbs / hbm, 4), "traffic": traffic,
                      "peak_source": f"{pk_kind} hbm_gbs", "algorithmic_bytes_per_launch": nbytes,
-                     "timed": "paged_decode_tc_kernel + split-KV combine per step, CUDA events"},
+                     "timed": "paged_decode_tc_kernel + split-KV combine per step, CUDA events"
+                              + ("; each step a CUDA-graph replay of paged_attention_decode()" if graph is not None
+                                 else "")},
         "e2e": {"value": round(nbytes_all / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "note": "public paged_attention_decode() with q / block tables / context lengths copied from "
@@ -391,8 +418,26 @@ def run_decode_reference(args):
 
 class Workload:
     """One hot-path workload: device-resident step, end-to-end step through the
-    public API with host buffers, algorithmic work per step, CPU baseline."""
+    public API with host buffers, algorithmic work per step, and a bounded
+    sample of it on host inputs through the numpy oracle (CPU baseline and the
+    reference arm)."""
     name = unit = bound = peak_key = kernel = desc = ""
+
+    def reference_sample(self):
+        """(step, work per step, text): one bounded oracle step on host inputs."""
+        raise NotImplementedError
+
+    def scale(self):
+        return 1e12 if self.unit == "TFLOP/s" else 1e9
+
+    def cpu_baseline(self, seconds, threads):
+        step, work, text = self.reference_sample()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds or n == 0:
+            step()
+            n += 1
+        dt = time.perf_counter() - t0
+        return n * work / dt / self.scale(), f"{n} x {text}, {dt:.1f} s, {threads} BLAS threads"
 
     def timed(self, fn, steps, warmup, device):
         for _ in range(warmup):
@@ -456,21 +501,15 @@ class PrefillWL(Workload):
         o = self.FP.flash_attention_prefill(self.dq, self.dk, self.dv, self.dcu, True)
         self.hout.copy_(o, non_blocking=True)
 
-    def cpu_baseline(self, seconds, threads):
+    def reference_sample(self):
         from oracle import attention_oracle as O
         L = 1024
         g = np.random.default_rng(1)
         q = g.standard_normal((L, 64, 128), dtype=np.float32)
         k = g.standard_normal((L, 8, 128), dtype=np.float32)
         v = g.standard_normal((L, 8, 128), dtype=np.float32)
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds or n == 0:
-            O.prefill(q, k, v, [0, L], True, acc=np.float32)
-            n += 1
-        dt = time.perf_counter() - t0
-        flop = n * 4.0 * 128 * 64 * L * (L + 1) / 2
-        return flop / dt / 1e12, f"{n} causal 1024-token sequences (64/8 heads, d 128) through the numpy oracle, " \
-                                 f"fp32, {dt:.1f} s, BLAS threads {threads}"
+        return (lambda: O.prefill(q, k, v, [0, L], True, acc=np.float32), 4.0 * 128 * 64 * L * (L + 1) / 2,
+                "one causal 1024-token sequence (64/8 heads, d 128) through the numpy oracle, fp32")
 
 
 class SparseWL(Workload):
@@ -521,24 +560,22 @@ class SparseWL(Workload):
         o = self.SA.sparse_attn_prefill(self.dq, self.dkv, self.dkv[..., :512], self.didx, self.cu, self.sink)
         self.hout.copy_(o, non_blocking=True)
 
-    def cpu_baseline(self, seconds, threads):
+    def reference_sample(self):
         from oracle import attention_oracle as O
-        n_tok = 4
-        q = self.q[:n_tok].float().cpu().numpy()
-        kv = self.kv[:32768].float().cpu().numpy()
-        idx = self.idx[:n_tok].cpu().numpy()
-        sink = self.sink.cpu().numpy()
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds or n == 0:
-            O.sparse_prefill(q, kv, kv[..., :512], idx, None, sink, acc=np.float32)
-            n += 1
-        dt = time.perf_counter() - t0
-        return n * n_tok * 2.0 * 64 * 1088 * 2048 / dt / 1e12, \
-            f"{n}x{n_tok} query tokens (64 heads, 2048 indices, 576/512) through the numpy oracle, fp32, {dt:.1f} s"
+        n_tok, KVL, K = 4, 32768, 2048
+        g = np.random.default_rng(2)
+        q = g.standard_normal((n_tok, 64, 576), dtype=np.float32)
+        kv = g.standard_normal((KVL, 1, 576), dtype=np.float32)
+        idx = np.stack([np.sort(g.choice(KVL - n_tok + i + 1, K, replace=False)) for i in range(n_tok)]).astype(np.int32)
+        sink = g.standard_normal(64).astype(np.float32)
+        return (lambda: O.sparse_prefill(q, kv, kv[..., :512], idx, None, sink, acc=np.float32),
+                n_tok * 2.0 * 64 * 1088 * K,
+                f"{n_tok} query tokens (64 heads, 2048 causal indices into a 32768-row latent, 576/512) "
+                "through the numpy oracle, fp32")
 
 
 class CompressWL(Workload):
-    name, unit, bound, peak_key, kernel = "compress", "GB/s", "hbm", "hbm_gbs", "compress_kernels"
+    name, unit, bound, peak_key, kernel = "compress", "GB/s", "hbm", "hbm_gbs", "compress_csa_hca_kernel"
     desc = ("CSA + HCA KV compression: 65536 tokens (16 sequences x 4096) x 512 dims bf16 K and V plus per-token "
             "fp32 gate logits; CSA stride 4 (8-token windows, as the reference's csa.py) and HCA 128-token "
             "windows, gate-softmax-weighted sums")
@@ -580,11 +617,11 @@ class CompressWL(Workload):
         self.args = (TK.ptr(self.k), TK.strides(self.k), TK.ptr(self.v), TK.strides(self.v), TK.ptr(self.gate), 1,
                      TK.ptr(self.cu_d), 16, T, TK.ptr(co), nc, TK.ptr(ck), TK.strides(ck), TK.ptr(cv),
                      TK.strides(cv), TK.ptr(ho), nh, TK.ptr(hk), TK.strides(hk), TK.ptr(hv), TK.strides(hv), 1, 512,
-                     512, 4, 128, 1, TK.stream_of(self.k))
+                     512, 4, 128, 1)
         self.fn = TK.lib().tak_compress_kv_csa_hca
 
     def step(self):
-        self.TK.check(self.fn(*self.args))
+        self.TK.check(self.fn(*self.args, self.TK.stream_of(self.k)))
         return self.outs[0][2]
 
     def e2e_setup(self):
@@ -603,24 +640,50 @@ class CompressWL(Workload):
         for h, d in zip(self.hout, (ck, cv, hk, hv)):
             h.copy_(d, non_blocking=True)
 
-    def cpu_baseline(self, seconds, threads):
+    def reference_sample(self):
         from oracle import attention_oracle as O
         T = 4096
-        k = self.k[:T].float().cpu().numpy()
-        v = self.v[:T].float().cpu().numpy()
-        g = self.gate[:T].cpu().numpy()
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds or n == 0:
-            O.compress_kv(k, v, [0, T], 4, 8, g, acc=np.float32)
-            O.compress_kv(k, v, [0, T], 128, 128, g, acc=np.float32)
-            n += 1
-        dt = time.perf_counter() - t0
-        b = n * (2 * T * 512 * 2 + T * 4 + 2 * (T // 4) * 512 * 2 + 2 * (T // 128) * 512 * 2)
-        return b / dt / 1e9, f"{n} x one 4096-token sequence, CSA + HCA gated, numpy oracle, fp32, {dt:.1f} s"
+        g = np.random.default_rng(3)
+        k = g.standard_normal((T, 1, 512), dtype=np.float32)
+        v = g.standard_normal((T, 1, 512), dtype=np.float32)
+        gate = g.standard_normal(T).astype(np.float32)
+
+        def one():
+            O.compress_kv(k, v, [0, T], 4, 8, gate, acc=np.float32)
+            O.compress_kv(k, v, [0, T], 128, 128, gate, acc=np.float32)
+
+        return (one, 2 * T * 512 * 2 + T * 4 + 2 * (T // 4) * 512 * 2 + 2 * (T // 128) * 512 * 2,
+                "one 4096-token sequence, CSA + HCA gated, through the numpy oracle, fp32")
 
 
 WORKLOADS = {"prefill": PrefillWL, "sparse": SparseWL, "compress": CompressWL}
 SMALL = False  # --small: a reduced instance of the workload (for ncu captures)
+
+
+def run_workload_reference(args, W):
+    """The reference math on the host CPU: the workload's bounded oracle step,
+    timed over --steps after --warmup, on all host threads."""
+    from threadpoolctl import threadpool_limits
+    w = W()
+    threads = os.cpu_count() or 1
+    step, work, text = w.reference_sample()
+    with threadpool_limits(limits=threads):
+        for _ in range(args.warmup):
+            step()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        dt = (time.perf_counter() - t0) / args.steps
+    v = work / dt / w.scale()
+    return {
+        "impl": "reference", "metric": METRIC, "workload": w.name, "value": round(v, 4), "unit": w.unit,
+        "n_gpus": 0, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w.desc, "sample_per_step": text, "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(v, 4), "unit": w.unit, "cores": threads, "kind": "port",
+                         "sample": f"{text}, one per step, {threads} BLAS threads"},
+        "e2e": {"value": round(v, 4), "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
 
 
 def run_workload_ours(args, rank, world, device, W):
@@ -629,8 +692,13 @@ def run_workload_ours(args, rank, world, device, W):
     w.setup(rank, device)
     if world > 1:
         torch.distributed.barrier()
+    step_fn = w.step
+    graph = None
+    if not args.no_graph:
+        graph, _ = capture_graph(w.step, device)
+        step_fn = graph.replay
     with Clocks(device.index) as clk:
-        ms = w.timed(w.step, args.steps, args.warmup, device)
+        ms = w.timed(step_fn, args.steps, args.warmup, device)
     if args.no_e2e:
         h2d = d2h = 0
         e2e_ms = float("nan")
@@ -673,8 +741,9 @@ def run_workload_ours(args, rank, world, device, W):
         "config": dict({"workload": w.desc, "parallelism": f"sequence sharding x{world} (weak scaling)"}, **w.config),
         "roofline": {"bound": w.bound, "achieved": round(per_gpu, 1), "peak": peak, "unit": w.unit,
                      "frac": round(per_gpu / peak, 4), "traffic": profile_traffic(f"{w.kernel}.md"),
-                     "peak_source": f"{pk_kind} {w.peak_key}", "algorithmic_work_per_step": w.work,
-                     "timed": f"{w.kernel} per step (public API, device-resident inputs), CUDA events"},
+                     "peak_source": f"{pk_kind} {w.peak_key} (burst)", "algorithmic_work_per_step": w.work,
+                     "timed": f"{w.kernel} per step (public API, device-resident inputs), CUDA events"
+                 + ("; each step a CUDA-graph replay of the call" if graph is not None else "")},
         "e2e": {"value": round(work_all / (e2e_ms * 1e-3) / scale, 1), "unit": w.unit, "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps * w.launches,
@@ -684,6 +753,12 @@ def run_workload_ours(args, rank, world, device, W):
         res["e2e"] = None
     if gather_ms is not None:
         res["config"]["output_gather_to_rank0_ms"] = round(gather_ms, 3)
+    sus = pk.get(w.peak_key + "_sustained")
+    if sus:
+        # the timed loop runs for seconds at the power cap: the sustained GEMM
+        # figure of the same file is the matching denominator
+        res["roofline"]["peak_sustained"] = sus
+        res["roofline"]["frac_of_sustained"] = round(per_gpu / sus, 4)
     if not args.no_cpu_baseline:
         from threadpoolctl import threadpool_limits
         threads = os.cpu_count() or 1
@@ -705,6 +780,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (profiling)")
     ap.add_argument("--small", action="store_true", help="reduced workload instance (profiling captures)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch each device-timed step eagerly instead of replaying a CUDA graph of it")
     args = ap.parse_args()
     global SMALL
     SMALL = args.small
@@ -719,9 +796,7 @@ def main():
             if args.workload == "decode":
                 print(json.dumps(run_decode_reference(args)), flush=True)
             else:
-                print(json.dumps({"impl": "reference", "workload": args.workload,
-                                  "unavailable": "reference arm implemented for the headline decode workload; "
-                                                 "this workload reports its CPU oracle as cpu_baseline"}), flush=True)
+                print(json.dumps(run_workload_reference(args, WORKLOADS[args.workload])), flush=True)
         return
 
     device = torch.device("cuda", local)

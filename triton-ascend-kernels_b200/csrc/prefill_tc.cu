@@ -18,10 +18,9 @@
 //   warp 8      TMA producer: both Q tiles once, then K and V blocks of 128
 //               rows into 2-stage rings (128-byte swizzle, 64-column boxes).
 //   warp 9      TMEM allocator + single-thread tcgen05.mma issuer.  Per K/V
-//               block j: PV_A(j), PV_B(j) (TS-MMA: P read from TMEM, V from
-//               smem, MN-major), then S_A(j+1) = Q_A K^T, S_B(j+1) = Q_B K^T
-//               (SS-MMA, M=N=128).  Each tile's S is rewritten only after
-//               that tile's PV of the previous block has completed.
+//               block j and tile t: PV_t(j) (TS-MMA: P read from TMEM, V from
+//               smem, MN-major), then S_t(j+1) = Q_t K^T (SS-MMA, M=N=128)
+//               once PV_t(j) has completed (S_t and P_t share TMEM columns).
 //   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B (thread = row =
 //               TMEM lane): load S, mask only on boundary blocks, online max
 //               with lazy rescaling (O and l rescaled only when the max grows
@@ -225,30 +224,36 @@ __global__ void __launch_bounds__(320, 1)
           ok = false;
           break;
         }
+        // Per tile: P.V of block j, then (once that P.V has read P) S of block
+        // j + 1, so a tile's next softmax can start while the other tile's
+        // softmax is still running.
         const int st = j & 1;
         if (!(ok = mbar_wait(&v_full[st], (j >> 1) & 1))) break;
+        const bool next = j + 1 < n_kv;
+        bool k_next = false;  // K block j + 1 waited for
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (j < n_t[t]) {
             if (!(ok = mbar_wait(&p_full[t], j & 1))) break;
             tc_fence_after();
             pv(t, j);
-          }
-        }
-        if (!ok) break;
-        tc_commit(&v_empty[st]);
-        if (j + 1 < n_kv) {
-          if (!(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) break;
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
+            if (t == 1 || j >= n_t[1]) tc_commit(&v_empty[st]);
             if (j + 1 < n_t[t]) {
+              if (!k_next && !(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) break;
+              k_next = true;
               // this tile's S/P columns are rewritten only after its PV of block j has read P
               if (!(ok = mbar_wait(&o_done[t], j & 1))) break;
               tc_fence_after();
               qk(t, j + 1);
             }
           }
-          if (!ok) break;
+        }
+        if (!ok) break;
+        if (next) {
+          // every tile with block j + 1 has issued its S MMA; the commit frees the K stage
+          // (a tile without block j + 1 issues none, and then k_full of block j + 1 may
+          // not have been waited for: wait here so the stage's phases stay in step)
+          if (!k_next && !(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) break;
           tc_commit(&k_empty[(j + 1) & 1]);
         }
       }
