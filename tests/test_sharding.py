@@ -102,6 +102,30 @@ def _decode_worker(rank, world, port, q_path):
         dist.destroy_process_group()
 
 
+def _gather_forms_worker(rank, world, port, q_path):
+    _init(rank, world, port)
+    try:
+        rows = [3, 5][rank]
+        row0 = [0, 3][rank]
+        local = torch.arange(row0, row0 + rows, dtype=torch.float32)[:, None] * torch.ones(1, 4)
+        a = S.gather_rows(local, row0, 8)                                    # contiguous offsets
+        b = S.gather_rows(local, torch.arange(row0, row0 + rows), 8, dst=1)  # index tensors, to rank 1
+        c = S.gather_rows(local, row0 if rank == 0 else torch.arange(row0, row0 + rows), 8)  # mixed
+        if rank == 1:
+            torch.save({"a": a, "b": b, "c": c}, q_path)
+        else:
+            assert b is None
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gather_forms(tmp_path):
+    res = _run(_gather_forms_worker, 2, tmp_path)
+    want = torch.arange(8, dtype=torch.float32)[:, None] * torch.ones(1, 4)
+    for key in "abc":
+        assert torch.equal(res[key], want), key
+
+
 def _run(worker, world, tmp_path):
     path = str(tmp_path / "result.pt")
     mp.spawn(worker, args=(world, _free_port(), path), nprocs=world, join=True)

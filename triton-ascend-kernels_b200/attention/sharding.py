@@ -81,36 +81,55 @@ def shard_requests(context_lens, world, rank):
 
 
 def gather_rows(local, index, total_rows, group=None, dst=None):
-    """Gather variable-sized row blocks: rank r holds rows `index` (global row
-    numbers, int64) of a [total_rows, ...] result.  With dst=None every rank
+    """Gather variable-sized row blocks: rank r holds rows `index` of a
+    [total_rows, ...] result -- an int64 tensor of global row numbers, or an
+    int for a contiguous block starting at that row.  With dst=None every rank
     returns the whole result (all-gather); with dst=k only rank k does and the
     others return None (gather, for results too large to replicate).  Blocks
-    are padded to the largest rank's row count for the collective."""
+    are padded to the largest rank's row count for the collective; contiguous
+    blocks are placed with one slice copy, others by index."""
     world = dist.get_world_size(group)
     me = dist.get_rank(group)
     dev = local.device
-    n = torch.tensor([local.shape[0]], dtype=torch.int64, device=dev)
-    counts = [torch.empty_like(n) for _ in range(world)]
-    dist.all_gather(counts, n, group=group)
-    counts = [int(c) for c in counts]
+    contiguous = not isinstance(index, torch.Tensor)
+    n = torch.tensor([local.shape[0], int(index) if contiguous else -1], dtype=torch.int64, device=dev)
+    heads = [torch.empty_like(n) for _ in range(world)]
+    dist.all_gather(heads, n, group=group)
+    heads = [(int(h[0]), int(h[1])) for h in heads]
+    counts = [c for c, _ in heads]
     mx = max(counts) if counts else 0
-    pad = local.new_zeros((mx,) + tuple(local.shape[1:]))
-    pad[: local.shape[0]] = local
-    ipad = torch.full((mx,), -1, dtype=torch.int64, device=dev)
-    ipad[: local.shape[0]] = index.to(dev)
+    if local.shape[0] == mx:
+        pad = local.contiguous()
+    else:
+        pad = local.new_zeros((mx,) + tuple(local.shape[1:]))
+        pad[: local.shape[0]] = local
     receive = dst is None or me == dst
     blocks = [torch.empty_like(pad) for _ in range(world)] if receive else None
-    idxs = [torch.empty_like(ipad) for _ in range(world)] if receive else None
     if dst is None:
         dist.all_gather(blocks, pad, group=group)
-        dist.all_gather(idxs, ipad, group=group)
     else:
         dist.gather(pad, blocks, dst=dst, group=group)
-        dist.gather(ipad, idxs, dst=dst, group=group)
+    idxs = None
+    if not all(r0 >= 0 for _, r0 in heads):
+        # some rank sent an index tensor: exchange the row numbers too
+        ipad = torch.full((mx,), -1, dtype=torch.int64, device=dev)
+        if contiguous:
+            ipad[: local.shape[0]] = torch.arange(int(index), int(index) + local.shape[0], device=dev)
+        else:
+            ipad[: local.shape[0]] = index.to(dev)
+        idxs = [torch.empty_like(ipad) for _ in range(world)] if receive else None
+        if dst is None:
+            dist.all_gather(idxs, ipad, group=group)
+        else:
+            dist.gather(ipad, idxs, dst=dst, group=group)
     if not receive:
         return None
     full = local.new_zeros((total_rows,) + tuple(local.shape[1:]))
-    for blk, ix, c in zip(blocks, idxs, counts):
-        if c:
-            full[ix[:c]] = blk[:c]
+    for r, (blk, (c, r0)) in enumerate(zip(blocks, heads)):
+        if not c:
+            continue
+        if idxs is None:
+            full[r0:r0 + c] = blk[:c]
+        else:
+            full[idxs[r][:c]] = blk[:c]
     return full
