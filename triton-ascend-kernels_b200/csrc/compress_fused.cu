@@ -66,22 +66,6 @@ struct FusedCompressParams {
   void* hca_v; int64_t shv[3];
 };
 
-// last sequence s with offs[s] <= slot (skipping empty sequences)
-__device__ __forceinline__ static int fc_find_seq(const int32_t* offs, int num_seqs, int64_t slot) {
-  int lo = 0, hi = num_seqs - 1, ans = 0;
-  while (lo <= hi) {
-    const int mid = (lo + hi) >> 1;
-    if (offs[mid] <= slot) {
-      ans = mid;
-      lo = mid + 1;
-    } else {
-      hi = mid - 1;
-    }
-  }
-  while (ans + 1 < num_seqs && offs[ans + 1] <= slot) ++ans;
-  return ans;
-}
-
 // Position in a CTA's run of units: unit = (chunk c, head, slice), chunk c =
 // chunk i of sequence s.  Advanced incrementally (one binary search per CTA).
 struct FcCursor {
@@ -89,13 +73,35 @@ struct FcCursor {
   int s, i, head, slice;
 };
 
+// Last sequence s with offs[s] <= slot, searched by a whole warp 32 ways at a
+// time (one coalesced probe and a ballot per level: one global round trip for
+// up to 32 sequences, instead of a chain of dependent loads).  All 32 lanes
+// must call it; every lane gets the result.
+__device__ __forceinline__ static int fc_find_seq_warp(const int32_t* offs, int num_seqs, int64_t slot) {
+  const int lane = threadIdx.x & 31;
+  int lo = 0, hi = num_seqs;  // answer in [lo, hi)
+  while (hi - lo > 32) {
+    const int step = (hi - lo + 31) / 32;
+    const int idx = lo + lane * step;
+    const bool le = idx < hi && offs[idx] <= slot;
+    const unsigned m = __ballot_sync(0xffffffffu, le);
+    const int last = m ? 31 - __clz(m) : 0;
+    lo = lo + last * step;
+    hi = min(lo + step, hi);
+  }
+  const int idx = lo + lane;
+  const bool le = idx < hi && offs[idx] <= slot;
+  const unsigned m = __ballot_sync(0xffffffffu, le);
+  return lo + (m ? 31 - __clz(m) : 0);
+}
+
 __device__ __forceinline__ static void fc_cursor_init(FcCursor& q, const FusedCompressParams& p, int64_t u) {
   const int64_t per = static_cast<int64_t>(p.heads) * p.slices;
   q.c = u / per;
   const int rem = static_cast<int>(u - q.c * per);
   q.head = rem / p.slices;
   q.slice = rem - q.head * p.slices;
-  q.s = fc_find_seq(p.hca_offsets, p.num_seqs, q.c);
+  q.s = fc_find_seq_warp(p.hca_offsets, p.num_seqs, q.c);
   q.i = static_cast<int>(q.c - p.hca_offsets[q.s]);
 }
 

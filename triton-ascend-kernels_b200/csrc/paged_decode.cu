@@ -27,6 +27,8 @@
 // Generic path (any dtype incl. fp32, any strides / block size / head dim):
 //   one CTA of 4 warps per (sequence, query head); each warp walks a strided
 //   subset of the keys (lanes split the head dim), then the warps merge.
+#include <cstdio>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -51,8 +53,10 @@ struct DecodeParams {
 // ---------------------------------------------------------------------------
 // fast path
 // ---------------------------------------------------------------------------
+// Two CTAs per SM for head dims up to 128; a 256-dim ring (192 KB of shared
+// memory) fits one CTA per SM, which may then use the full register file.
 template <typename T, int D, int CH, int NS>
-__global__ void __launch_bounds__(160, 2)
+__global__ void __launch_bounds__(160, D >= 256 ? 1 : 2)
     paged_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            const DecodeParams p) {
   constexpr int NREG = D / 64;        // 64-element (128-byte) column blocks per row
@@ -66,6 +70,10 @@ __global__ void __launch_bounds__(160, 2)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   uint64_t* empty = full + NS;
 
+  // let the split-KV combine grid (launched with programmatic stream
+  // serialization) be scheduled as this grid's last wave runs; it still waits
+  // for this whole grid to complete before reading any partial
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / p.head_chunks;
   const int hc = blockIdx.y % p.head_chunks;
@@ -290,13 +298,17 @@ __global__ void __launch_bounds__(160, 2)
 }
 
 // Merge the split partials of one (sequence, KV head, head chunk): weights of
-// every split first (shared memory), then one output element per thread and
-// iteration with all splits' loads independent (no serial latency chain).
+// every split first (shared memory), then each thread merges 4 consecutive
+// output elements of one head with all splits' 16-byte loads independent
+// (one memory round trip, not a chain).  When launched with programmatic
+// stream serialization the grid may start while the partial-writing grid is
+// still running; griddepcontrol.wait holds it until that grid has completed.
 template <typename T>
 __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeParams p) {
   __shared__ float wts[16 * 64];
   __shared__ float lsum[16 * 64];
   __shared__ float inv_l[16];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int kvh = blockIdx.y / p.head_chunks, hc = blockIdx.y % p.head_chunks, seq = blockIdx.x;
   const int ctx = min(p.context_lens[seq], p.max_ctx);
   const int split_tokens = p.pages_per_split * p.block_size;
@@ -328,21 +340,41 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeP
     if (p.lse) p.lse[seq * p.H + h0 + tid] = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
   }
   __syncthreads();
-  for (int i = tid; i < gcnt * p.D; i += 128) {
-    const int r = i / p.D, d = i % p.D;
-    const float* src = p.ws_o + ((static_cast<int64_t>(seq) * p.H + h0 + r) * p.max_splits) * p.D + d;
+  const int nvec = p.D / 4;
+  for (int i = tid; i < gcnt * nvec; i += 128) {
+    const int r = i / nvec, d = (i - r * nvec) * 4;
+    const float4* src =
+        reinterpret_cast<const float4*>(p.ws_o + ((static_cast<int64_t>(seq) * p.H + h0 + r) * p.max_splits) * p.D + d);
     const float* w = wts + r * n;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
     int j = 0;
-    for (; j + 4 <= n; j += 4) {
-      a0 += w[j] * src[(j + 0) * p.D];
-      a1 += w[j + 1] * src[(j + 1) * p.D];
-      a2 += w[j + 2] * src[(j + 2) * p.D];
-      a3 += w[j + 3] * src[(j + 3) * p.D];
+    for (; j + 8 <= n; j += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = src[static_cast<int64_t>(j + u) * nvec];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float wu = w[j + u];
+        a.x = fmaf(wu, v[u].x, a.x);
+        a.y = fmaf(wu, v[u].y, a.y);
+        a.z = fmaf(wu, v[u].z, a.z);
+        a.w = fmaf(wu, v[u].w, a.w);
+      }
     }
-    for (; j < n; ++j) a0 += w[j] * src[j * p.D];
-    reinterpret_cast<T*>(p.out)[seq * p.so_s + (h0 + r) * p.so_h + d * p.so_d] =
-        Elem<T>::from_f((a0 + a1 + a2 + a3) * inv_l[r]);
+    for (; j < n; ++j) {
+      const float4 v = src[static_cast<int64_t>(j) * nvec];
+      const float wu = w[j];
+      a.x = fmaf(wu, v.x, a.x);
+      a.y = fmaf(wu, v.y, a.y);
+      a.z = fmaf(wu, v.z, a.z);
+      a.w = fmaf(wu, v.w, a.w);
+    }
+    const float il = inv_l[r];
+    T* o = reinterpret_cast<T*>(p.out) + seq * p.so_s + (h0 + r) * p.so_h + d * p.so_d;
+    o[0] = Elem<T>::from_f(a.x * il);
+    o[p.so_d] = Elem<T>::from_f(a.y * il);
+    o[2 * p.so_d] = Elem<T>::from_f(a.z * il);
+    o[3 * p.so_d] = Elem<T>::from_f(a.w * il);
   }
 }
 
@@ -520,7 +552,26 @@ static int launch_fast(const PagedDecodeArgs& a, int pps, int max_splits, int he
   if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), SMEM)) return r;
   dim3 grid(max_splits, a.num_kv_heads * head_chunks, a.num_seqs);
   kern<<<grid, 160, SMEM, st>>>(mk, mv, p);
-  if (max_splits > 1) paged_decode_combine_kernel<T><<<dim3(a.num_seqs, a.num_kv_heads * head_chunks), 128, 0, st>>>(p);
+  if (max_splits > 1) {
+    // programmatic dependent launch: the combine grid may be scheduled during
+    // the main grid's last wave (it waits for the main grid in-kernel)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.num_seqs, a.num_kv_heads * head_chunks);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, paged_decode_combine_kernel<T>, p);
+    if (e != cudaSuccess) {
+      char buf[160];
+      std::snprintf(buf, sizeof(buf), "paged decode: combine launch failed: %s", cudaGetErrorString(e));
+      return set_error(3, buf);
+    }
+  }
   return 0;
 }
 
