@@ -656,7 +656,88 @@ class CompressWL(Workload):
                 "one 4096-token sequence, CSA + HCA gated, through the numpy oracle, fp32")
 
 
-WORKLOADS = {"prefill": PrefillWL, "sparse": SparseWL, "compress": CompressWL}
+class CsaWL(Workload):
+    name, unit, bound, peak_key, kernel = "csa", "TFLOP/s", "tensor", "bf16_tflops", "sparse_tc_kernel"
+    desc = ("CSA prefill forward over the compressed latent: 65536 tokens (16 sequences x 4096), 64 query heads on "
+            "one 512-dim latent used as K and V, bf16; gated CSA compression (m = 4, 8-token windows), "
+            "Lightning-indexer top-512 compressed slots + 128-token window per query, sparse attention with sinks")
+    graphable = False  # the reference-compatible wrapper sizes outputs from host-side offsets each call
+
+    def setup(self, rank, device):
+        import csa as CSA
+        self.CSA = CSA
+        S, QT = (2 if SMALL else 16), 4096
+        T = S * QT
+        gd = torch.Generator(device=device).manual_seed(61 + rank)
+        self.q = torch.empty(T, 64, 512, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.kv = torch.empty(T, 1, 512, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.gate = torch.empty(T, device=device).normal_(generator=gd)
+        self.sink = torch.empty(64, device=device).normal_(generator=gd)
+        self.cu_h = torch.arange(0, T + 1, QT, dtype=torch.int32)
+        self.n_win, self.top_k, self.m = 128, 512, 4
+        # attention work = every non-negative index (the reference also attends
+        # the non-causal picks of a row that has fewer than top_k causal slots)
+        ck, cv, offs = CSA.compress_kv_overlap(self.kv, self.kv, self.cu_h, self.m, gate=self.gate)
+        idx = CSA.build_csa_topk_idxs(self.q, ck, self.cu_h, offs, self.n_win, self.top_k, self.m)
+        n_idx = int((idx >= 0).sum())
+        self.work = 2.0 * 64 * (512 + 512) * n_idx
+        self.launches = 5
+        self.config = {"tokens": T, "indices_per_query": self.n_win + self.top_k, "valid_indices": n_idx,
+                       "l2_policy": "q (4.3 GB) and outputs stream; the 1.3 MB latent per sequence is L2-resident",
+                       "timed_path": "csa_prefill_forward(): compression, window rows, Lightning indexer, "
+                                     "concatenation and sparse attention, every step"}
+
+    def step(self):
+        return self.CSA.csa_prefill_forward(self.q, self.kv, self.kv, self.cu_h, self.n_win, self.top_k, self.m,
+                                            self.sink, gate=self.gate)
+
+    def phases(self, device):
+        """Device time of each stage of one forward (ms), eager."""
+        CSA = self.CSA
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        torch.cuda.synchronize(device)
+        ev[0].record()
+        ck, cv, offs = CSA.compress_kv_overlap(self.kv, self.kv, self.cu_h, self.m, gate=self.gate)
+        ev[1].record()
+        idx = CSA.build_csa_topk_idxs(self.q, ck, self.cu_h, offs, self.n_win, self.top_k, self.m)
+        ev[2].record()
+        kf = torch.cat([self.kv, ck], 0)
+        CSA.sparse_attn_prefill(self.q, kf, kf, idx, self.cu_h.to(device), attn_sink=self.sink)
+        ev[3].record()
+        torch.cuda.synchronize(device)
+        return {"compress_ms": round(ev[0].elapsed_time(ev[1]), 3), "index_ms": round(ev[1].elapsed_time(ev[2]), 3),
+                "concat_attention_ms": round(ev[2].elapsed_time(ev[3]), 3)}
+
+    def e2e_setup(self):
+        self.hq, self.hkv, self.hg = (t.cpu().pin_memory() for t in (self.q, self.kv, self.gate))
+        self.hout = torch.empty(self.q.shape, dtype=torch.bfloat16).pin_memory()
+        self.dq, self.dkv, self.dg = (torch.empty_like(t) for t in (self.q, self.kv, self.gate))
+        return (sum(t.numel() * t.element_size() for t in (self.hq, self.hkv, self.hg)),
+                self.hout.numel() * self.hout.element_size())
+
+    def e2e_step(self):
+        for d, h in ((self.dq, self.hq), (self.dkv, self.hkv), (self.dg, self.hg)):
+            d.copy_(h, non_blocking=True)
+        o = self.CSA.csa_prefill_forward(self.dq, self.dkv, self.dkv, self.cu_h, self.n_win, self.top_k, self.m,
+                                         self.sink, gate=self.dg)
+        self.hout.copy_(o, non_blocking=True)
+
+    def reference_sample(self):
+        from oracle import attention_oracle as O
+        L = 512
+        g = np.random.default_rng(4)
+        q = g.standard_normal((L, 64, 512), dtype=np.float32)
+        kv = g.standard_normal((L, 1, 512), dtype=np.float32)
+        sink = g.standard_normal(64).astype(np.float32)
+        idx = O.build_csa_topk_idxs(q, O.compress_kv(kv, kv, [0, L], 4, 8)[0], [0, L],
+                                    O.comp_offsets_for([L], 4), 128, 512, 4)
+        work = 2.0 * 64 * 1024 * int((idx >= 0).sum())
+        return (lambda: O.csa_prefill_forward(q, kv, kv, [0, L], 128, 512, 4, sink),
+                work, "one 512-token sequence through the numpy oracle's csa_prefill_forward (64 heads, 512-dim "
+                      "latent, window 128 + top-512), fp32")
+
+
+WORKLOADS = {"prefill": PrefillWL, "sparse": SparseWL, "compress": CompressWL, "csa": CsaWL}
 SMALL = False  # --small: a reduced instance of the workload (for ncu captures)
 
 
@@ -694,7 +775,7 @@ def run_workload_ours(args, rank, world, device, W):
         torch.distributed.barrier()
     step_fn = w.step
     graph = None
-    if not args.no_graph:
+    if not args.no_graph and getattr(w, "graphable", True):
         graph, _ = capture_graph(w.step, device)
         step_fn = graph.replay
     with Clocks(device.index) as clk:
@@ -753,6 +834,8 @@ def run_workload_ours(args, rank, world, device, W):
         res["e2e"] = None
     if gather_ms is not None:
         res["config"]["output_gather_to_rank0_ms"] = round(gather_ms, 3)
+    if hasattr(w, "phases"):
+        res["config"]["phases"] = w.phases(device)
     sus = pk.get(w.peak_key + "_sustained")
     if sus:
         # the timed loop runs for seconds at the power cap: the sustained GEMM

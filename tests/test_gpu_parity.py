@@ -451,21 +451,44 @@ def test_index_builders_bit_exact():
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_csa_indexer_bit_exact(dtype):
-    """Lightning indexer on 4 sequences, 512-dim compressed keys; ties and
-    fewer-than-k causal slots included (short sequences)."""
-    lens = [3, 40, 200, 513]
+@pytest.mark.parametrize("top_k", [16, 48, 300])
+def test_csa_indexer_bit_exact(dtype, top_k):
+    """Lightning indexer on 5 sequences, 512-dim compressed keys; ties and
+    fewer-than-k causal slots included (short sequences).  top_k 16 takes the
+    repeated-argmax selection, 48 and 300 the sorted one (up to 525 slots)."""
+    lens = [3, 40, 200, 513, 2100]
     Tn = sum(lens)
     g = torch.Generator().manual_seed(41)
     q = torch.randn(Tn, 4, 512, generator=g).to(DEV, dtype)
     k = torch.randn(Tn, 1, 512, generator=g).to(DEV, dtype)
     cuq = _cu_t(lens)
     ck, cv, offs = CSA.compress_kv_overlap(k, k, cuq, 4)
-    got = CSA.build_csa_topk_idxs(q, ck, cuq, offs, 8, 16, 4)
+    got = CSA.build_csa_topk_idxs(q, ck, cuq, offs, 8, top_k, 4)
     name = "bfloat16" if dtype == torch.bfloat16 else "float16"
-    ref = O.build_csa_topk_idxs(npy(q), npy(ck), cuq.cpu(), offs.cpu(), 8, 16, 4, name)
+    ref = O.build_csa_topk_idxs(npy(q), npy(ck), cuq.cpu(), offs.cpu(), 8, top_k, 4, name)
     assert_topk_match(got.cpu().numpy(), ref, npy(q), npy(ck), lambda t: Tn, 8,
                       2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_csa_hca_forward_latent512(dtype):
+    """MLA-style: one 512-dim latent tensor passed as both K and V, 64 query
+    heads on one KV head (the shared-latent 512/512 tensor-core path), ragged
+    sequences longer than the window and top-k."""
+    lens = [300, 1030, 7]
+    Tn = sum(lens)
+    g = torch.Generator().manual_seed(57)
+    q = torch.randn(Tn, 64, 512, generator=g).to(DEV, dtype)
+    kv = torch.randn(Tn, 1, 512, generator=g).to(DEV, dtype)
+    sink = torch.randn(64, generator=g).to(DEV)
+    cuq = _cu_t(lens)
+    name = "bfloat16" if dtype == torch.bfloat16 else "float16"
+    out = CSA.csa_prefill_forward(q, kv, kv, cuq, 64, 32, 4, sink)
+    ref, _, _ = O.csa_prefill_forward(npy(q), npy(kv), npy(kv), cuq.cpu(), 64, 32, 4, sink.cpu(), name)
+    close(out, ref, TOL16)
+    out = HCA.hca_prefill_forward(q, kv, kv, cuq, 64, 128, sink)
+    ref, _, _ = O.hca_prefill_forward(npy(q), npy(kv), npy(kv), cuq.cpu(), 64, 128, sink.cpu(), name)
+    close(out, ref, TOL16)
 
 
 def test_csa_hca_forward_bf16():

@@ -77,7 +77,9 @@ def csa_prefill_forward(q, k, v, cu_seqlens, n_win, top_k, m, attn_sink=None, *,
     compressed_k, compressed_v, comp_offsets = compress_kv_overlap(k, v, cu_seqlens, m, gate=gate)
     topk_idxs = build_csa_topk_idxs(q, compressed_k, cu_seqlens, comp_offsets, n_win, top_k, m)
     k_full = torch.cat([k, compressed_k], dim=0)
-    v_full = torch.cat([v, compressed_v], dim=0)
+    # one latent tensor as both K and V (MLA): its compressed K and V are equal,
+    # so the attention reads one [K | compressed] tensor as both
+    v_full = k_full if v is k else torch.cat([v, compressed_v], dim=0)
     return sparse_attn_prefill(q, k_full, v_full, topk_idxs, cu_seqlens, attn_sink=attn_sink, return_lse=return_lse)
 
 

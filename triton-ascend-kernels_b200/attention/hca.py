@@ -62,7 +62,9 @@ def hca_prefill_forward(q, k, v, cu_seqlens, n_win, m_prime, attn_sink=None, *, 
     total_tokens = q.shape[0]
     topk_idxs = build_hca_topk_idxs(cu_seqlens, comp_offsets, total_tokens, n_win, m_prime)
     k_full = torch.cat([k, compressed_k], dim=0)
-    v_full = torch.cat([v, compressed_v], dim=0)
+    # one latent tensor as both K and V (MLA): its compressed K and V are equal,
+    # so the attention reads one [K | compressed] tensor as both
+    v_full = k_full if v is k else torch.cat([v, compressed_v], dim=0)
     return sparse_attn_prefill(q, k_full, v_full, topk_idxs, cu_seqlens, attn_sink=attn_sink, return_lse=return_lse)
 
 

@@ -565,6 +565,11 @@ __device__ __forceinline__ float round_to_t<float>(float x) {
   return x;
 }
 
+// Top-k selection: up to kIdxRoundsMax picks by repeated block argmax, more
+// by one bitonic sort of the (at most kIdxSortMax) causal slots.
+constexpr int kIdxRoundsMax = 16;
+constexpr int kIdxSortMax = 8192;
+
 template <typename T>
 __global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
   extern __shared__ float sc[];  // [max_comp_per_seq] scores, -inf once taken
@@ -590,27 +595,137 @@ __global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const T* q = reinterpret_cast<const T*>(a.q) + row * a.sq[0] + (a.num_q_heads - 1) * a.sq[1];
   const T* ck = reinterpret_cast<const T*>(a.ck) + static_cast<int64_t>(c0) * a.sck[0] + (a.num_kv_heads - 1) * a.sck[1];
-  float qr[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int d = lane + 32 * j;
-    qr[j] = d < a.head_dim ? Elem<T>::to_f(q[d * a.sq[2]]) : 0.f;
+  bool vec = false;
+  if constexpr (sizeof(T) == 2) {
+    vec = a.sq[2] == 1 && a.sck[2] == 1 && a.head_dim % 8 == 0 && a.sck[0] % 8 == 0 &&
+          ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(ck)) & 15) == 0;
   }
-  for (int i = warp; i < n_valid; i += nwarps) {
-    const T* kr = ck + static_cast<int64_t>(i) * a.sck[0];
-    float acc = 0.f;
+  if (vec) {
+    // 16-byte loads: lane l owns dims [8l, 8l+8) and [8l+256, 8l+264); a warp
+    // scores 4 slots per step with all their loads in flight at once
+    if constexpr (sizeof(T) == 2) {
+      const int nch = a.head_dim / 8;
+      float qv[16];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int ch = lane + 32 * c;
+        uint4 u = make_uint4(0, 0, 0, 0);
+        if (ch < nch) u = *reinterpret_cast<const uint4*>(q + ch * 8);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = Elem<T>::unpack2(w[e]);
+          qv[c * 8 + 2 * e] = f.x;
+          qv[c * 8 + 2 * e + 1] = f.y;
+        }
+      }
+      for (int i0 = warp * 4; i0 < n_valid; i0 += nwarps * 4) {
+        uint4 kv[4][2];
+#pragma unroll
+        for (int si = 0; si < 4; ++si)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int ch = lane + 32 * c;
+            kv[si][c] = make_uint4(0, 0, 0, 0);
+            if (i0 + si < n_valid && ch < nch)
+              kv[si][c] = *reinterpret_cast<const uint4*>(ck + static_cast<int64_t>(i0 + si) * a.sck[0] + ch * 8);
+          }
+        float acc[4];
+#pragma unroll
+        for (int si = 0; si < 4; ++si) {
+          float sacc = 0.f;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t w[4] = {kv[si][c].x, kv[si][c].y, kv[si][c].z, kv[si][c].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = Elem<T>::unpack2(w[e]);
+              sacc = fmaf(qv[c * 8 + 2 * e], f.x, sacc);
+              sacc = fmaf(qv[c * 8 + 2 * e + 1], f.y, sacc);
+            }
+          }
+          acc[si] = warp_sum(sacc);
+        }
+        // lanes 0-3 write the four scores (a select, not a register-indexed load)
+        const float mine = lane == 0 ? acc[0] : lane == 1 ? acc[1] : lane == 2 ? acc[2] : acc[3];
+        if (lane < 4 && i0 + lane < n_valid) sc[i0 + lane] = round_to_t<T>(mine);
+      }
+    }
+  } else {
+    float qr[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int d = lane + 32 * j;
-      if (d < a.head_dim) acc += qr[j] * Elem<T>::to_f(kr[d * a.sck[2]]);
+      qr[j] = d < a.head_dim ? Elem<T>::to_f(q[d * a.sq[2]]) : 0.f;
     }
-    acc = warp_sum(acc);
-    if (lane == 0) sc[i] = round_to_t<T>(acc);
+    for (int i = warp; i < n_valid; i += nwarps) {
+      const T* kr = ck + static_cast<int64_t>(i) * a.sck[0];
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int d = lane + 32 * j;
+        if (d < a.head_dim) acc += qr[j] * Elem<T>::to_f(kr[d * a.sck[2]]);
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) sc[i] = round_to_t<T>(acc);
+    }
   }
   __syncthreads();
   const int64_t base = (decode ? static_cast<int64_t>(pos) : static_cast<int64_t>(a.total_tokens)) + c0;
   int32_t* out = a.out + static_cast<int64_t>(row) * a.ld + a.n_win;
   const int n_pick = min(k_sel, n_valid);
+  if (n_pick > kIdxRoundsMax && n_valid <= kIdxSortMax) {
+    // Many picks: sort the causal slots once.  Key = order-preserving bits of
+    // the score (with -0 folded into +0, so equal scores compare equal as in
+    // the rounds below) above the complemented slot index: descending key
+    // order is descending score with ties to the lower slot.  Padding keys are
+    // 0, below every real key.
+    unsigned long long* key = reinterpret_cast<unsigned long long*>(sc);
+    int n_pad = 1;
+    while (n_pad < n_valid) n_pad <<= 1;
+    // scores live in the first n_valid floats of the same buffer: read them
+    // all before any key is written
+    float own[kIdxSortMax / 256];
+#pragma unroll
+    for (int u = 0; u < kIdxSortMax / 256; ++u) {
+      const int i = threadIdx.x + u * 256;
+      own[u] = i < n_valid ? sc[i] + 0.f : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kIdxSortMax / 256; ++u) {
+      const int i = threadIdx.x + u * 256;
+      if (i < n_pad) {
+        unsigned long long kv = 0ull;
+        if (i < n_valid) {
+          uint32_t b = __float_as_uint(own[u]);
+          b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+          kv = (static_cast<unsigned long long>(b) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
+        }
+        key[i] = kv;
+      }
+    }
+    __syncthreads();
+    for (int kk = 2; kk <= n_pad; kk <<= 1) {
+      for (int j = kk >> 1; j > 0; j >>= 1) {
+        for (int i = threadIdx.x; i < n_pad; i += blockDim.x) {
+          const int ixj = i ^ j;
+          if (ixj > i) {
+            const unsigned long long x = key[i], y = key[ixj];
+            if (((i & kk) == 0) ? (x < y) : (x > y)) {
+              key[i] = y;
+              key[ixj] = x;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int r = threadIdx.x; r < n_pick; r += blockDim.x)
+      out[r] = static_cast<int32_t>(base + (0xffffffffu - static_cast<uint32_t>(key[r] & 0xffffffffull)));
+    for (int r = n_pick + threadIdx.x; r < k_sel; r += blockDim.x) out[r] = static_cast<int32_t>(base + r);
+    return;
+  }
   for (int r = 0; r < n_pick; ++r) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
@@ -660,7 +775,13 @@ int csa_indexer_launch(const IndexerArgs& a, cudaStream_t st) {
   const int rows = a.cu_seqlens ? a.total_tokens : a.num_seqs;
   if (rows <= 0) return 0;
   if (a.head_dim > 512) return set_error(2, "csa indexer: head_dim > 512 is not supported");
-  const size_t smem = static_cast<size_t>(a.max_comp_per_seq > 0 ? a.max_comp_per_seq : 1) * sizeof(float);
+  size_t smem = static_cast<size_t>(a.max_comp_per_seq > 0 ? a.max_comp_per_seq : 1) * sizeof(float);
+  if (a.top_k > kIdxRoundsMax && a.max_comp_per_seq <= kIdxSortMax) {
+    // room for the sort keys: 8 bytes per slot, padded to a power of two
+    size_t n_pad = 1;
+    while (n_pad < static_cast<size_t>(a.max_comp_per_seq)) n_pad <<= 1;
+    if (n_pad * sizeof(unsigned long long) > smem) smem = n_pad * sizeof(unsigned long long);
+  }
   if (smem > 200 * 1024) return set_error(2, "csa indexer: more than 51200 compressed slots in one sequence");
   if (a.dtype == kBF16) {
     if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(csa_indexer_kernel<__nv_bfloat16>),

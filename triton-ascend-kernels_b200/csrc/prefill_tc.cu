@@ -191,24 +191,30 @@ __global__ void __launch_bounds__(320, 1)
       constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t idesc_qk = tc_idesc_f16(AB, BM, BN, 0);
       const uint32_t idesc_pv = tc_idesc_f16(AB, BM, D, 1);
+      // Shared-memory descriptors are built once; a k-step adds its byte offset
+      // >> 4 to the 14-bit address field (shared addresses stay below 256 KB, so
+      // the field never carries).  Rebuilding both descriptors for every MMA
+      // made the single issuing thread, not the tensor core, the bottleneck.
+      const uint64_t q_desc0 = tc_sdesc_sw128(sbase + QOFF, 16, 1024);
+      const uint64_t k_desc0 = tc_sdesc_sw128(sbase + KOFF, 16, 1024);
+      const uint64_t v_desc0 = tc_sdesc_sw128(sbase + VOFF, TILE, 1024);
+      constexpr uint64_t kTileStep = (2 * TILE) >> 4;  // next Q tile / next K or V stage
       auto qk = [&](int t, int j) {
-        const int st = j & 1;
+        const uint64_t qd = q_desc0 + (t ? kTileStep : 0), kd = k_desc0 + ((j & 1) ? kTileStep : 0);
         const uint32_t d_tmem = taddr + 256 + t * 128;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * TILE + (kk & 3) * 32;
-          tc_mma_ss(d_tmem, tc_sdesc_sw128(sbase + QOFF + t * 2 * TILE + koff, 16, 1024),
-                    tc_sdesc_sw128(sbase + KOFF + st * 2 * TILE + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+          const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * TILE + (kk & 3) * 32) >> 4);
+          tc_mma_ss(d_tmem, qd + koff, kd + koff, idesc_qk, kk > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[t]);
       };
       auto pv = [&](int t, int j) {
-        const int st = j & 1;
+        const uint64_t vd = v_desc0 + ((j & 1) ? kTileStep : 0);
         const uint32_t p_tmem = taddr + 256 + t * 128;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          tc_mma_ts(taddr + t * 128, p_tmem + kk * 8,
-                    tc_sdesc_sw128(sbase + VOFF + st * 2 * TILE + kk * 2048, TILE, 1024), idesc_pv,
+          tc_mma_ts(taddr + t * 128, p_tmem + kk * 8, vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
                     (j > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&o_done[t]);
       };

@@ -207,6 +207,12 @@ __global__ void __launch_bounds__(288, 1)
       constexpr int NPV = DV < 256 ? DV : 256;
       const uint32_t idesc_qk = tc_idesc_f16(AB, 64, BN, 0);
       const uint32_t idesc_pv = tc_idesc_f16(AB, 64, NPV, 1);
+      // descriptors built once, advanced per k-step by constant offsets (see prefill_tc.cu)
+      const uint64_t q_desc = tc_sdesc_sw128(sbase + L::QOFF, 16, 1024);
+      const uint64_t k_desc0 = tc_sdesc_sw128(sbase + L::KVOFF, 16, 1024);
+      const uint64_t v_desc0 = tc_sdesc_sw128(sbase + L::KVOFF + (SHARED ? 0 : L::NQB * L::BLK), L::BLK, 1024);
+      constexpr uint64_t kStageStep = static_cast<uint64_t>(L::STAGE >> 4);
+      const uint64_t p_desc = tc_sdesc_sw128(sbase + L::POFF, 16, 1024);
       bool ok = mbar_wait(q_full, 0);
       int nq = 0, np = 0;  // next QK / PV to issue
       const uint64_t t0 = globaltimer();
@@ -219,12 +225,11 @@ __global__ void __launch_bounds__(288, 1)
           tc_fence_after();
           const int st = nq & 1;
           const uint32_t d_tmem = taddr + (16u << 16) + st * 64;
-          const uint32_t kbase = sbase + L::KVOFF + st * L::STAGE;
-#pragma unroll 1
+          const uint64_t kd = k_desc0 + (st ? kStageStep : 0);
+#pragma unroll
           for (int kk = 0; kk < DQK / 16; ++kk) {
-            const uint32_t koff = (kk >> 2) * L::BLK + (kk & 3) * 32;
-            tc_mma_ss(d_tmem, tc_sdesc_sw128(sbase + L::QOFF + koff, 16, 1024),
-                      tc_sdesc_sw128(kbase + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+            const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * L::BLK + (kk & 3) * 32) >> 4);
+            tc_mma_ss(d_tmem, q_desc + koff, kd + koff, idesc_qk, kk > 0 ? 1u : 0u);
           }
           tc_commit(&s_full[st]);
           ++nq;
@@ -234,13 +239,13 @@ __global__ void __launch_bounds__(288, 1)
         if (np < nq && mbar_try_wait(smem_u32(p_full), np & 1)) {
           tc_fence_after();
           const int st = np & 1;
-          const uint32_t vbase = sbase + L::KVOFF + st * L::STAGE + (SHARED ? 0 : L::NQB * L::BLK);
+          const uint64_t vd = v_desc0 + (st ? kStageStep : 0);
 #pragma unroll
           for (int half = 0; half < (DV + 255) / 256; ++half) {
 #pragma unroll
             for (int kk = 0; kk < BN / 16; ++kk) {
-              const uint64_t a = tc_sdesc_sw128(sbase + L::POFF + kk * 32, 16, 1024);
-              const uint64_t b = tc_sdesc_sw128(vbase + half * 4 * L::BLK + kk * 2048, L::BLK, 1024);
+              const uint64_t a = p_desc + static_cast<uint64_t>((kk * 32) >> 4);
+              const uint64_t b = vd + static_cast<uint64_t>((half * 4 * L::BLK + kk * 2048) >> 4);
               tc_mma_ss(taddr + half * 256, a, b, idesc_pv, (np > 0 || kk > 0) ? 1u : 0u);
             }
           }
@@ -449,11 +454,13 @@ int sparse_tc_launch(const SparseArgs& a, cudaStream_t st, bool* handled) {
   int r = -1;
   if (a.dtype == kBF16) {
     if (shared && dq == 576 && dv == 512) r = launch_sparse_tc<__nv_bfloat16, 576, 512, true>(a, st);
+    else if (shared && dq == 512 && dv == 512) r = launch_sparse_tc<__nv_bfloat16, 512, 512, true>(a, st);
     else if (dq == 128 && dv == 128) r = launch_sparse_tc<__nv_bfloat16, 128, 128, false>(a, st);
     else if (dq == 64 && dv == 64) r = launch_sparse_tc<__nv_bfloat16, 64, 64, false>(a, st);
     else if (dq == 256 && dv == 256) r = launch_sparse_tc<__nv_bfloat16, 256, 256, false>(a, st);
   } else {
     if (shared && dq == 576 && dv == 512) r = launch_sparse_tc<__half, 576, 512, true>(a, st);
+    else if (shared && dq == 512 && dv == 512) r = launch_sparse_tc<__half, 512, 512, true>(a, st);
     else if (dq == 128 && dv == 128) r = launch_sparse_tc<__half, 128, 128, false>(a, st);
     else if (dq == 64 && dv == 64) r = launch_sparse_tc<__half, 64, 64, false>(a, st);
     else if (dq == 256 && dv == 256) r = launch_sparse_tc<__half, 256, 256, false>(a, st);
