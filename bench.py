@@ -737,7 +737,135 @@ class CsaWL(Workload):
                       "latent, window 128 + top-512), fp32")
 
 
-WORKLOADS = {"prefill": PrefillWL, "sparse": SparseWL, "compress": CompressWL, "csa": CsaWL}
+class MixedWL(Workload):
+    """One GPU's share of the box-scale mixed serving step: the global problem
+    at N GPUs is N/8 of the 8-GPU step (N x 32 prefill sequences, N x 512
+    decode requests), drawn from one seed and assigned to ranks by a greedy
+    longest-processing-time rule on estimated roofline time."""
+    name, unit, bound, peak_key, kernel = "mixed", "% of roofline", "mixed", None, "mixed_step"
+    desc = ("mixed serving step, one GPU's share of 8: varlen causal prefill of 32 sequences with lengths "
+            "log-uniform in [512, 32768] (64 q heads / 8 KV heads, d 128, bf16) plus paged decode of 512 requests "
+            "with contexts U[1, 131072] (32 q heads / 8 KV heads, d 128, page 128, bf16), requests and sequences "
+            "balanced across GPUs by estimated time; the value is the roofline time of the step (prefill FLOPs at "
+            "the measured bf16 peak + decode bytes at the measured HBM copy rate) over its measured time")
+    world = 1
+    POOL = 40960  # pages (21.5 GB of K/V); block tables alias it -- every read still comes from HBM
+
+    def scale(self):
+        return 0.01  # work is in roofline seconds: work / seconds / 0.01 = percent
+
+    def setup(self, rank, device):
+        import flash_attention_prefill as FP
+        import paged_attention_decode as PD
+        import sharding
+        self.FP, self.PD = FP, PD
+        pk, _ = peaks()
+        tens, hbm = pk["bf16_tflops"] * 1e12, pk["hbm_gbs"] * 1e9
+        world = self.world
+        n_pre, n_dec = (4 if SMALL else 32) * world, (64 if SMALL else 512) * world
+        g = torch.Generator().manual_seed(20261201)
+        lens = _loguniform_lengths(n_pre, 512, 32768, g)
+        ctx_all = torch.randint(1, 131072 + 1, (n_dec,), generator=g, dtype=torch.int64)
+        pre_cost = [4.0 * 128 * 64 * L * (L + 1) / 2 / tens for L in lens]
+        dec_cost = [int(c) * 8 * 128 * 2 * 2 / hbm for c in ctx_all]
+        owner = sharding.lpt_assign(pre_cost + dec_cost, world)
+        mine_p = [i for i in range(n_pre) if owner[i] == rank]
+        mine_d = [b for b in range(n_dec) if owner[n_pre + b] == rank]
+        # prefill share
+        self.lens = [lens[i] for i in mine_p]
+        T = sum(self.lens)
+        cu = [0]
+        for L in self.lens:
+            cu.append(cu[-1] + L)
+        gd = torch.Generator(device=device).manual_seed(1000 + rank)
+        self.q = torch.empty(T, 64, 128, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.k = torch.empty(T, 8, 128, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.v = torch.empty(T, 8, 128, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.cu = torch.tensor(cu, dtype=torch.int32, device=device)
+        # decode share: block tables drawn from the page pool (aliased across requests)
+        self.ctx = ctx_all[mine_d].to(torch.int32)
+        B = len(mine_d)
+        maxb = 131072 // 128
+        pool = self.POOL if not SMALL else 4096
+        self.bt = torch.randint(0, pool, (max(B, 1), maxb), generator=g, dtype=torch.int32)[:B].contiguous()
+        self.kc = torch.empty(pool, 8, 128, 128, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.vc = torch.empty(pool, 8, 128, 128, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.qd = torch.empty(B, 32, 128, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.btd, self.ctxd = self.bt.to(device), self.ctx.to(device)
+        self.pre_flops = 4.0 * 128 * 64 * sum(L * (L + 1) / 2 for L in self.lens)
+        self.dec_bytes = int(self.ctx.to(torch.int64).sum()) * 8 * 128 * 2 * 2 + 2 * B * 32 * 128 * 2
+        self.work = self.pre_flops / tens + self.dec_bytes / hbm
+        self.launches = 3
+        self.config = {"prefill_sequences": len(self.lens), "prefill_tokens": T, "decode_requests": B,
+                       "decode_context_tokens": int(self.ctx.to(torch.int64).sum()),
+                       "prefill_tflop": round(self.pre_flops / 1e12, 3), "decode_gb": round(self.dec_bytes / 1e9, 3),
+                       "roofline_ms": round(self.work * 1e3, 3), "kv_pool_pages": pool,
+                       "l2_policy": "inputs larger than L2 (aliased page pool of 21.5 GB)",
+                       "assignment": f"LPT over {n_pre} sequences + {n_dec} requests on {world} GPU(s)"}
+
+    def step(self):
+        out = self.FP.flash_attention_prefill(self.q, self.k, self.v, self.cu, True)
+        self.PD.paged_attention_decode(self.qd, self.kc, self.vc, self.btd, self.ctxd, 128, 128)
+        return out
+
+    def phases(self, device):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        torch.cuda.synchronize(device)
+        ev[0].record()
+        self.FP.flash_attention_prefill(self.q, self.k, self.v, self.cu, True)
+        ev[1].record()
+        self.PD.paged_attention_decode(self.qd, self.kc, self.vc, self.btd, self.ctxd, 128, 128)
+        ev[2].record()
+        torch.cuda.synchronize(device)
+        pms, dms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+        pk, _ = peaks()
+        return {"prefill_ms": round(pms, 3), "prefill_tflops": round(self.pre_flops / (pms * 1e-3) / 1e12, 1),
+                "decode_ms": round(dms, 3), "decode_gbs": round(self.dec_bytes / (dms * 1e-3) / 1e9, 1)}
+
+    def e2e_setup(self):
+        self.h = [t.cpu().pin_memory() for t in (self.q, self.k, self.v, self.qd, self.bt, self.ctx)]
+        self.d = [torch.empty_like(t) for t in (self.q, self.k, self.v, self.qd, self.btd, self.ctxd)]
+        self.hout = [torch.empty(self.q.shape, dtype=torch.bfloat16).pin_memory(),
+                     torch.empty(self.qd.shape, dtype=torch.bfloat16).pin_memory()]
+        return (sum(t.numel() * t.element_size() for t in self.h),
+                sum(t.numel() * t.element_size() for t in self.hout))
+
+    def e2e_step(self):
+        for d, h in zip(self.d, self.h):
+            d.copy_(h, non_blocking=True)
+        q, k, v, qd, bt, ctx = self.d
+        o1 = self.FP.flash_attention_prefill(q, k, v, self.cu, True)
+        o2 = self.PD.paged_attention_decode(qd, self.kc, self.vc, bt, ctx, 128, 128)
+        self.hout[0].copy_(o1, non_blocking=True)
+        self.hout[1].copy_(o2, non_blocking=True)
+
+    def reference_sample(self):
+        from oracle import attention_oracle as O
+        pk, _ = peaks()
+        g = np.random.default_rng(5)
+        L = 1024
+        q = g.standard_normal((L, 64, 128), dtype=np.float32)
+        k = g.standard_normal((L, 8, 128), dtype=np.float32)
+        v = g.standard_normal((L, 8, 128), dtype=np.float32)
+        ctx = np.array([4096, 65536], dtype=np.int32)
+        npg = [(int(c) + 127) // 128 for c in ctx]
+        kc = g.standard_normal((sum(npg), 8, 128, 128), dtype=np.float32)
+        vc = g.standard_normal((sum(npg), 8, 128, 128), dtype=np.float32)
+        bt = np.zeros((2, max(npg)), np.int32)
+        bt[0, :npg[0]] = np.arange(npg[0])
+        bt[1, :npg[1]] = np.arange(npg[0], npg[0] + npg[1])
+        qd = g.standard_normal((2, 32, 128), dtype=np.float32)
+
+        def one():
+            O.prefill(q, k, v, [0, L], True, acc=np.float32)
+            O.paged_decode(qd, kc, vc, bt, ctx, 128, acc=np.float32)
+
+        work = 4.0 * 128 * 64 * L * (L + 1) / 2 / (pk["bf16_tflops"] * 1e12) + \
+            int(ctx.sum()) * 8 * 128 * 2 * 2 / (pk["hbm_gbs"] * 1e9)
+        return one, work, "one causal 1024-token prefill + decode of 2 requests (4096, 65536 tokens), numpy oracle"
+
+
+WORKLOADS = {"prefill": PrefillWL, "sparse": SparseWL, "compress": CompressWL, "csa": CsaWL, "mixed": MixedWL}
 SMALL = False  # --small: a reduced instance of the workload (for ncu captures)
 
 
@@ -770,6 +898,7 @@ def run_workload_reference(args, W):
 def run_workload_ours(args, rank, world, device, W):
     pk, pk_kind = peaks()
     w = W()
+    w.world = world
     w.setup(rank, device)
     if world > 1:
         torch.distributed.barrier()
@@ -811,10 +940,10 @@ def run_workload_ours(args, rank, world, device, W):
         ms, e2e_ms, work_all = float(mx[0]), float(mx[1]), float(tot[2])
     if rank != 0:
         return None
-    scale = 1e12 if w.unit == "TFLOP/s" else 1e9
+    scale = w.scale()
     val = work_all / (ms * 1e-3) / scale
     per_gpu = float(w.work) / (ms * 1e-3) / scale
-    peak = pk[w.peak_key]
+    peak = pk[w.peak_key] if w.peak_key else 100.0
     res = {
         "metric": METRIC, "workload": w.name, "value": round(val, 1), "unit": w.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
@@ -822,10 +951,12 @@ def run_workload_ours(args, rank, world, device, W):
         "config": dict({"workload": w.desc, "parallelism": f"sequence sharding x{world} (weak scaling)"}, **w.config),
         "roofline": {"bound": w.bound, "achieved": round(per_gpu, 1), "peak": peak, "unit": w.unit,
                      "frac": round(per_gpu / peak, 4), "traffic": profile_traffic(f"{w.kernel}.md"),
-                     "peak_source": f"{pk_kind} {w.peak_key} (burst)", "algorithmic_work_per_step": w.work,
+                     "peak_source": (f"{pk_kind} {w.peak_key} (burst)" if w.peak_key else
+                                     f"{pk_kind} bf16_tflops (burst) for prefill + hbm_gbs for decode"),
+                     "algorithmic_work_per_step": w.work,
                      "timed": f"{w.kernel} per step (public API, device-resident inputs), CUDA events"
                  + ("; each step a CUDA-graph replay of the call" if graph is not None else "")},
-        "e2e": {"value": round(work_all / (e2e_ms * 1e-3) / scale, 1), "unit": w.unit, "ms_per_step": round(e2e_ms, 3),
+        "e2e": {"value": round(work_all / (e2e_ms * 1e-3) / scale, 2), "unit": w.unit, "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps * w.launches,
         "clocks": clk.summary(),
@@ -836,7 +967,7 @@ def run_workload_ours(args, rank, world, device, W):
         res["config"]["output_gather_to_rank0_ms"] = round(gather_ms, 3)
     if hasattr(w, "phases"):
         res["config"]["phases"] = w.phases(device)
-    sus = pk.get(w.peak_key + "_sustained")
+    sus = pk.get(w.peak_key + "_sustained") if w.peak_key else None
     if sus:
         # the timed loop runs for seconds at the power cap: the sustained GEMM
         # figure of the same file is the matching denominator
