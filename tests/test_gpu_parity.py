@@ -203,7 +203,7 @@ def test_golden_hca_decode(case):
 
 
 # ---------------------------------------------------------------------------
-# BASELINE-shaped configurations and edge cases
+# benchmark-shaped configurations and edge cases
 # ---------------------------------------------------------------------------
 
 def _cu_t(lens):
@@ -308,8 +308,8 @@ def test_paged_decode_fp32_and_stale_tail():
     close(out, ref, TOL16)
 
 
-def test_paged_decode_cfg2_sample():
-    """BASELINE decode shape (batch 64, 32/8 heads, d=128, page 128, pool 5000,
+def test_paged_decode_bench_shape_sample():
+    """The decode bench shape (batch 64, 32/8 heads, d=128, page 128, pool 5000,
     ctx U[1,8192]) -- checked against the oracle on 6 of the 64 requests."""
     q, kc, vc, bt, cl = _paged_case(64, 32, 8, 128, 128, 8192, 5000, torch.bfloat16, 11)
     out, lse = PD.paged_attention_decode(q, kc, vc, bt, cl, 128, 128, return_lse=True)
@@ -336,7 +336,7 @@ def _sparse_case(Tn, H, Hkv, D, Dv, rows, K, dtype, seed, shared_latent=False, p
 
 @pytest.mark.parametrize("with_sink", [False, True])
 def test_sparse_prefill_mla_shape(with_sink, kernel_path):
-    """BASELINE sparse shape at small size: 64 query heads sharing 1 KV head,
+    """The sparse bench shape at small size: 64 query heads sharing 1 KV head,
     Dqk 576 (512 latent + 64 rope), Dv 512 with v a view of k's first 512
     dims, 256 indices per token with -1 padding and a fully masked row."""
     q, k, v, idx, sink = _sparse_case(24, 64, 1, 576, 512, 1500, 256, torch.bfloat16, 21, shared_latent=True)
@@ -347,8 +347,8 @@ def test_sparse_prefill_mla_shape(with_sink, kernel_path):
     close_lse(lse, ref_lse)
 
 
-def test_sparse_prefill_cfg3_index_width():
-    """cfg3 index width: 2048 sorted unique indices per token drawn causally
+def test_sparse_prefill_wide_index_rows():
+    """The sparse bench's index width: 2048 sorted unique indices per token drawn causally
     from a 32768-row latent KV (MQA, 64 heads, 576/512), -1 padding for early
     positions; 16 tokens checked against the oracle."""
     g = torch.Generator().manual_seed(23)
