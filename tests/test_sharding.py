@@ -126,6 +126,28 @@ def test_two_rank_gather_forms(tmp_path):
         assert torch.equal(res[key], want), key
 
 
+def _concat_worker(rank, world, port, q_path):
+    _init(rank, world, port)
+    try:
+        rows = [5, 2, 0][rank]  # uneven blocks, one empty
+        start = [0, 5, 7][rank]
+        local = torch.arange(start, start + rows, dtype=torch.float32)[:, None] * torch.ones(1, 3)
+        a = S.concat_rows(local)
+        b = S.concat_rows(local, dst=2)
+        if rank == 2:
+            torch.save({"a": a, "b": b}, q_path)
+        else:
+            assert b is None
+    finally:
+        dist.destroy_process_group()
+
+
+def test_three_rank_concat_uneven_blocks(tmp_path):
+    res = _run(_concat_worker, 3, tmp_path)
+    want = torch.arange(7, dtype=torch.float32)[:, None] * torch.ones(1, 3)
+    assert torch.equal(res["a"], want) and torch.equal(res["b"], want)
+
+
 def _run(worker, world, tmp_path):
     path = str(tmp_path / "result.pt")
     mp.spawn(worker, args=(world, _free_port(), path), nprocs=world, join=True)

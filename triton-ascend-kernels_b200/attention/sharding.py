@@ -133,3 +133,16 @@ def gather_rows(local, index, total_rows, group=None, dst=None):
         else:
             full[idxs[r][:c]] = blk[:c]
     return full
+
+
+def concat_rows(local, group=None, dst=None):
+    """Every rank's [rows_r, ...] block, concatenated in rank order (blocks may
+    differ in length): offsets are the prefix sums of the ranks' row counts.
+    dst as in gather_rows."""
+    world = dist.get_world_size(group)
+    me = dist.get_rank(group)
+    n = torch.tensor([local.shape[0]], dtype=torch.int64, device=local.device)
+    counts = [torch.empty_like(n) for _ in range(world)]
+    dist.all_gather(counts, n, group=group)
+    counts = [int(c) for c in counts]
+    return gather_rows(local, sum(counts[:me]), sum(counts), group=group, dst=dst)
