@@ -376,6 +376,77 @@ def test_sparse_prefill_gqa_fp32_and_oob():
     close(out, ref, TOL32)
 
 
+def _sparse_decode_case(ctx, H, Hkv, D, Dv, P, n_win, n_comp_slots, ncomp, dtype, seed, shared_latent=False):
+    """Paged window + compressed rows for sparse decode, with index rows that
+    exercise the slot-position rule: window slots hold the last n_win logical
+    positions (negative ones masked) plus one position == ctx (masked) and one
+    -1; compressed slots hold ctx + row for sorted random rows, plus one index
+    below ctx (masked in a compressed slot), one past the last compressed row
+    and -1 padding."""
+    g = torch.Generator().manual_seed(seed)
+    B = len(ctx)
+    maxb = max((max(ctx) + P - 1) // P, 1)
+    pool = sum((c + P - 1) // P for c in ctx) + 5
+    perm = torch.randperm(pool, generator=g).to(torch.int32)
+    bt = torch.zeros(B, maxb, dtype=torch.int32)
+    i = 0
+    for b, c in enumerate(ctx):
+        for j in range((c + P - 1) // P):
+            bt[b, j] = perm[i]
+            i += 1
+    kc = torch.randn(pool, Hkv, P, D, generator=g).to(DEV, dtype)
+    ck = torch.randn(ncomp, Hkv, D, generator=g).to(DEV, dtype)
+    if shared_latent:
+        vc, cv = kc[..., :Dv], ck[..., :Dv]
+    else:
+        vc = torch.randn(pool, Hkv, P, Dv, generator=g).to(DEV, dtype)
+        cv = torch.randn(ncomp, Hkv, Dv, generator=g).to(DEV, dtype)
+    q = torch.randn(B, H, D, generator=g).to(DEV, dtype)
+    idx = torch.full((B, n_win + n_comp_slots), -1, dtype=torch.int32)
+    for b, c in enumerate(ctx):
+        idx[b, :n_win] = torch.arange(c - n_win, c, dtype=torch.int32)
+        if b % 3 == 1:
+            idx[b, n_win // 2] = c          # position == ctx: masked
+            idx[b, n_win // 3] = -1
+        n_here = (b * 37) % (n_comp_slots + 1)
+        rows = torch.randperm(ncomp, generator=g)[:n_here].sort().values.to(torch.int32)
+        idx[b, n_win:n_win + rows.numel()] = c + rows
+        if b % 4 == 2 and n_here > 2:
+            idx[b, n_win] = c - 1            # below ctx in a compressed slot: masked
+            idx[b, n_win + n_here - 1] = c + ncomp  # past the compressed rows: masked
+    sink = torch.randn(H, generator=g).to(DEV)
+    cl = torch.tensor(ctx, dtype=torch.int32)
+    return q, kc, vc, ck, cv, bt.to(DEV), idx.to(DEV), cl.to(DEV), sink
+
+
+@pytest.mark.parametrize("shape", ["latent576", "latent512", "gqa128", "gqa64"])
+@pytest.mark.parametrize("with_sink", [False, True])
+def test_sparse_decode_paged_and_compressed(shape, with_sink, kernel_path):
+    """Sparse decode over a paged window plus compressed rows: 64 heads sharing
+    one latent KV head (Dqk 576 or 512, V a view of K), and GQA with 128- and
+    64-dim heads; ragged index rows (slot counts not a multiple of 64), empty
+    and short contexts, and every masking case of the slot-position rule."""
+    ctx = [0, 1, 5, 127, 128, 3 * 64 + 7, 9 * 64, 1000, 33, 2]
+    if shape.startswith("latent"):
+        D = int(shape[6:])
+        case = _sparse_decode_case(ctx, 64, 1, D, 512, 64, 128, 200, 700, torch.bfloat16, 51, shared_latent=True)
+        n_win = 128
+    elif shape == "gqa128":
+        case = _sparse_decode_case(ctx, 16, 4, 128, 128, 16, 40, 90, 300, torch.float16, 52)
+        n_win = 40
+    else:
+        case = _sparse_decode_case(ctx, 8, 2, 64, 64, 32, 70, 30, 120, torch.bfloat16, 53)
+        n_win = 70
+    q, kc, vc, ck, cv, bt, idx, cl, sink = case
+    P = kc.shape[2]
+    s = sink if with_sink else None
+    out, lse = SA.sparse_attn_decode(q, kc, vc, ck, cv, bt, idx, cl, n_win, P, s, return_lse=True)
+    ref, ref_lse = O.sparse_decode(npy(q), npy(kc), npy(vc), npy(ck), npy(cv), bt.cpu(), idx.cpu(), cl.cpu(),
+                                   n_win, P, None if s is None else s.cpu())
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("gated", [False, True])
 def test_compress_csa_hca(dtype, gated):

@@ -1,4 +1,5 @@
-// Top-k sparse attention (prefill form) on the 5th-generation tensor cores.
+// Top-k sparse attention (prefill and decode forms) on the 5th-generation
+// tensor cores.
 //
 // Semantics: attention/sparse_attn_fwd.py of the reference (kernel SA:10-98):
 // token t, query head h attends to rows topk_idxs[t, :] of K/V (negative =
@@ -7,6 +8,13 @@
 // (SA:94-95); plus the natural-log LSE.  Also covers the MLA-style latent
 // layout the reference cannot express (Dqk = 576 = 512 latent + 64 rope,
 // Dv = 512, V a view of K's first 512 columns).
+//
+// Decode form (kernel SA:105-246): one query token per request; slot c of the
+// request's index row is a window slot for c < num_win (index = logical
+// position, valid when 0 <= idx < ctx, read from the paged cache through the
+// block table) and a compressed slot otherwise (valid when idx >= ctx, row
+// idx - ctx of the compressed K/V).  Only the producer's row addressing and the
+// validity mask differ from the prefill form.
 //
 // One CTA = one query token x one group of up to 64 query heads sharing a KV
 // head (MQA: all 64 heads of the token).  The 64 head rows are the MMA's
@@ -49,7 +57,29 @@ struct SparseTcParams {
   float* lse;
   int H, Hkv, G, head_chunks;
   float scale_log2;
+  // Row sources, in elements.  Prefill: row r of head h is k + r*k_s0 + h*k_sh.
+  // Decode: k/v are the paged caches (page stride k_s0, head k_sh, row in page
+  // k_sr) and ck/cv the compressed rows (row stride ck_s0, head ck_sh).
+  const void* k;
+  const void* v;
+  const void* ck;
+  const void* cv;
+  int64_t k_s0, k_sh, k_sr, v_s0, v_sh, v_sr;
+  int64_t ck_s0, ck_sh, cv_s0, cv_sh;
+  const int32_t* bt;
+  int64_t sbt0, sbt1;
+  const int32_t* ctx_lens;
+  int64_t ncomp;
+  int num_win, block_size;
+  int decode;
 };
+
+// Validity of slot c holding index j (decode: by slot position, SA:151-171 for
+// the window slots [0, num_win) and SA:197-210 for the compressed ones).
+__device__ __forceinline__ bool sp_slot_valid(const SparseTcParams& p, int c, int64_t j, int ctx) {
+  if (!p.decode) return j >= 0 && j < p.kv_rows;
+  return c < p.num_win ? (j >= 0 && j < ctx) : (j >= ctx && j - ctx < p.ncomp);
+}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1) {
   asm volatile(
@@ -99,8 +129,7 @@ struct SpLayout {
 
 template <typename T, int DQK, int DV, bool SHARED>
 __global__ void __launch_bounds__(288, 1)
-    sparse_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const SparseTcParams p, const void* kbase_ptr,
-                     int64_t krow_stride, const void* vbase_ptr, int64_t vrow_stride) {
+    sparse_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const SparseTcParams p) {
   using L = SpLayout<DQK, DV, SHARED>;
   constexpr int BN = 64;
   constexpr int NPROD = 128;  // producer threads
@@ -125,6 +154,7 @@ __global__ void __launch_bounds__(288, 1)
   const int n_tiles = (p.k_topk + BN - 1) / BN;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int32_t* idx_row = p.topk + static_cast<int64_t>(t) * p.stk0;
+  const int ctx = p.decode ? p.ctx_lens[t] : 0;
 
   if (tid == 0) {
     mbar_init(q_full, 1);
@@ -160,21 +190,41 @@ __global__ void __launch_bounds__(288, 1)
       for (int cb = 0; cb < L::NQB; ++cb)
         tma_load_2d(smem + L::QOFF + cb * L::BLK, &tmQ, q_full, cb * 64, t * p.H + h0);
     }
-    const T* kb = reinterpret_cast<const T*>(kbase_ptr);
-    const T* vb = reinterpret_cast<const T*>(vbase_ptr);
-    auto load_rows = [&](int j, int64_t* rows) {
+    const T* kb = reinterpret_cast<const T*>(p.k);
+    const T* vb = reinterpret_cast<const T*>(p.v);
+    const int32_t* bt_row = p.decode ? p.bt + static_cast<int64_t>(t) * p.sbt0 : nullptr;
+    // K (and V unless shared) row addresses of this thread's 4 slots of tile j; null = masked
+    auto load_rows = [&](int j, const T** kr, const T** vr) {
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         const int c = j * BN + g * 16 + rsub;
         const int64_t r = (j < n_tiles && c < p.k_topk) ? static_cast<int64_t>(idx_row[c * p.stk1]) : -1;
-        rows[g] = (r >= 0 && r < p.kv_rows) ? r * p.Hkv + kvh : -1;
+        kr[g] = nullptr;
+        vr[g] = nullptr;
+        if (!(j < n_tiles && c < p.k_topk) || !sp_slot_valid(p, c, r, ctx)) continue;
+        if (!p.decode) {
+          kr[g] = kb + r * p.k_s0 + kvh * p.k_sh;
+          if (!SHARED) vr[g] = vb + r * p.v_s0 + kvh * p.v_sh;
+        } else if (c < p.num_win) {  // window slot: logical position -> page, row in page (SA:160-166)
+          const int64_t page = bt_row[(r / p.block_size) * p.sbt1];
+          const int64_t off = r % p.block_size;
+          kr[g] = kb + page * p.k_s0 + kvh * p.k_sh + off * p.k_sr;
+          if (!SHARED) vr[g] = vb + page * p.v_s0 + kvh * p.v_sh + off * p.v_sr;
+        } else {  // compressed slot: row idx - ctx (SA:205-210)
+          const int64_t cr = r - ctx;
+          kr[g] = reinterpret_cast<const T*>(p.ck) + cr * p.ck_s0 + kvh * p.ck_sh;
+          if (!SHARED) vr[g] = reinterpret_cast<const T*>(p.cv) + cr * p.cv_s0 + kvh * p.cv_sh;
+        }
       }
     };
-    int64_t cur[4], nxt[4];
-    load_rows(0, cur);
+    const T* cur[4];
+    const T* nxt[4];
+    const T* vcur[4];
+    const T* vnxt[4];
+    load_rows(0, cur, vcur);
     for (int j = 0; j < n_tiles; ++j) {
       const int st = j & 1;
-      load_rows(j + 1, nxt);  // in flight while this tile's stage frees up
+      load_rows(j + 1, nxt, vnxt);  // in flight while this tile's stage frees up
       if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1)) {
         *abort_flag = 1;
         break;
@@ -183,13 +233,14 @@ __global__ void __launch_bounds__(288, 1)
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         const int row = g * 16 + rsub;
-        const bool ok = cur[g] >= 0;
-        const T* src = kb + (ok ? cur[g] : 0) * krow_stride + chunk * 8;
+        const bool ok = cur[g] != nullptr;
+        // masked rows: a zero-byte copy (zero fill) from an in-bounds address
+        const T* src = (ok ? cur[g] : kb) + chunk * 8;
         const uint32_t dst_off = row * 128 + ((chunk ^ (row & 7)) << 4);
 #pragma unroll
         for (int cb = 0; cb < L::NQB; ++cb) cp_async_16(kst + cb * L::BLK + dst_off, src + cb * 64, ok);
         if (!SHARED) {
-          const T* vsrc = vb + (ok ? cur[g] : 0) * vrow_stride + chunk * 8;
+          const T* vsrc = (ok ? vcur[g] : vb) + chunk * 8;
 #pragma unroll
           for (int cb = 0; cb < L::NVB; ++cb)
             cp_async_16(kst + (L::NQB + cb) * L::BLK + dst_off, vsrc + cb * 64, ok);
@@ -197,7 +248,10 @@ __global__ void __launch_bounds__(288, 1)
       }
       cp_async_mbar_arrive(&kv_full[st]);
 #pragma unroll
-      for (int g = 0; g < 4; ++g) cur[g] = nxt[g];
+      for (int g = 0; g < 4; ++g) {
+        cur[g] = nxt[g];
+        vcur[g] = vnxt[g];
+      }
     }
     cp_async_wait_all();
   } else if (warp == 8) {
@@ -281,8 +335,8 @@ __global__ void __launch_bounds__(288, 1)
       const int c0 = j * BN + lane, c1 = c0 + 32;
       const int64_t r0 = c0 < p.k_topk ? static_cast<int64_t>(idx_row[c0 * p.stk1]) : -1;
       const int64_t r1 = c1 < p.k_topk ? static_cast<int64_t>(idx_row[c1 * p.stk1]) : -1;
-      const uint32_t lo = __ballot_sync(0xffffffffu, r0 >= 0 && r0 < p.kv_rows);
-      const uint32_t hi_m = __ballot_sync(0xffffffffu, r1 >= 0 && r1 < p.kv_rows);
+      const uint32_t lo = __ballot_sync(0xffffffffu, c0 < p.k_topk && sp_slot_valid(p, c0, r0, ctx));
+      const uint32_t hi_m = __ballot_sync(0xffffffffu, c1 < p.k_topk && sp_slot_valid(p, c1, r1, ctx));
       return hi ? hi_m : lo;
     };
     uint32_t vnext = n_tiles > 0 ? tile_mask(0) : 0u;
@@ -401,10 +455,8 @@ static int launch_sparse_tc(const SparseArgs& a, cudaStream_t st) {
   using L = SpLayout<DQK, DV, SHARED>;
   const int G = a.num_q_heads / a.num_kv_heads;
   CUtensorMap mq;
-  // q as [T * H, Dqk] rows (TMA); gathered K/V rows by cp.async from row bases
+  // q as [T * H, Dqk] rows (TMA); gathered K/V rows by cp.async from their row addresses
   if (int r = encode_rows_map(&mq, a.q, static_cast<int64_t>(a.num_tokens) * a.num_q_heads, DQK, a.sq[1], 64)) return r;
-  const int64_t krow = a.num_kv_heads == 1 ? a.sk[0] : a.sk[1];
-  const int64_t vrow = a.num_kv_heads == 1 ? a.sv[0] : a.sv[1];
   SparseTcParams p{};
   p.topk = a.topk;
   p.stk0 = a.stk[0];
@@ -421,35 +473,81 @@ static int launch_sparse_tc(const SparseArgs& a, cudaStream_t st) {
   p.G = G;
   p.head_chunks = (G + 63) / 64;
   p.scale_log2 = a.scale * kLog2e;
+  p.k = a.k;
+  p.v = a.v;
+  p.k_s0 = a.sk[0];
+  p.k_sh = a.sk[1];
+  p.v_s0 = a.sv[0];
+  p.v_sh = a.sv[1];
+  p.decode = a.decode;
+  if (a.decode) {
+    p.k_sr = a.sk[2];
+    p.v_sr = a.sv[2];
+    p.ck = a.ck;
+    p.cv = a.cv;
+    p.ck_s0 = a.sck[0];
+    p.ck_sh = a.sck[1];
+    p.cv_s0 = a.scv[0];
+    p.cv_sh = a.scv[1];
+    p.bt = a.block_tables;
+    p.sbt0 = a.sbt[0];
+    p.sbt1 = a.sbt[1];
+    p.ctx_lens = a.context_lens;
+    p.ncomp = a.num_compressed;
+    p.num_win = a.num_win;
+    p.block_size = a.block_size;
+  }
   auto kern = sparse_tc_kernel<T, DQK, DV, SHARED>;
   if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::SMEM)) return r;
   dim3 grid(a.num_tokens, a.num_kv_heads * p.head_chunks);
-  kern<<<grid, 288, L::SMEM, st>>>(mq, p, a.k, krow, a.v, vrow);
+  kern<<<grid, 288, L::SMEM, st>>>(mq, p);
   return 0;
 }
 
-static bool rows_ok(const void* ptr, const int64_t* s, int hkv) {
+// A gathered row source takes 16-byte copies: base 16-byte aligned, innermost
+// stride 1 and every stride the kernel steps by a multiple of 8 elements (the
+// head stride only when there is more than one KV head).
+static bool rows_ok(const void* ptr, const int64_t* s, int nd, int hkv) {
   if (reinterpret_cast<uintptr_t>(ptr) & 15) return false;
-  if (s[2] != 1) return false;
-  const int64_t row = hkv == 1 ? s[0] : s[1];
-  if (hkv > 1 && s[0] != hkv * s[1]) return false;
-  return row > 0 && (row * 2) % 16 == 0;
+  if (s[nd - 1] != 1) return false;
+  for (int i = 0; i < nd - 1; ++i) {
+    if (i == 1 && hkv == 1) continue;
+    if (s[i] % 8) return false;
+  }
+  return true;
+}
+
+static bool same_view(const void* a, const int64_t* sa, const void* b, const int64_t* sb, int nd) {
+  if (a != b) return false;
+  for (int i = 0; i < nd; ++i)
+    if (sa[i] != sb[i]) return false;
+  return true;
 }
 
 int sparse_tc_launch(const SparseArgs& a, cudaStream_t st, bool* handled) {
   *handled = false;
-  if (a.decode || a.dtype == kF32) return 0;
+  if (a.dtype == kF32) return 0;
   const int G = a.num_q_heads / a.num_kv_heads;
   if (G > 64 && G % 64 != 0) return 0;
-  if (a.num_tokens > 2147483647 / 64 || a.kv_rows * a.num_kv_heads > 2147483647) return 0;
+  if (a.num_tokens > 2147483647 / 64) return 0;
   // q rows [T * H, Dqk] must be dense over heads
   if ((reinterpret_cast<uintptr_t>(a.q) & 15) || a.sq[2] != 1 || a.sq[0] != static_cast<int64_t>(a.num_q_heads) * a.sq[1] ||
       (a.sq[1] * 2) % 16 != 0)
     return 0;
-  if (!rows_ok(a.k, a.sk, a.num_kv_heads) || !rows_ok(a.v, a.sv, a.num_kv_heads)) return 0;
+  bool shared;
+  if (!a.decode) {
+    if (!rows_ok(a.k, a.sk, 3, a.num_kv_heads) || !rows_ok(a.v, a.sv, 3, a.num_kv_heads)) return 0;
+    shared = same_view(a.v, a.sv, a.k, a.sk, 3);
+  } else {
+    // with no compressed rows every compressed slot is masked and ck/cv are never read
+    const bool comp = a.num_compressed > 0;
+    if (!rows_ok(a.k, a.sk, 4, a.num_kv_heads) || !rows_ok(a.v, a.sv, 4, a.num_kv_heads) || a.block_size <= 0 ||
+        (comp && (!rows_ok(a.ck, a.sck, 3, a.num_kv_heads) || !rows_ok(a.cv, a.scv, 3, a.num_kv_heads))))
+      return 0;
+    shared = same_view(a.v, a.sv, a.k, a.sk, 4) && (!comp || same_view(a.cv, a.scv, a.ck, a.sck, 3));
+  }
+  shared = shared && a.head_dim_v <= a.head_dim;
   if (a.so[2] != 1 || (a.so[0] % 8) || (a.so[1] % 8) || (reinterpret_cast<uintptr_t>(a.out) & 15)) return 0;
-  const bool shared = a.v == a.k && a.sv[0] == a.sk[0] && a.sv[1] == a.sk[1] && a.sv[2] == a.sk[2] &&
-                      a.head_dim_v <= a.head_dim;
   const int dq = a.head_dim, dv = a.head_dim_v;
   int r = -1;
   if (a.dtype == kBF16) {
