@@ -161,6 +161,10 @@ int tak_build_token_to_seq(const int32_t* cu_seqlens, int64_t num_seqs, int64_t 
  * outputs [num_compressed,H_kv,D(v)].  gate: NULL = plain mean (the
  * reference); else float32 [T] logits and each slot is the softmax(gate)-
  * weighted sum of its window (an addition, no counterpart in the reference).
+ * v = NULL (with compressed_v = NULL and head_dim_v = 0; v_strides and
+ * cv_strides are then ignored) pools K alone: for callers whose V is a view
+ * of K, whose compressed V is then the same view of compressed K (an
+ * addition; the reference always pools both).
  */
 int tak_compress_kv(const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
                     const float* gate, int64_t gate_stride, const int32_t* cu_seqlens, const int32_t* comp_offsets,
@@ -173,7 +177,8 @@ int tak_compress_kv(const void* k, const int64_t* k_strides, const void* v, cons
  * from a paged cache [num_blocks,H_kv,P,D].  Replaces the page gather +
  * compress of csa_decode_forward (attention/csa.py:225-256) and
  * hca_decode_forward (attention/hca.py:204-232).  gate (optional) is
- * float32 [num_blocks, P] with strides gate_strides[2].
+ * float32 [num_blocks, P] with strides gate_strides[2].  v_cache = NULL
+ * pools K alone, as for tak_compress_kv.
  */
 int tak_compress_kv_paged(const void* k_cache, const int64_t* k_strides, const void* v_cache,
                           const int64_t* v_strides, const float* gate, const int64_t* gate_strides,

@@ -562,6 +562,43 @@ def test_csa_hca_forward_latent512(dtype):
     close(out, ref, TOL16)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_csa_hca_decode_latent512(dtype):
+    """MLA-style decode: one paged 512-dim latent cache passed as both K and V
+    (pooled once, compressed V a view of compressed K, the shared-latent
+    tensor-core sparse path), 64 query heads, ragged contexts across pages."""
+    ctx = [300, 1030, 7, 129, 64]
+    g = torch.Generator().manual_seed(59)
+    P = 64
+    _, kc, _, _, _, bt, _, cl, sink = _sparse_decode_case(ctx, 64, 1, 512, 512, P, 1, 1, 1, dtype, 59,
+                                                          shared_latent=True)
+    q = torch.randn(len(ctx), 64, 512, generator=g).to(DEV, dtype)
+    name = "bfloat16" if dtype == torch.bfloat16 else "float16"
+    out = CSA.csa_decode_forward(q, kc, kc, bt, cl, 64, 32, 4, P, sink)
+    ref, _, _ = O.csa_decode_forward(npy(q), npy(kc), npy(kc), bt.cpu(), cl.cpu(), 64, 32, 4, P, sink.cpu(), name)
+    close(out, ref, TOL16)
+    out = HCA.hca_decode_forward(q, kc, kc, bt, cl, 64, 128, P, sink)
+    ref, _, _ = O.hca_decode_forward(npy(q), npy(kc), npy(kc), bt.cpu(), cl.cpu(), 64, 128, P, sink.cpu(), name)
+    close(out, ref, TOL16)
+
+
+@pytest.mark.parametrize("stride,window", [(4, 8), (128, 128), (3, 6)])
+def test_compress_paged_k_only_latent(stride, window):
+    """Paged pooling with V a prefix view of K (576-dim latent + rope rows, V =
+    the first 512 columns): K is pooled once and compressed V is the same view
+    of compressed K, equal to pooling V on its own."""
+    ctx = [0, 1, 5, 300, 1030, 129, 64, 2]
+    _, kc, vc, _, _, bt, _, cl, _ = _sparse_decode_case(ctx, 8, 1, 576, 512, 64, 1, 1, 1, torch.bfloat16, 61,
+                                                        shared_latent=True)
+    ck, cv, offs, lens, _ = T.compress_paged(kc, vc, bt, cl, 64, stride, window)
+    assert cv.data_ptr() == ck.data_ptr() and cv.shape[-1] == 512
+    kt, cut = O.gather_paged_to_tnd(npy(kc), bt.cpu(), cl.cpu(), 64)
+    rk, _, roffs = O.compress_kv(kt, kt[..., :512], cut, stride, window)
+    np.testing.assert_array_equal(offs.cpu().numpy(), roffs)
+    close(ck, rk, 1e-2)
+    close(cv, rk[..., :512], 1e-2)
+
+
 def test_csa_hca_forward_bf16():
     lens = [50, 200]
     Tn = sum(lens)

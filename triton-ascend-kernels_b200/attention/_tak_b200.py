@@ -215,9 +215,18 @@ def compress_csa_hca(k, v, cu_seqlens, m, m_prime, gate=None):
     return (ck, cv, co), (hk, hv, ho)
 
 
+def is_prefix_view(v, k):
+    """v is k or k[..., :Dv] (same storage offset and strides): pooling k
+    then covers v."""
+    return (v.data_ptr() == k.data_ptr() and v.stride() == k.stride() and v.dim() == k.dim()
+            and v.shape[:-1] == k.shape[:-1] and v.shape[-1] <= k.shape[-1] and v.dtype == k.dtype)
+
+
 def compress_paged(k_cache, v_cache, block_tables, context_lens, block_size, stride, window):
     """Pool each sequence's first context_lens[s] rows straight out of a paged
     cache (fuses the reference's page gather, CSA:225-256 / HCA:204-232).
+    When v_cache is a prefix view of k_cache (MLA latent caches) K is pooled
+    once and compressed_v is the same view of compressed_k.
     Returns (compressed_k, compressed_v, comp_offsets[int32, device], lengths[host])."""
     dev = k_cache.device
     bt = as_i32(block_tables, dev)
@@ -226,14 +235,17 @@ def compress_paged(k_cache, v_cache, block_tables, context_lens, block_size, str
     offs = comp_offsets_host(lens, stride)
     nc = offs[-1]
     hkv = k_cache.shape[1]
+    k_only = is_prefix_view(v_cache, k_cache)
     ck = k_cache.new_empty((nc, hkv, k_cache.shape[3]))
-    cv = v_cache.new_empty((nc, hkv, v_cache.shape[3]))
+    cv = ck[..., :v_cache.shape[3]] if k_only else v_cache.new_empty((nc, hkv, v_cache.shape[3]))
     offs_t = torch.tensor(offs, dtype=torch.int32).to(dev)
     if nc:
+        vv, cvv = (None, None) if k_only else (v_cache, cv)
         check(lib().tak_compress_kv_paged(
-            ptr(k_cache), strides(k_cache), ptr(v_cache), strides(v_cache), None, None, ptr(bt), strides(bt),
-            ptr(cl), block_size, ptr(offs_t), len(lens), nc, ptr(ck), strides(ck), ptr(cv), strides(cv), hkv,
-            k_cache.shape[3], v_cache.shape[3], stride, window, dtype_code(k_cache), stream_of(k_cache)))
+            ptr(k_cache), strides(k_cache), ptr(vv), None if vv is None else strides(vv), None, None, ptr(bt),
+            strides(bt), ptr(cl), block_size, ptr(offs_t), len(lens), nc, ptr(ck), strides(ck), ptr(cvv),
+            None if cvv is None else strides(cvv), hkv, k_cache.shape[3], 0 if k_only else v_cache.shape[3],
+            stride, window, dtype_code(k_cache), stream_of(k_cache)))
     return ck, cv, offs_t, lens, offs
 
 

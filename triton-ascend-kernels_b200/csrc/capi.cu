@@ -331,9 +331,13 @@ static int compress_common(CompressArgs& a, const void* k, const int64_t* k_stri
                            int64_t head_dim_v, int64_t stride, int64_t window, int dtype) {
   TAK_REQUIRE(dtype >= 0 && dtype <= 2, "compress: unknown dtype");
   TAK_REQUIRE(stride > 0 && window > 0, "compress: stride and window must be positive");
-  TAK_REQUIRE(num_kv_heads > 0 && head_dim > 0 && head_dim_v > 0, "compress: bad head sizes");
-  TAK_REQUIRE(k && v && k_strides && v_strides && comp_offsets && compressed_k && compressed_v && ck_strides &&
-                  cv_strides,
+  // v == null: K only (no V rows, no compressed V, head_dim_v 0), for callers whose V is a view of K
+  const bool k_only = v == nullptr;
+  TAK_REQUIRE(num_kv_heads > 0 && head_dim > 0 && (k_only ? head_dim_v == 0 : head_dim_v > 0),
+              "compress: bad head sizes");
+  TAK_REQUIRE(k_only == (compressed_v == nullptr), "compress: v and compressed_v must both be given or both null");
+  TAK_REQUIRE(k && k_strides && (k_only || v_strides) && comp_offsets && compressed_k && ck_strides &&
+                  (k_only || cv_strides),
               "compress: null pointer");
   a.k = k; copy_strides(a.sk, k_strides, nk);
   a.v = v; copy_strides(a.sv, v_strides, nk);
@@ -403,6 +407,7 @@ int tak_compress_kv_csa_hca(const void* k, const int64_t* k_strides, const void*
                             void* hca_v, const int64_t* hca_v_strides, int64_t num_kv_heads, int64_t head_dim,
                             int64_t head_dim_v, int64_t m, int64_t m_prime, int dtype, void* stream) {
   if (num_csa == 0 && num_hca == 0) return 0;
+  TAK_REQUIRE(v && csa_v && hca_v, "compress csa+hca: null v");
   TAK_REQUIRE(m > 0 && m_prime > 0, "compress csa+hca: m and m_prime must be positive");
   TAK_REQUIRE(total_tokens > 0, "compress csa+hca: total_tokens must be positive when slots exist");
   CompressArgs csa{}, hca{};

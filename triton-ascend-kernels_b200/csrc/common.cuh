@@ -145,6 +145,23 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
   }
 }
 
+// Last sequence s with offs[s] <= slot (offs: per-sequence slot offsets, num_seqs + 1
+// entries), skipping empty sequences that share the offset.
+__device__ __forceinline__ int find_slot_seq(const int32_t* offs, int num_seqs, int64_t slot) {
+  int lo = 0, hi = num_seqs - 1, ans = 0;
+  while (lo <= hi) {
+    const int mid = (lo + hi) >> 1;
+    if (offs[mid] <= slot) {
+      ans = mid;
+      lo = mid + 1;
+    } else {
+      hi = mid - 1;
+    }
+  }
+  while (ans + 1 < num_seqs && offs[ans + 1] <= slot) ++ans;
+  return ans;
+}
+
 // ----------------------------------------------------------------------------
 // TMA (tensor) loads and bulk copies, plain (no multicast)
 // ----------------------------------------------------------------------------

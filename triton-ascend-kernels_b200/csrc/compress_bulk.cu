@@ -1,0 +1,287 @@
+// KV compression (CSA windows of two strides, HCA windows of one) streamed
+// through shared memory by bulk copies: the pooling of compress_kv_overlap
+// (CSA:9-69) and compress_kv_simple (HCA:9-69) for rows that come from a TND
+// tensor or straight from a paged cache (the page gather of the decode wrappers,
+// CSA:225-253 and HCA:204-230, fused into the pooling).  Plain mean only (the
+// reference's pooling); gated pooling stays on compress_stream_kernel.
+//
+// Work split.  A persistent grid (about four CTAs per SM in all) gives each
+// CTA an equal run of consecutive slots; the rows those slots pool (plus the
+// one-stride halo of the run's last CSA window) stream through a ring of
+// shared-memory stages, each stage a chunk of CH rows of one sequence.  The
+// last warp is the producer: one cp.async.bulk per row and per tensor (K row, V
+// row: plain copies of D*2 bytes, so any page layout whose strides keep rows
+// 16-byte aligned works, and no tensor map is needed) into a stage as soon as
+// every consumer warp has released it, completing on the stage's mbarrier, so
+// block-table loads and copy issue never stall the consumers.  Every consumer
+// thread owns one 16-byte vector (8 elements) of the [K | V] row, adds
+// the chunk's rows into the current stride-sized block, and writes a slot as
+// soon as its last block completes (a CSA slot is block i + block i+1).
+// With V a view of K (MLA latent caches) the caller passes no V and pools K
+// once.
+//
+// Waits are mbarrier waits bounded in time; a timed-out wait records a device
+// error and the waiting warp leaves its loop (the producer waits, bounded, for
+// the copies it issued before it exits).
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tak {
+
+namespace cb {
+constexpr int kMaxStages = 16;
+constexpr int kRingBytes = 48 * 1024;  // four CTAs per SM
+constexpr int kChunkBytes = 8 * 1024;  // rows per chunk: ~8 KB, between 8 and 32 rows
+}  // namespace cb
+
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// The segment of a CTA's slot run that lies in one sequence, and the rows it
+// pools: slots [i0, i1) of sequence s, rows [r, r_end) (r advances chunk by chunk).
+struct BulkSeg {
+  int64_t slot, seg_end;
+  int s, i0, i1, L, r, r_end;
+  int64_t tok0;
+};
+
+template <int WIN_BLOCKS>
+__device__ __forceinline__ void bulk_seg_open(BulkSeg& g, const CompressArgs& a, int64_t gend) {
+  const bool paged = a.cu_seqlens == nullptr;
+  while (g.s + 1 < a.num_seqs && a.comp_offsets[g.s + 1] <= g.slot) ++g.s;
+  g.seg_end = min(gend, static_cast<int64_t>(a.comp_offsets[g.s + 1]));
+  g.i0 = static_cast<int>(g.slot - a.comp_offsets[g.s]);
+  g.i1 = static_cast<int>(g.seg_end - a.comp_offsets[g.s]);
+  g.L = paged ? a.context_lens[g.s] : (a.cu_seqlens[g.s + 1] - a.cu_seqlens[g.s]);
+  g.tok0 = paged ? 0 : a.cu_seqlens[g.s];
+  g.r = g.i0 * a.stride;
+  g.r_end = min((g.i1 + WIN_BLOCKS - 1) * a.stride, g.L);
+}
+
+// Move past a chunk of `ch` rows; opens the next segment when this one is done.
+// Returns false when the run is exhausted.
+template <int WIN_BLOCKS>
+__device__ __forceinline__ bool bulk_seg_next(BulkSeg& g, const CompressArgs& a, int64_t gend, int ch) {
+  g.r += ch;
+  if (g.r < g.r_end) return true;
+  g.slot = g.seg_end;
+  if (g.slot >= gend) return false;
+  bulk_seg_open<WIN_BLOCKS>(g, a, gend);
+  return true;
+}
+
+template <typename T, int WIN_BLOCKS>
+__global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a, int slots_per_cta, int ch,
+                                                            int nst) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int nk = a.head_dim / 8, nv = a.head_dim_v / 8;
+  const int ncw = (nk + nv + 31) / 32;  // consumer warps; warp ncw is the producer
+  const uint32_t kbytes = nk * 16, vbytes = nv * 16, row_bytes = kbytes + vbytes;
+  const uint32_t stage_bytes = row_bytes * ch;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * stage_bytes);
+  uint64_t* empty = full + nst;
+  const int h = blockIdx.y;
+  const int j = threadIdx.x, warp = j >> 5, lane = j & 31;
+  const bool paged = a.cu_seqlens == nullptr;
+  const int m = a.stride;
+  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * slots_per_cta;
+  const int64_t gend = min(g0 + slots_per_cta, a.num_compressed);
+  if (g0 >= gend) return;
+
+  if (j == 0) {
+    for (int i = 0; i < nst; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], ncw);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  BulkSeg cur_seg;
+  cur_seg.slot = g0;
+  cur_seg.s = find_slot_seq(a.comp_offsets, a.num_seqs, g0);
+  bulk_seg_open<WIN_BLOCKS>(cur_seg, a, gend);
+
+  if (warp == ncw) {
+    // ---------------- producer: chunk q -> stage q % nst ----------------
+    BulkSeg& pc = cur_seg;
+    const T* kb = reinterpret_cast<const T*>(a.k);
+    const T* vb = reinterpret_cast<const T*>(a.v);
+    int issued = 0;
+    for (bool more = true; more; ++issued) {
+      const int st = issued % nst;
+      if (issued >= nst && !mbar_wait(&empty[st], ((issued / nst) - 1) & 1)) break;
+      const int n = min(ch, pc.r_end - pc.r);
+      uint8_t* dst = smem + st * stage_bytes;
+      if (lane == 0) mbar_arrive_expect_tx(&full[st], n * row_bytes);
+      __syncwarp();
+      if (lane < n) {
+        const int r = pc.r + lane;
+        int64_t ko, vo;
+        if (paged) {
+          const int64_t page = a.block_tables[pc.s * a.sbt[0] + (r / a.block_size) * a.sbt[1]];
+          const int64_t off = r % a.block_size;
+          ko = page * a.sk[0] + h * a.sk[1] + off * a.sk[2];
+          vo = page * a.sv[0] + h * a.sv[1] + off * a.sv[2];
+        } else {
+          ko = (pc.tok0 + r) * a.sk[0] + h * a.sk[1];
+          vo = (pc.tok0 + r) * a.sv[0] + h * a.sv[1];
+        }
+        bulk_copy_g2s(dst + lane * row_bytes, kb + ko, kbytes, &full[st]);
+        if (vbytes) bulk_copy_g2s(dst + lane * row_bytes + kbytes, vb + vo, vbytes, &full[st]);
+      }
+      more = bulk_seg_next<WIN_BLOCKS>(pc, a, gend, ch);
+    }
+    // leave no copy in flight into this CTA's shared memory: the last phase of
+    // every stage used has landed (bounded waits)
+    if (lane == 0)
+      for (int q = max(0, issued - nst); q < issued; ++q) mbar_wait(&full[q % nst], (q / nst) & 1);
+    return;
+  }
+
+  // ---------------- consumers: thread j owns 16-byte vector j of the [K | V] row ----------------
+  const bool active = j < nk + nv;
+  const bool is_k = j < nk;
+  const int d0 = (is_k ? j : j - nk) * 8;
+  const int64_t* so = is_k ? a.sck : a.scv;
+  const int64_t so0 = so[0];
+  T* const dst_base = reinterpret_cast<T*>(is_k ? a.ck : a.cv) + h * so[1] + d0;
+  const float inv_full = 1.f / static_cast<float>(WIN_BLOCKS * m);
+  BulkSeg& cc = cur_seg;
+  T* obase = dst_base + static_cast<int64_t>(a.comp_offsets[cc.s]) * so0;
+  float prev[8], cur[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) prev[e] = cur[e] = 0.f;
+  int blk = cc.i0;                              // block being accumulated
+  int blk_end = min((blk + 1) * m, cc.r_end);  // row after its last row
+  auto store = [&](int emit, const float* o) {
+    if (!active) return;
+    uint4 q;
+    q.x = Elem<T>::pack2(o[0], o[1]);
+    q.y = Elem<T>::pack2(o[2], o[3]);
+    q.z = Elem<T>::pack2(o[4], o[5]);
+    q.w = Elem<T>::pack2(o[6], o[7]);
+    __stcg(reinterpret_cast<uint4*>(obase + emit * so0), q);
+  };
+  for (int q = 0, more = 1; more; ++q) {
+    const int st = q % nst;
+    if (!mbar_wait(&full[st], (q / nst) & 1)) break;
+    const int n = min(ch, cc.r_end - cc.r);
+    const uint8_t* src = smem + st * stage_bytes + j * 16;
+    for (int k = 0; k < n; ++k) {
+      if (active) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src + k * row_bytes);
+        const uint32_t* pw = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f2 = Elem<T>::unpack2(pw[e]);
+          cur[2 * e] += f2.x;
+          cur[2 * e + 1] += f2.y;
+        }
+      }
+      if (cc.r + k + 1 == blk_end) {
+        // block `blk` is complete: emit the slot it finishes
+        const int emit = WIN_BLOCKS == 1 ? blk : blk - 1;
+        if (emit >= cc.i0 && emit < cc.i1) {
+          const int wr0 = emit * m;
+          const float inv =
+              wr0 + WIN_BLOCKS * m <= cc.L ? inv_full : 1.f / static_cast<float>(cc.L - wr0);
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = (cur[e] + (WIN_BLOCKS == 2 ? prev[e] : 0.f)) * inv;
+          store(emit, o);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          prev[e] = cur[e];
+          cur[e] = 0.f;
+        }
+        ++blk;
+        blk_end = min((blk + 1) * m, cc.r_end);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+    const bool seg_done = cc.r + ch >= cc.r_end;
+    if (seg_done) {
+      // CSA: the last slot's window ends at the sequence end (block i1 may not exist)
+      if (WIN_BLOCKS == 2 && cc.i1 * m >= cc.L && cc.i1 - 1 >= cc.i0 && cc.i1 - 1 == blk - 1) {
+        const int emit = cc.i1 - 1;
+        const float inv = 1.f / static_cast<float>(cc.L - emit * m);
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = prev[e] * inv;
+        store(emit, o);
+      }
+    }
+    more = bulk_seg_next<WIN_BLOCKS>(cc, a, gend, ch);
+    if (seg_done && more) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) prev[e] = cur[e] = 0.f;
+      blk = cc.i0;
+      blk_end = min((blk + 1) * m, cc.r_end);
+      obase = dst_base + static_cast<int64_t>(a.comp_offsets[cc.s]) * so0;
+    }
+  }
+}
+
+// Takes plain-mean pooling of 16-bit rows whose every stride is a multiple of
+// 8 elements, with windows of one or two strides.  Returns false (nothing
+// launched) for anything else.
+template <typename T>
+static bool compress_bulk_typed(const CompressArgs& a, cudaStream_t st, int* err) {
+  const bool paged = a.cu_seqlens == nullptr;
+  if (a.gate) return false;
+  if (!(a.window == a.stride || a.window == 2 * a.stride)) return false;
+  const int nk = a.head_dim / 8, nv = a.head_dim_v / 8;
+  if (a.head_dim % 8 || a.head_dim_v % 8 || nk + nv > 256 || nk == 0) return false;
+  const int nd = paged ? 4 : 3;
+  if (a.sk[nd - 1] != 1 || (a.v && a.sv[nd - 1] != 1)) return false;
+  for (int i = 0; i < nd - 1; ++i) {
+    if (a.sk[i] % 8) return false;
+    if (a.v && a.sv[i] % 8) return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v)) & 15) return false;
+  if (a.sck[2] != 1 || a.sck[0] % 8 || a.sck[1] % 8 || (reinterpret_cast<uintptr_t>(a.ck) & 15)) return false;
+  if (a.cv && (a.scv[2] != 1 || a.scv[0] % 8 || a.scv[1] % 8 || (reinterpret_cast<uintptr_t>(a.cv) & 15)))
+    return false;
+  const int row_bytes = (nk + nv) * 16;
+  const int ch = max(8, min(32, cb::kChunkBytes / row_bytes));
+  const int nst = max(2, min(cb::kMaxStages, cb::kRingBytes / (row_bytes * ch)));
+  const int smem = nst * row_bytes * ch + nst * 16;
+  const int threads = ((nk + nv + 31) / 32 + 1) * 32;  // consumer warps + the producer warp
+  // equal slot runs: ~4 CTAs per SM over all KV heads
+  const int64_t target = static_cast<int64_t>(num_sms()) * 4;
+  const int64_t per_head = std::max<int64_t>(1, (target + a.num_kv_heads - 1) / a.num_kv_heads);
+  const int64_t spc64 = (a.num_compressed + per_head - 1) / per_head;
+  if (spc64 > 2147483647) return false;
+  const int spc = static_cast<int>(spc64);
+  const unsigned ctas = static_cast<unsigned>((a.num_compressed + spc - 1) / spc);
+  const dim3 grid(ctas, a.num_kv_heads);
+  if (a.window == a.stride) {
+    auto kern = compress_bulk_kernel<T, 1>;
+    if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
+    kern<<<grid, threads, smem, st>>>(a, spc, ch, nst);
+  } else {
+    auto kern = compress_bulk_kernel<T, 2>;
+    if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
+    kern<<<grid, threads, smem, st>>>(a, spc, ch, nst);
+  }
+  *err = 0;
+  return true;
+}
+
+bool compress_bulk_launch(const CompressArgs& a, cudaStream_t st, int* err) {
+  *err = 0;
+  if (a.dtype == kBF16) return compress_bulk_typed<__nv_bfloat16>(a, st, err);
+  if (a.dtype == kF16) return compress_bulk_typed<__half>(a, st, err);
+  return false;
+}
+
+}  // namespace tak

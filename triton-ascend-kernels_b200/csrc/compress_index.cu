@@ -24,22 +24,6 @@
 
 namespace tak {
 
-__device__ __forceinline__ int find_slot_seq(const int32_t* offs, int num_seqs, int64_t slot) {
-  int lo = 0, hi = num_seqs - 1, ans = 0;
-  while (lo <= hi) {
-    const int mid = (lo + hi) >> 1;
-    if (offs[mid] <= slot) {
-      ans = mid;
-      lo = mid + 1;
-    } else {
-      hi = mid - 1;
-    }
-  }
-  // skip empty sequences that share the same offset
-  while (ans + 1 < num_seqs && offs[ans + 1] <= slot) ++ans;
-  return ans;
-}
-
 template <typename T, int VEC>
 __global__ void compress_kernel(const CompressArgs a) {
   const int64_t slot = blockIdx.x;
@@ -392,8 +376,9 @@ static int compress_typed(const CompressArgs& a, cudaStream_t st) {
   const bool paged = a.cu_seqlens == nullptr;
   const int64_t kd = paged ? a.sk[3] : a.sk[2];
   const int64_t vd = paged ? a.sv[3] : a.sv[2];
-  bool vec = sizeof(T) == 2 && kd == 1 && vd == 1 && a.sck[2] == 1 && a.scv[2] == 1 && a.head_dim % 8 == 0 &&
-             a.head_dim_v % 8 == 0;
+  // no V (K-only pooling): its strides are all 0 and never used
+  bool vec = sizeof(T) == 2 && kd == 1 && (vd == 1 || !a.v) && a.sck[2] == 1 && (a.scv[2] == 1 || !a.cv) &&
+             a.head_dim % 8 == 0 && a.head_dim_v % 8 == 0;
   const int64_t* strides[] = {a.sk, a.sv};
   for (const int64_t* s4 : strides)
     for (int i = 0; i < (paged ? 3 : 2); ++i) vec = vec && (s4[i] % 8 == 0);
@@ -402,6 +387,8 @@ static int compress_typed(const CompressArgs& a, cudaStream_t st) {
         ((reinterpret_cast<uintptr_t>(a.ck) | reinterpret_cast<uintptr_t>(a.cv)) & 15) == 0;
   dim3 grid(static_cast<unsigned>(a.num_compressed), a.num_kv_heads);
   if constexpr (sizeof(T) == 2) {
+    int err = 0;
+    if (compress_bulk_launch(a, st, &err)) return err;
     const int threads = (a.head_dim + a.head_dim_v) / 8;
     if (vec && threads <= 128 && a.window == a.stride && a.stride >= 64) {
       compress_split_kernel<T><<<grid, 512, 0, st>>>(a);

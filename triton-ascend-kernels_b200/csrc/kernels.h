@@ -104,6 +104,11 @@ struct CompressArgs {
   int64_t total_rows;  // TND token count (only the fused CSA + HCA launch reads it)
 };
 int compress_launch(const CompressArgs& a, cudaStream_t st);
+// Plain-mean pooling streamed through shared memory by bulk copies (16-bit
+// rows, strides in multiples of 8 elements, window = stride or 2 * stride, no
+// gate).  Returns false, launching nothing, for other shapes; *err is the
+// launch status when it returns true.
+bool compress_bulk_launch(const CompressArgs& a, cudaStream_t st, int* err);
 // CSA (window 2m, stride m) and HCA (window = stride = m') pooling of the same
 // K/V/gate in one pass; falls back to two compress_launch calls for shapes the
 // fused kernel does not take.

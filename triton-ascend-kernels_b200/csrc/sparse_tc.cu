@@ -71,13 +71,13 @@ struct SparseTcParams {
   const int32_t* ctx_lens;
   int64_t ncomp;
   int num_win, block_size;
-  int decode;
 };
 
 // Validity of slot c holding index j (decode: by slot position, SA:151-171 for
 // the window slots [0, num_win) and SA:197-210 for the compressed ones).
+template <bool DECODE>
 __device__ __forceinline__ bool sp_slot_valid(const SparseTcParams& p, int c, int64_t j, int ctx) {
-  if (!p.decode) return j >= 0 && j < p.kv_rows;
+  if (!DECODE) return j >= 0 && j < p.kv_rows;
   return c < p.num_win ? (j >= 0 && j < ctx) : (j >= ctx && j - ctx < p.ncomp);
 }
 
@@ -127,7 +127,7 @@ struct SpLayout {
   static constexpr int TMEM_COLS = DV <= 128 ? 128 : (DV <= 256 ? 256 : 512);
 };
 
-template <typename T, int DQK, int DV, bool SHARED>
+template <typename T, int DQK, int DV, bool SHARED, bool DECODE>
 __global__ void __launch_bounds__(288, 1)
     sparse_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const SparseTcParams p) {
   using L = SpLayout<DQK, DV, SHARED>;
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(288, 1)
   const int n_tiles = (p.k_topk + BN - 1) / BN;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int32_t* idx_row = p.topk + static_cast<int64_t>(t) * p.stk0;
-  const int ctx = p.decode ? p.ctx_lens[t] : 0;
+  const int ctx = DECODE ? p.ctx_lens[t] : 0;
 
   if (tid == 0) {
     mbar_init(q_full, 1);
@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(288, 1)
     }
     const T* kb = reinterpret_cast<const T*>(p.k);
     const T* vb = reinterpret_cast<const T*>(p.v);
-    const int32_t* bt_row = p.decode ? p.bt + static_cast<int64_t>(t) * p.sbt0 : nullptr;
+    const int32_t* bt_row = DECODE ? p.bt + static_cast<int64_t>(t) * p.sbt0 : nullptr;
     // K (and V unless shared) row addresses of this thread's 4 slots of tile j; null = masked
     auto load_rows = [&](int j, const T** kr, const T** vr) {
 #pragma unroll
@@ -201,8 +201,8 @@ __global__ void __launch_bounds__(288, 1)
         const int64_t r = (j < n_tiles && c < p.k_topk) ? static_cast<int64_t>(idx_row[c * p.stk1]) : -1;
         kr[g] = nullptr;
         vr[g] = nullptr;
-        if (!(j < n_tiles && c < p.k_topk) || !sp_slot_valid(p, c, r, ctx)) continue;
-        if (!p.decode) {
+        if (!(j < n_tiles && c < p.k_topk) || !sp_slot_valid<DECODE>(p, c, r, ctx)) continue;
+        if (!DECODE) {
           kr[g] = kb + r * p.k_s0 + kvh * p.k_sh;
           if (!SHARED) vr[g] = vb + r * p.v_s0 + kvh * p.v_sh;
         } else if (c < p.num_win) {  // window slot: logical position -> page, row in page (SA:160-166)
@@ -335,8 +335,8 @@ __global__ void __launch_bounds__(288, 1)
       const int c0 = j * BN + lane, c1 = c0 + 32;
       const int64_t r0 = c0 < p.k_topk ? static_cast<int64_t>(idx_row[c0 * p.stk1]) : -1;
       const int64_t r1 = c1 < p.k_topk ? static_cast<int64_t>(idx_row[c1 * p.stk1]) : -1;
-      const uint32_t lo = __ballot_sync(0xffffffffu, c0 < p.k_topk && sp_slot_valid(p, c0, r0, ctx));
-      const uint32_t hi_m = __ballot_sync(0xffffffffu, c1 < p.k_topk && sp_slot_valid(p, c1, r1, ctx));
+      const uint32_t lo = __ballot_sync(0xffffffffu, c0 < p.k_topk && sp_slot_valid<DECODE>(p, c0, r0, ctx));
+      const uint32_t hi_m = __ballot_sync(0xffffffffu, c1 < p.k_topk && sp_slot_valid<DECODE>(p, c1, r1, ctx));
       return hi ? hi_m : lo;
     };
     uint32_t vnext = n_tiles > 0 ? tile_mask(0) : 0u;
@@ -450,8 +450,8 @@ static int encode_rows_map(CUtensorMap* m, const void* base, int64_t rows, int64
   return encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base, dims, strides, box, es, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <typename T, int DQK, int DV, bool SHARED>
-static int launch_sparse_tc(const SparseArgs& a, cudaStream_t st) {
+template <typename T, int DQK, int DV, bool SHARED, bool DECODE>
+static int launch_sparse_tc_mode(const SparseArgs& a, cudaStream_t st) {
   using L = SpLayout<DQK, DV, SHARED>;
   const int G = a.num_q_heads / a.num_kv_heads;
   CUtensorMap mq;
@@ -479,7 +479,6 @@ static int launch_sparse_tc(const SparseArgs& a, cudaStream_t st) {
   p.k_sh = a.sk[1];
   p.v_s0 = a.sv[0];
   p.v_sh = a.sv[1];
-  p.decode = a.decode;
   if (a.decode) {
     p.k_sr = a.sk[2];
     p.v_sr = a.sv[2];
@@ -497,11 +496,17 @@ static int launch_sparse_tc(const SparseArgs& a, cudaStream_t st) {
     p.num_win = a.num_win;
     p.block_size = a.block_size;
   }
-  auto kern = sparse_tc_kernel<T, DQK, DV, SHARED>;
+  auto kern = sparse_tc_kernel<T, DQK, DV, SHARED, DECODE>;
   if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::SMEM)) return r;
   dim3 grid(a.num_tokens, a.num_kv_heads * p.head_chunks);
   kern<<<grid, 288, L::SMEM, st>>>(mq, p);
   return 0;
+}
+
+template <typename T, int DQK, int DV, bool SHARED>
+static int launch_sparse_tc(const SparseArgs& a, cudaStream_t st) {
+  return a.decode ? launch_sparse_tc_mode<T, DQK, DV, SHARED, true>(a, st)
+                  : launch_sparse_tc_mode<T, DQK, DV, SHARED, false>(a, st);
 }
 
 // A gathered row source takes 16-byte copies: base 16-byte aligned, innermost
