@@ -226,6 +226,21 @@ int tak_build_decode_topk_idxs(const int32_t* context_lens, const int32_t* comp_
                                void* stream);
 
 /*
+ * comp_offsets [num_seqs + 1] (int32, device) computed on the device from
+ * per-sequence lengths (is_cu = 0: lens[num_seqs], e.g. context_lens) or from
+ * cu_seqlens (is_cu = 1: lens[num_seqs + 1]): max(1, ceil(L / stride)) slots
+ * per non-empty sequence, cumulative -- the comp_offsets of
+ * compress_kv_overlap / compress_kv_simple (attention/csa.py:38-59,
+ * attention/hca.py:38-59), which the reference builds on the host.  With
+ * capacity >= 0 the offsets are clamped to it and a larger total records
+ * device error 3 (tak_read_device_error); the pooling, index and attention
+ * entry points then touch no slot beyond the capacity.  Lets the decode
+ * wrappers run without reading lengths on the host (an addition).
+ */
+int tak_comp_offsets(const int32_t* lens, int64_t num_seqs, int is_cu, int64_t stride, int64_t capacity,
+                     int32_t* comp_offsets, void* stream);
+
+/*
  * CSA Lightning indexer: columns [n_win, n_win + top_k) of the index rows.
  * Replaces the indexer of build_csa_topk_idxs (attention/csa.py:119-164) and
  * of csa_decode_forward (:278-302).  Prefill (cu_seqlens != NULL): one row per

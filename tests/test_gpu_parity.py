@@ -582,6 +582,49 @@ def test_csa_hca_decode_latent512(dtype):
     close(out, ref, TOL16)
 
 
+@pytest.mark.parametrize("kind", ["csa", "hca"])
+def test_decode_wrappers_graph_capture(kind):
+    """csa/hca_decode_forward with max_compressed read nothing on the host, so
+    one call is captured in a CUDA graph; replays after the context lengths
+    and queries change in place (within the block tables' reach) equal the
+    oracle each time."""
+    ctx0 = [300, 1030, 7, 129, 64]
+    P, n_win = 64, 64
+    _, kc, _, _, _, bt, _, cl, sink = _sparse_decode_case(ctx0, 64, 1, 512, 512, P, 1, 1, 1, torch.bfloat16, 67,
+                                                          shared_latent=True)
+    g = torch.Generator().manual_seed(68)
+    q = torch.randn(len(ctx0), 64, 512, generator=g).to(DEV, torch.bfloat16)
+    stride = 4 if kind == "csa" else 128
+    cap = sum(max(1, -(-c // stride)) for c in (1030,) * len(ctx0))  # every request at the longest context
+
+    def run():
+        if kind == "csa":
+            return CSA.csa_decode_forward(q, kc, kc, bt, cl, n_win, 32, 4, P, sink, max_compressed=cap)
+        return HCA.hca_decode_forward(q, kc, kc, bt, cl, n_win, 128, P, sink, max_compressed=cap)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        run()  # warm-up outside the capture (kernel attributes, library load)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = run()
+    for new_ctx in (ctx0, [5, 1000, 64, 0, 1], [299, 1, 7, 128, 63]):
+        cl.copy_(torch.tensor(new_ctx, dtype=torch.int32))
+        q.copy_(torch.randn(len(ctx0), 64, 512, generator=g))
+        graph.replay()
+        torch.cuda.synchronize()
+        if kind == "csa":
+            ref, _, _ = O.csa_decode_forward(npy(q), npy(kc), npy(kc), bt.cpu(), cl.cpu(), n_win, 32, 4, P,
+                                             sink.cpu(), "bfloat16")
+        else:
+            ref, _, _ = O.hca_decode_forward(npy(q), npy(kc), npy(kc), bt.cpu(), cl.cpu(), n_win, 128, P,
+                                             sink.cpu(), "bfloat16")
+        close(out, ref, TOL16)
+    del graph
+
+
 @pytest.mark.parametrize("stride,window", [(4, 8), (128, 128), (3, 6)])
 def test_compress_paged_k_only_latent(stride, window):
     """Paged pooling with V a prefix view of K (576-dim latent + rope rows, V =

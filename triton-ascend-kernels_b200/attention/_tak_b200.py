@@ -48,6 +48,7 @@ _SIGS = {
     "tak_build_window_idxs": ([_P, _I64, _I64, _I64, _P, _I64, _P], _I32),
     "tak_build_hca_topk_idxs": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P], _I32),
     "tak_build_decode_topk_idxs": ([_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P], _I32),
+    "tak_comp_offsets": ([_P, _I64, _I32, _I64, _I64, _P, _P], _I32),
     "tak_csa_indexer_topk": ([_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                               _P, _I64, _I32, _P], _I32),
 }
@@ -222,28 +223,54 @@ def is_prefix_view(v, k):
             and v.shape[:-1] == k.shape[:-1] and v.shape[-1] <= k.shape[-1] and v.dtype == k.dtype)
 
 
-def compress_paged(k_cache, v_cache, block_tables, context_lens, block_size, stride, window):
+def comp_offsets_device(lens, stride, capacity=-1, is_cu=False):
+    """comp_offsets [n + 1] int32 computed on the device from int32 lengths
+    (or cu_seqlens, is_cu=True); no host read.  capacity >= 0 clamps the
+    offsets and records device error 3 when the total exceeds it."""
+    n = lens.shape[0] - (1 if is_cu else 0)
+    offs = torch.empty(n + 1, dtype=torch.int32, device=lens.device)
+    check(lib().tak_comp_offsets(ptr(lens), n, 1 if is_cu else 0, stride, capacity, ptr(offs), stream_of(lens)))
+    return offs
+
+
+def max_slots_per_seq(block_tables, block_size, stride):
+    """Slots of the longest context a block table can address (a host bound
+    from shapes: max(1, ceil(max_blocks * P / stride)))."""
+    return max(1, -(-int(block_tables.shape[1]) * int(block_size) // stride))
+
+
+def compress_paged(k_cache, v_cache, block_tables, context_lens, block_size, stride, window, capacity=None):
     """Pool each sequence's first context_lens[s] rows straight out of a paged
     cache (fuses the reference's page gather, CSA:225-256 / HCA:204-232).
     When v_cache is a prefix view of k_cache (MLA latent caches) K is pooled
     once and compressed_v is the same view of compressed_k.
-    Returns (compressed_k, compressed_v, comp_offsets[int32, device], lengths[host])."""
+    capacity=None sizes the outputs exactly (one device->host read of
+    context_lens); an int sizes them [capacity, ...] and computes the offsets
+    on the device, with no host read (CUDA-graph capturable; a total above
+    the capacity records device error 3).
+    Returns (compressed_k, compressed_v, comp_offsets[int32, device],
+    lengths[host] or None, comp_offsets[host] or None)."""
     dev = k_cache.device
     bt = as_i32(block_tables, dev)
     cl = as_i32(context_lens, dev)
-    lens = cl.cpu().tolist()
-    offs = comp_offsets_host(lens, stride)
-    nc = offs[-1]
+    if capacity is None:
+        lens = cl.cpu().tolist()
+        offs = comp_offsets_host(lens, stride)
+        nc = offs[-1]
+        offs_t = torch.tensor(offs, dtype=torch.int32).to(dev)
+    else:
+        lens = offs = None
+        nc = int(capacity)
+        offs_t = comp_offsets_device(cl, stride, nc)
     hkv = k_cache.shape[1]
     k_only = is_prefix_view(v_cache, k_cache)
     ck = k_cache.new_empty((nc, hkv, k_cache.shape[3]))
     cv = ck[..., :v_cache.shape[3]] if k_only else v_cache.new_empty((nc, hkv, v_cache.shape[3]))
-    offs_t = torch.tensor(offs, dtype=torch.int32).to(dev)
     if nc:
         vv, cvv = (None, None) if k_only else (v_cache, cv)
         check(lib().tak_compress_kv_paged(
             ptr(k_cache), strides(k_cache), ptr(vv), None if vv is None else strides(vv), None, None, ptr(bt),
-            strides(bt), ptr(cl), block_size, ptr(offs_t), len(lens), nc, ptr(ck), strides(ck), ptr(cvv),
+            strides(bt), ptr(cl), block_size, ptr(offs_t), cl.shape[0], nc, ptr(ck), strides(ck), ptr(cvv),
             None if cvv is None else strides(cvv), hkv, k_cache.shape[3], 0 if k_only else v_cache.shape[3],
             stride, window, dtype_code(k_cache), stream_of(k_cache)))
     return ck, cv, offs_t, lens, offs

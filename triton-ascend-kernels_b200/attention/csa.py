@@ -84,15 +84,22 @@ def csa_prefill_forward(q, k, v, cu_seqlens, n_win, top_k, m, attn_sink=None, *,
 
 
 def csa_decode_forward(q, k_cache, v_cache, block_tables, context_lens,
-                       n_win, top_k, m, block_size=16, attn_sink=None, *, return_lse=False):
+                       n_win, top_k, m, block_size=16, attn_sink=None, *, return_lse=False, max_compressed=None):
     """CSA decode forward (paged layout): compress each sequence's context
-    straight from the pages, index with the Lightning indexer, sparse decode."""
+    straight from the pages, index with the Lightning indexer, sparse decode.
+
+    max_compressed (keyword-only addition): None sizes the compressed rows
+    exactly from context_lens read on the host (as the reference does); an
+    int bound on sum_s max(1, ceil(ctx_s / m)) keeps everything on the device
+    (no host read, so the call can be captured in a CUDA graph); a total above
+    it records device error 3."""
     _t.require_cuda(q, k_cache, v_cache)
     dev = q.device
     num_seqs, num_q_heads, head_dim = q.shape
     num_kv_heads = k_cache.shape[1]
-    ck, cv, offs, lens, offs_h = _t.compress_paged(k_cache, v_cache, block_tables, context_lens, block_size, m, 2 * m)
-    if sum(lens) == 0:
+    ck, cv, offs, lens, offs_h = _t.compress_paged(k_cache, v_cache, block_tables, context_lens, block_size, m, 2 * m,
+                                                   capacity=max_compressed)
+    if lens is not None and sum(lens) == 0:
         out = torch.zeros_like(q)
         if return_lse:
             return out, torch.full((num_seqs, num_q_heads), float("-inf"), device=dev)
@@ -103,7 +110,10 @@ def csa_decode_forward(q, k_cache, v_cache, block_tables, context_lens,
     L = _t.lib()
     st = _t.stream_of(q)
     _t.check(L.tak_build_decode_topk_idxs(_t.ptr(cl), _t.ptr(offs), num_seqs, n_win, top_k, 0, _t.ptr(idx), K, st))
-    mc = max((offs_h[i + 1] - offs_h[i] for i in range(num_seqs)), default=0)
+    if offs_h is not None:
+        mc = max((offs_h[i + 1] - offs_h[i] for i in range(num_seqs)), default=0)
+    else:
+        mc = min(_t.max_slots_per_seq(block_tables, block_size, m), ck.shape[0])
     if top_k and mc:
         _t.check(L.tak_csa_indexer_topk(
             _t.ptr(q), _t.strides(q), _t.ptr(ck), _t.strides(ck), None, _t.ptr(cl), _t.ptr(offs), num_seqs,

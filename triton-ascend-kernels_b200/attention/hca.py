@@ -69,21 +69,28 @@ def hca_prefill_forward(q, k, v, cu_seqlens, n_win, m_prime, attn_sink=None, *, 
 
 
 def hca_decode_forward(q, k_cache, v_cache, block_tables, context_lens,
-                       n_win, m_prime, block_size=16, attn_sink=None, *, return_lse=False):
+                       n_win, m_prime, block_size=16, attn_sink=None, *, return_lse=False, max_compressed=None):
     """HCA decode forward (paged layout): compress each sequence's context
-    straight from the pages, index (window + all causal slots), sparse decode."""
+    straight from the pages, index (window + all causal slots), sparse decode.
+
+    max_compressed (keyword-only addition): as for csa_decode_forward; with an
+    int the compressed columns of the index rows are sized from the block
+    table's reach, max(1, ceil(max_blocks * P / m')), the extra columns -1."""
     _t.require_cuda(q, k_cache, v_cache)
     dev = q.device
     num_seqs, num_q_heads, _ = q.shape
     ck, cv, offs, lens, offs_h = _t.compress_paged(k_cache, v_cache, block_tables, context_lens, block_size,
-                                                   m_prime, m_prime)
-    if sum(lens) == 0:
+                                                   m_prime, m_prime, capacity=max_compressed)
+    if lens is not None and sum(lens) == 0:
         out = torch.zeros_like(q)
         if return_lse:
             return out, torch.full((num_seqs, num_q_heads), float("-inf"), device=dev)
         return out
     cl = _t.as_i32(context_lens, dev)
-    mx = _max_n_comp(lens, offs_h, m_prime)
+    if lens is not None:
+        mx = _max_n_comp(lens, offs_h, m_prime)
+    else:
+        mx = min(_t.max_slots_per_seq(block_tables, block_size, m_prime), ck.shape[0])
     K = n_win + mx
     idx = torch.empty((num_seqs, K), dtype=torch.int32, device=dev)
     _t.check(_t.lib().tak_build_decode_topk_idxs(_t.ptr(cl), _t.ptr(offs), num_seqs, n_win, mx, m_prime,

@@ -450,6 +450,16 @@ int tak_build_hca_topk_idxs(const int32_t* cu_seqlens, const int32_t* comp_offse
   return r ? r : check_launch("hca idxs");
 }
 
+int tak_comp_offsets(const int32_t* lens, int64_t num_seqs, int is_cu, int64_t stride, int64_t capacity,
+                     int32_t* comp_offsets, void* stream) {
+  TAK_REQUIRE(num_seqs >= 0 && num_seqs <= 2147483647 && stride > 0 && stride <= 2147483647,
+              "comp offsets: bad num_seqs / stride");
+  TAK_REQUIRE(comp_offsets && (num_seqs == 0 || lens), "comp offsets: null pointer");
+  const int r = comp_offsets_launch(lens, static_cast<int>(num_seqs), is_cu ? 1 : 0, static_cast<int>(stride),
+                                    capacity, comp_offsets, static_cast<cudaStream_t>(stream));
+  return r ? r : check_launch("comp offsets");
+}
+
 int tak_build_decode_topk_idxs(const int32_t* context_lens, const int32_t* comp_offsets, int64_t num_seqs,
                                int64_t n_win, int64_t n_comp_cols, int64_t m_prime, int32_t* out, int64_t ld,
                                void* stream) {

@@ -43,6 +43,15 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
       : "memory");
 }
 
+// c += (a0, a1) as one packed fp32 pair add (same rounding as two adds).
+__device__ __forceinline__ void cb_add2(float& c0, float& c1, float a0, float a1) {
+  uint64_t c = (static_cast<uint64_t>(__float_as_uint(c1)) << 32) | __float_as_uint(c0);
+  const uint64_t aa = (static_cast<uint64_t>(__float_as_uint(a1)) << 32) | __float_as_uint(a0);
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(c) : "l"(aa));
+  c0 = __uint_as_float(static_cast<uint32_t>(c));
+  c1 = __uint_as_float(static_cast<uint32_t>(c >> 32));
+}
+
 // The segment of a CTA's slot run that lies in one sequence, and the rows it
 // pools: slots [i0, i1) of sequence s, rows [r, r_end) (r advances chunk by chunk).
 struct BulkSeg {
@@ -77,8 +86,7 @@ __device__ __forceinline__ bool bulk_seg_next(BulkSeg& g, const CompressArgs& a,
 }
 
 template <typename T, int WIN_BLOCKS>
-__global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a, int slots_per_cta, int ch,
-                                                            int nst) {
+__global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a, int ch, int nst) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int nk = a.head_dim / 8, nv = a.head_dim_v / 8;
   const int ncw = (nk + nv + 31) / 32;  // consumer warps; warp ncw is the producer
@@ -90,8 +98,11 @@ __global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a
   const int j = threadIdx.x, warp = j >> 5, lane = j & 31;
   const bool paged = a.cu_seqlens == nullptr;
   const int m = a.stride;
+  // equal runs of the slots that exist (num_compressed may be a capacity above the total)
+  const int64_t total = min(a.num_compressed, static_cast<int64_t>(a.comp_offsets[a.num_seqs]));
+  const int64_t slots_per_cta = (total + gridDim.x - 1) / gridDim.x;
   const int64_t g0 = static_cast<int64_t>(blockIdx.x) * slots_per_cta;
-  const int64_t gend = min(g0 + slots_per_cta, a.num_compressed);
+  const int64_t gend = min(g0 + slots_per_cta, total);
   if (g0 >= gend) return;
 
   if (j == 0) {
@@ -154,48 +165,66 @@ __global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a
   T* const dst_base = reinterpret_cast<T*>(is_k ? a.ck : a.cv) + h * so[1] + d0;
   const float inv_full = 1.f / static_cast<float>(WIN_BLOCKS * m);
   BulkSeg& cc = cur_seg;
-  T* obase = dst_base + static_cast<int64_t>(a.comp_offsets[cc.s]) * so0;
   float prev[8], cur[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) prev[e] = cur[e] = 0.f;
   int blk = cc.i0;                              // block being accumulated
   int blk_end = min((blk + 1) * m, cc.r_end);  // row after its last row
-  auto store = [&](int emit, const float* o) {
+  // where the slot finished by block `blk` goes (slot blk, or blk - 1 for CSA)
+  T* optr = dst_base + (static_cast<int64_t>(a.comp_offsets[cc.s]) + blk - (WIN_BLOCKS - 1)) * so0;
+  auto emit_slot = [&](int emit, const float* acc2, const float* acc1) {
+    const int wr0 = emit * m;
+    const float inv = wr0 + WIN_BLOCKS * m <= cc.L ? inv_full : 1.f / static_cast<float>(cc.L - wr0);
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = (acc2 ? acc2[e] + acc1[e] : acc1[e]) * inv;
     if (!active) return;
     uint4 q;
     q.x = Elem<T>::pack2(o[0], o[1]);
     q.y = Elem<T>::pack2(o[2], o[3]);
     q.z = Elem<T>::pack2(o[4], o[5]);
     q.w = Elem<T>::pack2(o[6], o[7]);
-    __stcg(reinterpret_cast<uint4*>(obase + emit * so0), q);
+    __stcg(reinterpret_cast<uint4*>(dst_base + (static_cast<int64_t>(a.comp_offsets[cc.s]) + emit) * so0), q);
   };
+  // idle lanes (past the row's last vector) read vector 0 and store nothing
+  const uint32_t col_off = active ? j * 16 : 0;
   for (int q = 0, more = 1; more; ++q) {
     const int st = q % nst;
     if (!mbar_wait(&full[st], (q / nst) & 1)) break;
     const int n = min(ch, cc.r_end - cc.r);
-    const uint8_t* src = smem + st * stage_bytes + j * 16;
-    for (int k = 0; k < n; ++k) {
-      if (active) {
+    const uint8_t* src = smem + st * stage_bytes + col_off;
+    int k = 0;
+    while (k < n) {
+      // rows of this chunk that belong to block `blk`
+      const int kend = min(n, blk_end - cc.r);
+#pragma unroll 4
+      for (; k < kend; ++k) {
         const uint4 u = *reinterpret_cast<const uint4*>(src + k * row_bytes);
         const uint32_t* pw = reinterpret_cast<const uint32_t*>(&u);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f2 = Elem<T>::unpack2(pw[e]);
-          cur[2 * e] += f2.x;
-          cur[2 * e + 1] += f2.y;
+          cb_add2(cur[2 * e], cur[2 * e + 1], f2.x, f2.y);
         }
       }
-      if (cc.r + k + 1 == blk_end) {
+      if (cc.r + kend == blk_end) {
         // block `blk` is complete: emit the slot it finishes
         const int emit = WIN_BLOCKS == 1 ? blk : blk - 1;
         if (emit >= cc.i0 && emit < cc.i1) {
           const int wr0 = emit * m;
-          const float inv =
-              wr0 + WIN_BLOCKS * m <= cc.L ? inv_full : 1.f / static_cast<float>(cc.L - wr0);
-          float o[8];
+          if (wr0 + WIN_BLOCKS * m <= cc.L && active) {
+            float o[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) o[e] = (cur[e] + (WIN_BLOCKS == 2 ? prev[e] : 0.f)) * inv;
-          store(emit, o);
+            for (int e = 0; e < 8; ++e) o[e] = (WIN_BLOCKS == 2 ? prev[e] + cur[e] : cur[e]) * inv_full;
+            uint4 qv;
+            qv.x = Elem<T>::pack2(o[0], o[1]);
+            qv.y = Elem<T>::pack2(o[2], o[3]);
+            qv.z = Elem<T>::pack2(o[4], o[5]);
+            qv.w = Elem<T>::pack2(o[6], o[7]);
+            __stcg(reinterpret_cast<uint4*>(optr), qv);
+          } else if (wr0 + WIN_BLOCKS * m > cc.L) {
+            emit_slot(emit, WIN_BLOCKS == 2 ? prev : nullptr, cur);
+          }
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -204,29 +233,22 @@ __global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a
         }
         ++blk;
         blk_end = min((blk + 1) * m, cc.r_end);
+        optr += so0;
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
     const bool seg_done = cc.r + ch >= cc.r_end;
-    if (seg_done) {
-      // CSA: the last slot's window ends at the sequence end (block i1 may not exist)
-      if (WIN_BLOCKS == 2 && cc.i1 * m >= cc.L && cc.i1 - 1 >= cc.i0 && cc.i1 - 1 == blk - 1) {
-        const int emit = cc.i1 - 1;
-        const float inv = 1.f / static_cast<float>(cc.L - emit * m);
-        float o[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = prev[e] * inv;
-        store(emit, o);
-      }
-    }
+    // CSA: the last slot's window ends at the sequence end (block i1 may not exist)
+    if (seg_done && WIN_BLOCKS == 2 && cc.i1 * m >= cc.L && cc.i1 - 1 >= cc.i0 && cc.i1 - 1 == blk - 1)
+      emit_slot(cc.i1 - 1, nullptr, prev);
     more = bulk_seg_next<WIN_BLOCKS>(cc, a, gend, ch);
     if (seg_done && more) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) prev[e] = cur[e] = 0.f;
       blk = cc.i0;
       blk_end = min((blk + 1) * m, cc.r_end);
-      obase = dst_base + static_cast<int64_t>(a.comp_offsets[cc.s]) * so0;
+      optr = dst_base + (static_cast<int64_t>(a.comp_offsets[cc.s]) + blk - (WIN_BLOCKS - 1)) * so0;
     }
   }
 }
@@ -256,22 +278,20 @@ static bool compress_bulk_typed(const CompressArgs& a, cudaStream_t st, int* err
   const int nst = max(2, min(cb::kMaxStages, cb::kRingBytes / (row_bytes * ch)));
   const int smem = nst * row_bytes * ch + nst * 16;
   const int threads = ((nk + nv + 31) / 32 + 1) * 32;  // consumer warps + the producer warp
-  // equal slot runs: ~4 CTAs per SM over all KV heads
+  // ~4 CTAs per SM over all KV heads; each CTA takes an equal run of the slots
+  // (sized on the device from the offsets)
   const int64_t target = static_cast<int64_t>(num_sms()) * 4;
   const int64_t per_head = std::max<int64_t>(1, (target + a.num_kv_heads - 1) / a.num_kv_heads);
-  const int64_t spc64 = (a.num_compressed + per_head - 1) / per_head;
-  if (spc64 > 2147483647) return false;
-  const int spc = static_cast<int>(spc64);
-  const unsigned ctas = static_cast<unsigned>((a.num_compressed + spc - 1) / spc);
+  const unsigned ctas = static_cast<unsigned>(std::min<int64_t>(per_head, a.num_compressed));
   const dim3 grid(ctas, a.num_kv_heads);
   if (a.window == a.stride) {
     auto kern = compress_bulk_kernel<T, 1>;
     if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
-    kern<<<grid, threads, smem, st>>>(a, spc, ch, nst);
+    kern<<<grid, threads, smem, st>>>(a, ch, nst);
   } else {
     auto kern = compress_bulk_kernel<T, 2>;
     if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
-    kern<<<grid, threads, smem, st>>>(a, spc, ch, nst);
+    kern<<<grid, threads, smem, st>>>(a, ch, nst);
   }
   *err = 0;
   return true;

@@ -28,6 +28,7 @@ template <typename T, int VEC>
 __global__ void compress_kernel(const CompressArgs a) {
   const int64_t slot = blockIdx.x;
   const int h = blockIdx.y;
+  if (slot >= a.comp_offsets[a.num_seqs]) return;  // num_compressed may be a capacity
   const int s = find_slot_seq(a.comp_offsets, a.num_seqs, slot);
   const int i = static_cast<int>(slot - a.comp_offsets[s]);
   const bool paged = a.cu_seqlens == nullptr;
@@ -108,6 +109,7 @@ __global__ void compress_kernel(const CompressArgs a) {
 template <typename T, int WIN_BLOCKS>
 __global__ void __launch_bounds__(128) compress_stream_kernel(const CompressArgs a, int slots_per_cta) {
   const int64_t g0 = static_cast<int64_t>(blockIdx.x) * slots_per_cta;
+  const int64_t total = min(a.num_compressed, static_cast<int64_t>(a.comp_offsets[a.num_seqs]));
   const int h = blockIdx.y;
   const int nk = a.head_dim / 8, nv = a.head_dim_v / 8;
   const int j = threadIdx.x;
@@ -120,7 +122,8 @@ __global__ void __launch_bounds__(128) compress_stream_kernel(const CompressArgs
   const int64_t* so = is_k ? a.sck : a.scv;
   const bool paged = a.cu_seqlens == nullptr;
   const int m = a.stride;
-  const int64_t gend = min(g0 + slots_per_cta, a.num_compressed);
+  const int64_t gend = min(g0 + slots_per_cta, total);
+  if (g0 >= gend) return;
   int64_t slot = g0;
   int s = find_slot_seq(a.comp_offsets, a.num_seqs, slot);
   while (slot < gend) {
@@ -263,6 +266,7 @@ __global__ void __launch_bounds__(512) compress_split_kernel(const CompressArgs 
   __shared__ float gpart[RG][2];
   const int64_t slot = blockIdx.x;
   const int h = blockIdx.y;
+  if (slot >= a.comp_offsets[a.num_seqs]) return;  // num_compressed may be a capacity
   const int s = find_slot_seq(a.comp_offsets, a.num_seqs, slot);
   const int i = static_cast<int>(slot - a.comp_offsets[s]);
   const bool paged = a.cu_seqlens == nullptr;
@@ -512,6 +516,49 @@ __global__ void decode_idxs_kernel(const int32_t* context_lens, const int32_t* o
   }
 }
 
+// Slot offsets from lengths (is_cu = 0) or cu_seqlens (is_cu = 1): max(1,
+// ceil(L / stride)) slots per non-empty sequence, cumulative (CSA:38-59).  One
+// CTA: each thread scans a contiguous run of sequences, the run totals are
+// scanned in shared memory.  A total above `capacity` (>= 0) records error 3
+// and the offsets are clamped to the capacity.
+__global__ void __launch_bounds__(1024) comp_offsets_kernel(const int32_t* lens, int num_seqs, int is_cu,
+                                                            int stride, int64_t capacity, int32_t* offs) {
+  __shared__ int64_t part[1024];
+  const int t = threadIdx.x, nt = blockDim.x;
+  const int per = (num_seqs + nt - 1) / nt;
+  const int b0 = min(t * per, num_seqs), b1 = min(b0 + per, num_seqs);
+  auto slots = [&](int s) -> int64_t {
+    const int64_t L = is_cu ? static_cast<int64_t>(lens[s + 1]) - lens[s] : lens[s];
+    return L > 0 ? ((L + stride - 1) / stride > 1 ? (L + stride - 1) / stride : int64_t{1}) : int64_t{0};
+  };
+  int64_t sum = 0;
+  for (int s = b0; s < b1; ++s) sum += slots(s);
+  part[t] = sum;
+  __syncthreads();
+  for (int off = 1; off < nt; off <<= 1) {  // inclusive Hillis-Steele scan of the run totals
+    const int64_t v = t >= off ? part[t - off] : 0;
+    __syncthreads();
+    part[t] += v;
+    __syncthreads();
+  }
+  int64_t run = part[t] - sum;  // exclusive prefix of this thread's run
+  // past the capacity the offsets stop growing: later sequences get no slots,
+  // so nothing that reads these offsets touches a row beyond the capacity
+  const int64_t cap = capacity >= 0 ? capacity : INT64_MAX;
+  if (t == 0) offs[0] = 0;
+  for (int s = b0; s < b1; ++s) {
+    run += slots(s);
+    offs[s + 1] = static_cast<int32_t>(min(run, cap));
+  }
+  if (t == nt - 1 && part[t] > cap) record_error(3);
+}
+
+int comp_offsets_launch(const int32_t* lens, int num_seqs, int is_cu, int stride, int64_t capacity, int32_t* offs,
+                        cudaStream_t st) {
+  comp_offsets_kernel<<<1, 1024, 0, st>>>(lens, num_seqs, is_cu, stride, capacity, offs);
+  return 0;
+}
+
 int token_to_seq_launch(const int32_t* cu, int num_seqs, int total_tokens, int32_t* out, cudaStream_t st) {
   if (total_tokens <= 0) return 0;
   token_to_seq_kernel<<<(total_tokens + 255) / 256, 256, 0, st>>>(cu, num_seqs, total_tokens, out);
@@ -574,7 +621,8 @@ __global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
     pos = row - a.cu_seqlens[s];
   }
   const int c0 = a.comp_offsets[s];
-  const int nc = a.comp_offsets[s + 1] - c0;
+  // the score array holds max_comp_per_seq slots (a bound the caller derives)
+  const int nc = min(a.comp_offsets[s + 1] - c0, a.max_comp_per_seq);
   if (nc <= 0) return;
   const int k_sel = min(a.top_k, nc);
   // slot i is causal iff i*m < pos  <=>  i < ceil(pos/m)

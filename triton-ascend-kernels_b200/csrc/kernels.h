@@ -119,6 +119,8 @@ int window_idxs_launch(const int32_t* cu, int num_seqs, int total_tokens, int n_
                        cudaStream_t st);
 int hca_idxs_launch(const int32_t* cu, const int32_t* offs, int num_seqs, int total_tokens, int n_win,
                     int max_n_comp, int m_prime, int32_t* out, int64_t ld, cudaStream_t st);
+int comp_offsets_launch(const int32_t* lens, int num_seqs, int is_cu, int stride, int64_t capacity, int32_t* offs,
+                        cudaStream_t st);
 int decode_idxs_launch(const int32_t* context_lens, const int32_t* offs, int num_seqs, int n_win, int n_comp_cols,
                        int m_prime, int32_t* out, int64_t ld, cudaStream_t st);
 
