@@ -523,11 +523,14 @@ def test_index_builders_bit_exact():
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("top_k", [16, 48, 300])
-def test_csa_indexer_bit_exact(dtype, top_k):
-    """Lightning indexer on 5 sequences, 512-dim compressed keys; ties and
-    fewer-than-k causal slots included (short sequences).  top_k 16 takes the
-    repeated-argmax selection, 48 and 300 the sorted one (up to 525 slots)."""
-    lens = [3, 40, 200, 513, 2100]
+@pytest.mark.parametrize("rows", ["many", "few"])
+def test_csa_indexer_bit_exact(dtype, top_k, rows):
+    """Lightning indexer on 512-dim compressed keys; ties and fewer-than-k
+    causal slots included (short sequences).  top_k 16 takes the
+    repeated-argmax selection, 48 and 300 the sorted one (up to 525 slots).
+    "many" (2856 query rows) runs the 256-thread kernel, "few" (271 rows, under
+    two per SM) the 512-thread one."""
+    lens = [3, 40, 200, 513, 2100] if rows == "many" else [3, 8, 260]
     Tn = sum(lens)
     g = torch.Generator().manual_seed(41)
     q = torch.randn(Tn, 4, 512, generator=g).to(DEV, dtype)

@@ -604,11 +604,15 @@ __device__ __forceinline__ float round_to_t<float>(float x) {
 constexpr int kIdxRoundsMax = 16;
 constexpr int kIdxSortMax = 8192;
 
-template <typename T>
-__global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
+// NT threads; SPW slots scored per warp step (all their loads in flight at
+// once): 256 x 4 when there are many rows, 512 x 8 for the few long rows of
+// decode, where one CTA per row leaves most SMs idle and the score loads are
+// latency-bound.
+template <typename T, int NT, int SPW>
+__global__ void __launch_bounds__(NT) csa_indexer_kernel(const IndexerArgs a) {
   extern __shared__ float sc[];  // [max_comp_per_seq] scores, -inf once taken
-  __shared__ float red_v[8];
-  __shared__ int red_i[8];
+  __shared__ float red_v[NT / 32];
+  __shared__ int red_i[NT / 32];
   const int row = blockIdx.x;
   const bool decode = a.cu_seqlens == nullptr;
   int s, pos;
@@ -637,7 +641,7 @@ __global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
   }
   if (vec) {
     // 16-byte loads: lane l owns dims [8l, 8l+8) and [8l+256, 8l+264); a warp
-    // scores 4 slots per step with all their loads in flight at once
+    // scores SPW slots per step with all their loads in flight at once
     if constexpr (sizeof(T) == 2) {
       const int nch = a.head_dim / 8;
       float qv[16];
@@ -654,10 +658,10 @@ __global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
           qv[c * 8 + 2 * e + 1] = f.y;
         }
       }
-      for (int i0 = warp * 4; i0 < n_valid; i0 += nwarps * 4) {
-        uint4 kv[4][2];
+      for (int i0 = warp * SPW; i0 < n_valid; i0 += nwarps * SPW) {
+        uint4 kv[SPW][2];
 #pragma unroll
-        for (int si = 0; si < 4; ++si)
+        for (int si = 0; si < SPW; ++si)
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const int ch = lane + 32 * c;
@@ -665,9 +669,9 @@ __global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
             if (i0 + si < n_valid && ch < nch)
               kv[si][c] = *reinterpret_cast<const uint4*>(ck + static_cast<int64_t>(i0 + si) * a.sck[0] + ch * 8);
           }
-        float acc[4];
+        float acc[SPW];
 #pragma unroll
-        for (int si = 0; si < 4; ++si) {
+        for (int si = 0; si < SPW; ++si) {
           float sacc = 0.f;
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
@@ -681,9 +685,12 @@ __global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
           }
           acc[si] = warp_sum(sacc);
         }
-        // lanes 0-3 write the four scores (a select, not a register-indexed load)
-        const float mine = lane == 0 ? acc[0] : lane == 1 ? acc[1] : lane == 2 ? acc[2] : acc[3];
-        if (lane < 4 && i0 + lane < n_valid) sc[i0 + lane] = round_to_t<T>(mine);
+        // lanes 0..SPW-1 write the scores (selects, not a register-indexed load)
+        float mine = acc[0];
+#pragma unroll
+        for (int si = 1; si < SPW; ++si)
+          if (lane == si) mine = acc[si];
+        if (lane < SPW && i0 + lane < n_valid) sc[i0 + lane] = round_to_t<T>(mine);
       }
     }
   } else {
@@ -720,16 +727,16 @@ __global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
     while (n_pad < n_valid) n_pad <<= 1;
     // scores live in the first n_valid floats of the same buffer: read them
     // all before any key is written
-    float own[kIdxSortMax / 256];
+    float own[kIdxSortMax / NT];
 #pragma unroll
-    for (int u = 0; u < kIdxSortMax / 256; ++u) {
-      const int i = threadIdx.x + u * 256;
+    for (int u = 0; u < kIdxSortMax / NT; ++u) {
+      const int i = threadIdx.x + u * NT;
       own[u] = i < n_valid ? sc[i] + 0.f : 0.f;
     }
     __syncthreads();
 #pragma unroll
-    for (int u = 0; u < kIdxSortMax / 256; ++u) {
-      const int i = threadIdx.x + u * 256;
+    for (int u = 0; u < kIdxSortMax / NT; ++u) {
+      const int i = threadIdx.x + u * NT;
       if (i < n_pad) {
         unsigned long long kv = 0ull;
         if (i < n_valid) {
@@ -806,6 +813,14 @@ __global__ void __launch_bounds__(256) csa_indexer_kernel(const IndexerArgs a) {
   for (int r = n_pick + threadIdx.x; r < k_sel; r += blockDim.x) out[r] = static_cast<int32_t>(base + r);
 }
 
+template <typename T, int NT, int SPW>
+static int launch_indexer(const IndexerArgs& a, int rows, size_t smem, cudaStream_t st) {
+  auto kern = csa_indexer_kernel<T, NT, SPW>;
+  if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), static_cast<int>(smem))) return r;
+  kern<<<rows, NT, smem, st>>>(a);
+  return 0;
+}
+
 int csa_indexer_launch(const IndexerArgs& a, cudaStream_t st) {
   const int rows = a.cu_seqlens ? a.total_tokens : a.num_seqs;
   if (rows <= 0) return 0;
@@ -818,23 +833,13 @@ int csa_indexer_launch(const IndexerArgs& a, cudaStream_t st) {
     if (n_pad * sizeof(unsigned long long) > smem) smem = n_pad * sizeof(unsigned long long);
   }
   if (smem > 200 * 1024) return set_error(2, "csa indexer: more than 51200 compressed slots in one sequence");
-  if (a.dtype == kBF16) {
-    if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(csa_indexer_kernel<__nv_bfloat16>),
-                                       static_cast<int>(smem)))
-      return r;
-    csa_indexer_kernel<__nv_bfloat16><<<rows, 256, smem, st>>>(a);
-  } else if (a.dtype == kF16) {
-    if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(csa_indexer_kernel<__half>),
-                                       static_cast<int>(smem)))
-      return r;
-    csa_indexer_kernel<__half><<<rows, 256, smem, st>>>(a);
-  } else {
-    if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(csa_indexer_kernel<float>),
-                                       static_cast<int>(smem)))
-      return r;
-    csa_indexer_kernel<float><<<rows, 256, smem, st>>>(a);
-  }
-  return 0;
+  // few rows (decode): wider CTAs with more score loads in flight
+  const bool wide = rows < 2 * num_sms();
+  if (a.dtype == kBF16) return wide ? launch_indexer<__nv_bfloat16, 512, 8>(a, rows, smem, st)
+                                    : launch_indexer<__nv_bfloat16, 256, 4>(a, rows, smem, st);
+  if (a.dtype == kF16) return wide ? launch_indexer<__half, 512, 8>(a, rows, smem, st)
+                                   : launch_indexer<__half, 256, 4>(a, rows, smem, st);
+  return launch_indexer<float, 256, 4>(a, rows, smem, st);
 }
 
 }  // namespace tak
