@@ -737,6 +737,125 @@ class CsaWL(Workload):
                       "latent, window 128 + top-512), fp32")
 
 
+def csa_decode_bytes(ctx, n_idx, B, H, D, n_win, top_k, m):
+    """Algorithmic HBM bytes of one CSA decode step over a latent cache (V a
+    view of K, pooled once): every context row read once by the pooling, the
+    compressed rows written, read once by the indexer and gathered once per
+    valid index by the attention, plus q, out and the index rows."""
+    slots = sum(max(1, -(-int(c) // m)) for c in ctx if c > 0)
+    row = D * 2
+    return (int(sum(int(c) for c in ctx)) * row + slots * row        # pooling: read context, write slots
+            + B * row + slots * row + B * (n_win + top_k) * 4         # indexer: last-head q, slot rows, idx
+            + n_idx * row + 2 * B * H * D * 2 + B * (n_win + top_k) * 4)  # attention: gathered rows, q, out, idx
+
+
+class CsaDecodeWL(Workload):
+    name, unit, bound, peak_key, kernel = "csa_decode", "GB/s", "hbm", "hbm_gbs", "compress_bulk_kernel"
+    desc = ("CSA decode forward over a paged latent cache: 64 requests (one query token each, 64 query heads), "
+            "one 512-dim latent KV head used as K and V, bf16, contexts uniform in [1, 8192], page 128; "
+            "pooling straight from the pages (m = 4, 8-token windows), Lightning-indexer top-512 + 128-token "
+            "window, sparse attention with sinks")
+
+    def setup(self, rank, device):
+        import csa as CSA
+        self.CSA = CSA
+        B, H, D, P = (16 if SMALL else 64), 64, 512, 128
+        self.P, self.n_win, self.top_k, self.m = P, 128, 512, 4
+        g = torch.Generator().manual_seed(71 + rank)
+        ctx = torch.randint(1, 8192 + 1, (B,), generator=g, dtype=torch.int64).to(torch.int32)
+        maxb = 8192 // P
+        pool = B * maxb
+        perm = torch.randperm(pool, generator=g).to(torch.int32)
+        bt = torch.zeros(B, maxb, dtype=torch.int32)
+        i = 0
+        for b in range(B):
+            n = (int(ctx[b]) + P - 1) // P
+            bt[b, :n] = perm[i:i + n]
+            i += n
+        gd = torch.Generator(device=device).manual_seed(72 + rank)
+        self.kc = torch.empty(pool, 1, P, D, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.q = torch.empty(B, H, D, device=device, dtype=torch.bfloat16).normal_(generator=gd)
+        self.sink = torch.empty(H, device=device).normal_(generator=gd)
+        self.bt, self.ctx = bt.to(device), ctx.to(device)
+        self.ctx_h, self.bt_h = ctx, bt
+        # capacity of the compressed rows: the exact slot count, known from the
+        # request lengths when the batch is formed (no host read per step)
+        self.cap = sum(max(1, -(-int(c) // self.m)) for c in ctx.tolist())
+        # valid attention indices: window positions < ctx plus every causal compressed slot picked (<= top_k)
+        n_idx = sum(min(int(c), self.n_win) + min(-(-int(c) // self.m), self.top_k) for c in ctx.tolist())
+        self.work = csa_decode_bytes(ctx.tolist(), n_idx, B, H, D, self.n_win, self.top_k, self.m)
+        self.launches = 5  # slot offsets, pooling, window rows, indexer, sparse attention
+        self.config = {"requests": B, "context_tokens": int(ctx.sum()), "compressed_slots": self.cap,
+                       "valid_indices": n_idx,
+                       "l2_policy": "the 269 MB of context rows streamed by the pooling exceed L2",
+                       "timed_path": "csa_decode_forward(max_compressed=slots) per step: no host read, "
+                                     "captured as one CUDA graph"}
+
+    def step(self):
+        return self.CSA.csa_decode_forward(self.q, self.kc, self.kc, self.bt, self.ctx, self.n_win, self.top_k,
+                                           self.m, self.P, self.sink, max_compressed=self.cap)
+
+    def phases(self, device):
+        """Device time of each stage of one eager forward (ms)."""
+        CSA, T = self.CSA, self.CSA._t
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        torch.cuda.synchronize(device)
+        ev[0].record()
+        ck, cv, offs, _, _ = T.compress_paged(self.kc, self.kc, self.bt, self.ctx, self.P, self.m, 2 * self.m,
+                                              capacity=self.cap)
+        ev[1].record()
+        B = self.q.shape[0]
+        K = self.n_win + self.top_k
+        idx = torch.empty((B, K), dtype=torch.int32, device=device)
+        L, st = T.lib(), T.stream_of(self.q)
+        T.check(L.tak_build_decode_topk_idxs(T.ptr(self.ctx), T.ptr(offs), B, self.n_win, self.top_k, 0,
+                                             T.ptr(idx), K, st))
+        mc = min(T.max_slots_per_seq(self.bt, self.P, self.m), ck.shape[0])
+        T.check(L.tak_csa_indexer_topk(T.ptr(self.q), T.strides(self.q), T.ptr(ck), T.strides(ck), None,
+                                       T.ptr(self.ctx), T.ptr(offs), B, B, 64, 1, 512, self.n_win, self.top_k,
+                                       self.m, mc, T.ptr(idx), K, T.dtype_code(self.q), st))
+        ev[2].record()
+        CSA.sparse_attn_decode(self.q, self.kc, self.kc, ck, cv, self.bt, idx, self.ctx, self.n_win, self.P,
+                               self.sink)
+        ev[3].record()
+        torch.cuda.synchronize(device)
+        return {"pool_ms": round(ev[0].elapsed_time(ev[1]), 3), "index_ms": round(ev[1].elapsed_time(ev[2]), 3),
+                "attention_ms": round(ev[2].elapsed_time(ev[3]), 3)}
+
+    def e2e_setup(self):
+        # per step a serving engine sends the new queries, lengths and block tables
+        self.hq = self.q.cpu().pin_memory()
+        self.hctx, self.hbt = self.ctx_h.pin_memory(), self.bt_h.pin_memory()
+        self.hout = torch.empty(self.q.shape, dtype=torch.bfloat16).pin_memory()
+        self.dq, self.dctx, self.dbt = (torch.empty_like(t) for t in (self.q, self.ctx, self.bt))
+        return (sum(t.numel() * t.element_size() for t in (self.hq, self.hctx, self.hbt)),
+                self.hout.numel() * self.hout.element_size())
+
+    def e2e_step(self):
+        for d, h in ((self.dq, self.hq), (self.dctx, self.hctx), (self.dbt, self.hbt)):
+            d.copy_(h, non_blocking=True)
+        # the reference-compatible call: compressed rows sized from the lengths read on the host
+        o = self.CSA.csa_decode_forward(self.dq, self.kc, self.kc, self.dbt, self.dctx, self.n_win, self.top_k,
+                                        self.m, self.P, self.sink)
+        self.hout.copy_(o, non_blocking=True)
+
+    def reference_sample(self):
+        from oracle import attention_oracle as O
+        g = np.random.default_rng(5)
+        B, H, D, P = 2, 64, 512, 128
+        ctx = np.array([4096, 4096], dtype=np.int32)
+        maxb = 4096 // P
+        bt = np.arange(B * maxb, dtype=np.int32).reshape(B, maxb)
+        kc = g.standard_normal((B * maxb, 1, P, D), dtype=np.float32)
+        q = g.standard_normal((B, H, D), dtype=np.float32)
+        sink = g.standard_normal(H).astype(np.float32)
+        n_idx = sum(min(int(c), 128) + min(-(-int(c) // 4), 512) for c in ctx)
+        work = csa_decode_bytes(ctx.tolist(), n_idx, B, H, D, 128, 512, 4)
+        return (lambda: O.csa_decode_forward(q, kc, kc, bt, ctx, 128, 512, 4, P, sink),
+                work, "two 4096-token requests through the numpy oracle's csa_decode_forward (64 heads, 512-dim "
+                      "latent, page 128, window 128 + top-512), fp32")
+
+
 class MixedWL(Workload):
     """One GPU's share of the box-scale mixed serving step: the global problem
     at N GPUs is N/8 of the 8-GPU step (N x 32 prefill sequences, N x 512
@@ -865,7 +984,8 @@ class MixedWL(Workload):
         return one, work, "one causal 1024-token prefill + decode of 2 requests (4096, 65536 tokens), numpy oracle"
 
 
-WORKLOADS = {"prefill": PrefillWL, "sparse": SparseWL, "compress": CompressWL, "csa": CsaWL, "mixed": MixedWL}
+WORKLOADS = {"prefill": PrefillWL, "sparse": SparseWL, "compress": CompressWL, "csa": CsaWL, "mixed": MixedWL,
+             "csa_decode": CsaDecodeWL}
 SMALL = False  # --small: a reduced instance of the workload (for ncu captures)
 
 

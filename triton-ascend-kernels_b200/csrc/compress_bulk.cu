@@ -8,19 +8,22 @@
 // Work split.  A persistent grid (about four CTAs per SM in all) gives each
 // CTA an equal run of consecutive slots; the rows those slots pool (plus the
 // one-stride halo of the run's last CSA window) stream through a ring of
-// shared-memory stages, each stage a chunk of CH rows of one sequence.  The
-// last warp is the producer: one cp.async.bulk per row and per tensor (K row, V
-// row: plain copies of D*2 bytes, so any page layout whose strides keep rows
-// 16-byte aligned works, and no tensor map is needed) into a stage as soon as
-// every consumer warp has released it, completing on the stage's mbarrier, so
-// block-table loads and copy issue never stall the consumers.  Every consumer
+// shared-memory stages, each stage a chunk of CH rows of one sequence (its K
+// rows, then its V rows).  The last warp is the producer: plain cp.async.bulk
+// copies (no tensor map; any layout whose strides keep rows 16-byte aligned),
+// one per page piece and tensor when rows are contiguous within a page, else
+// one per row, into a stage as soon as every consumer warp has released it,
+// completing on the stage's mbarrier, so block-table loads and copy issue never
+// stall the consumers.  Every consumer
 // thread owns one 16-byte vector (8 elements) of the [K | V] row, adds
 // the chunk's rows into the current stride-sized block, and writes a slot as
 // soon as its last block completes (a CSA slot is block i + block i+1).
 // With V a view of K (MLA latent caches) the caller passes no V and pools K
 // once.
 //
-// Waits are mbarrier waits bounded in time; a timed-out wait records a device
+// Waits are mbarrier waits that suspend the warp in hardware between probes
+// (spinning warps would take issue slots from the consumers) and are bounded
+// in time; a timed-out wait records a device
 // error and the waiting warp leaves its loop (the producer waits, bounded, for
 // the copies it issued before it exits).
 #include <algorithm>
@@ -41,15 +44,6 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
-}
-
-// c += (a0, a1) as one packed fp32 pair add (same rounding as two adds).
-__device__ __forceinline__ void cb_add2(float& c0, float& c1, float a0, float a1) {
-  uint64_t c = (static_cast<uint64_t>(__float_as_uint(c1)) << 32) | __float_as_uint(c0);
-  const uint64_t aa = (static_cast<uint64_t>(__float_as_uint(a1)) << 32) | __float_as_uint(a0);
-  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(c) : "l"(aa));
-  c0 = __uint_as_float(static_cast<uint32_t>(c));
-  c1 = __uint_as_float(static_cast<uint32_t>(c >> 32));
 }
 
 // The segment of a CTA's slot run that lies in one sequence, and the rows it
@@ -85,8 +79,12 @@ __device__ __forceinline__ bool bulk_seg_next(BulkSeg& g, const CompressArgs& a,
   return true;
 }
 
-template <typename T, int WIN_BLOCKS>
-__global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a, int ch, int nst) {
+// MC: the stride m when it is known at compile time (4: the reference's CSA),
+// else 0.  With MC > 0 and chunks a multiple of MC rows, every chunk starts on
+// a block boundary and whole blocks are summed in fresh registers and emitted
+// with no per-row tests.
+template <typename T, int WIN_BLOCKS, int MC>
+__global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a, int ch, int nst, int span) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int nk = a.head_dim / 8, nv = a.head_dim_v / 8;
   const int ncw = (nk + nv + 31) / 32;  // consumer warps; warp ncw is the producer
@@ -127,12 +125,40 @@ __global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a
     int issued = 0;
     for (bool more = true; more; ++issued) {
       const int st = issued % nst;
-      if (issued >= nst && !mbar_wait(&empty[st], ((issued / nst) - 1) & 1)) break;
+      if (issued >= nst && !mbar_wait_sleep(&empty[st], ((issued / nst) - 1) & 1, 2000)) break;
       const int n = min(ch, pc.r_end - pc.r);
+      // stage layout: the chunk's K rows, then its V rows
       uint8_t* dst = smem + st * stage_bytes;
+      uint8_t* vdst = dst + ch * kbytes;
       if (lane == 0) mbar_arrive_expect_tx(&full[st], n * row_bytes);
       __syncwarp();
-      if (lane < n) {
+      if (span) {
+        // rows contiguous within a page (or a sequence): one copy per page
+        // piece and tensor; lane t takes the piece in the chunk's t-th page
+        const int r0 = pc.r;
+        int a0 = r0, a1 = r0 + n;
+        int64_t ko = 0, vo = 0;
+        bool mine = lane == 0;
+        if (paged) {
+          const int pg = r0 / a.block_size + lane;
+          a0 = max(r0, pg * a.block_size);
+          a1 = min(r0 + n, (pg + 1) * a.block_size);
+          mine = a0 < a1;
+          if (mine) {
+            const int64_t page = a.block_tables[pc.s * a.sbt[0] + static_cast<int64_t>(pg) * a.sbt[1]];
+            const int64_t off = a0 - static_cast<int64_t>(pg) * a.block_size;
+            ko = page * a.sk[0] + h * a.sk[1] + off * a.sk[2];
+            vo = page * a.sv[0] + h * a.sv[1] + off * a.sv[2];
+          }
+        } else {
+          ko = (pc.tok0 + r0) * a.sk[0] + h * a.sk[1];
+          vo = (pc.tok0 + r0) * a.sv[0] + h * a.sv[1];
+        }
+        if (mine) {
+          bulk_copy_g2s(dst + (a0 - r0) * kbytes, kb + ko, (a1 - a0) * kbytes, &full[st]);
+          if (vbytes) bulk_copy_g2s(vdst + (a0 - r0) * vbytes, vb + vo, (a1 - a0) * vbytes, &full[st]);
+        }
+      } else if (lane < n) {
         const int r = pc.r + lane;
         int64_t ko, vo;
         if (paged) {
@@ -144,8 +170,8 @@ __global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a
           ko = (pc.tok0 + r) * a.sk[0] + h * a.sk[1];
           vo = (pc.tok0 + r) * a.sv[0] + h * a.sv[1];
         }
-        bulk_copy_g2s(dst + lane * row_bytes, kb + ko, kbytes, &full[st]);
-        if (vbytes) bulk_copy_g2s(dst + lane * row_bytes + kbytes, vb + vo, vbytes, &full[st]);
+        bulk_copy_g2s(dst + lane * kbytes, kb + ko, kbytes, &full[st]);
+        if (vbytes) bulk_copy_g2s(vdst + lane * vbytes, vb + vo, vbytes, &full[st]);
       }
       more = bulk_seg_next<WIN_BLOCKS>(pc, a, gend, ch);
     }
@@ -186,33 +212,32 @@ __global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a
     q.w = Elem<T>::pack2(o[6], o[7]);
     __stcg(reinterpret_cast<uint4*>(dst_base + (static_cast<int64_t>(a.comp_offsets[cc.s]) + emit) * so0), q);
   };
-  // idle lanes (past the row's last vector) read vector 0 and store nothing
-  const uint32_t col_off = active ? j * 16 : 0;
+  // this thread's vector in a stage ([K rows | V rows]) and its row pitch;
+  // idle lanes (past the row's last vector) read K vector 0 and store nothing
+  const uint32_t col_off = !active ? 0u : is_k ? j * 16u : ch * kbytes + (j - nk) * 16u;
+  const uint32_t pitch = (active && !is_k) ? vbytes : kbytes;
   for (int q = 0, more = 1; more; ++q) {
     const int st = q % nst;
-    if (!mbar_wait(&full[st], (q / nst) & 1)) break;
+    if (!mbar_wait_sleep(&full[st], (q / nst) & 1, 2000)) break;
     const int n = min(ch, cc.r_end - cc.r);
     const uint8_t* src = smem + st * stage_bytes + col_off;
-    int k = 0;
-    while (k < n) {
-      // rows of this chunk that belong to block `blk`
-      const int kend = min(n, blk_end - cc.r);
-#pragma unroll 4
-      for (; k < kend; ++k) {
-        const uint4 u = *reinterpret_cast<const uint4*>(src + k * row_bytes);
-        const uint32_t* pw = reinterpret_cast<const uint32_t*>(&u);
+    auto row_acc = [&](float* acc, int k, bool first) {
+      const uint4 u = *reinterpret_cast<const uint4*>(src + k * pitch);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f2 = Elem<T>::unpack2(pw[e]);
-          cb_add2(cur[2 * e], cur[2 * e + 1], f2.x, f2.y);
-        }
+      for (int e = 0; e < 4; ++e) {
+        const float2 f2 = Elem<T>::unpack2(w[e]);
+        acc[2 * e] = first ? f2.x : acc[2 * e] + f2.x;
+        acc[2 * e + 1] = first ? f2.y : acc[2 * e + 1] + f2.y;
       }
-      if (cc.r + kend == blk_end) {
-        // block `blk` is complete: emit the slot it finishes
-        const int emit = WIN_BLOCKS == 1 ? blk : blk - 1;
-        if (emit >= cc.i0 && emit < cc.i1) {
-          const int wr0 = emit * m;
-          if (wr0 + WIN_BLOCKS * m <= cc.L && active) {
+    };
+    auto finish_block = [&]() {
+      // block `blk` (in cur) is complete: emit the slot it finishes
+      const int emit = WIN_BLOCKS == 1 ? blk : blk - 1;
+      if (emit >= cc.i0 && emit < cc.i1) {
+        const int wr0 = emit * m;
+        if (wr0 + WIN_BLOCKS * m <= cc.L) {
+          if (active) {
             float o[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) o[e] = (WIN_BLOCKS == 2 ? prev[e] + cur[e] : cur[e]) * inv_full;
@@ -222,19 +247,37 @@ __global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a
             qv.z = Elem<T>::pack2(o[4], o[5]);
             qv.w = Elem<T>::pack2(o[6], o[7]);
             __stcg(reinterpret_cast<uint4*>(optr), qv);
-          } else if (wr0 + WIN_BLOCKS * m > cc.L) {
-            emit_slot(emit, WIN_BLOCKS == 2 ? prev : nullptr, cur);
           }
+        } else {
+          emit_slot(emit, WIN_BLOCKS == 2 ? prev : nullptr, cur);
         }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          prev[e] = cur[e];
-          cur[e] = 0.f;
-        }
-        ++blk;
-        blk_end = min((blk + 1) * m, cc.r_end);
-        optr += so0;
       }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        prev[e] = cur[e];
+        cur[e] = 0.f;
+      }
+      ++blk;
+      blk_end = min((blk + 1) * m, cc.r_end);
+      optr += so0;
+    };
+    int k = 0;
+    if (MC > 0) {
+      // whole blocks: MC rows summed straight into cur (empty at a block start)
+      for (; k + MC <= n && cc.r + k + MC == blk_end; k += MC) {
+        row_acc(cur, k, true);
+#pragma unroll
+        for (int i = 1; i < MC; ++i) row_acc(cur, k + i, false);
+        finish_block();
+      }
+    }
+    while (k < n) {
+      // rows of this chunk that belong to block `blk` (a partial block: the
+      // sequence end, or any block when MC == 0)
+      const int kend = min(n, blk_end - cc.r);
+#pragma unroll 4
+      for (; k < kend; ++k) row_acc(cur, k, false);
+      if (cc.r + kend == blk_end) finish_block();
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
@@ -284,15 +327,16 @@ static bool compress_bulk_typed(const CompressArgs& a, cudaStream_t st, int* err
   const int64_t per_head = std::max<int64_t>(1, (target + a.num_kv_heads - 1) / a.num_kv_heads);
   const unsigned ctas = static_cast<unsigned>(std::min<int64_t>(per_head, a.num_compressed));
   const dim3 grid(ctas, a.num_kv_heads);
-  if (a.window == a.stride) {
-    auto kern = compress_bulk_kernel<T, 1>;
-    if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
-    kern<<<grid, threads, smem, st>>>(a, ch, nst);
-  } else {
-    auto kern = compress_bulk_kernel<T, 2>;
-    if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
-    kern<<<grid, threads, smem, st>>>(a, ch, nst);
-  }
+  // rows whose pitch equals the copied bytes are contiguous within a page (a
+  // sequence, for TND): the producer copies page pieces instead of single rows
+  const int64_t kp = paged ? a.sk[2] : a.sk[0], vp = paged ? a.sv[2] : a.sv[0];
+  const int span = (kp * 2 == nk * 16 && (!a.v || vp * 2 == nv * 16)) ? 1 : 0;
+  void (*kern)(const CompressArgs, int, int, int);
+  const bool m4 = a.stride == 4 && ch % 4 == 0;
+  if (a.window == a.stride) kern = m4 ? compress_bulk_kernel<T, 1, 4> : compress_bulk_kernel<T, 1, 0>;
+  else kern = m4 ? compress_bulk_kernel<T, 2, 4> : compress_bulk_kernel<T, 2, 0>;
+  if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
+  kern<<<grid, threads, smem, st>>>(a, ch, nst, span);
   *err = 0;
   return true;
 }
