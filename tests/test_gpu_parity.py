@@ -521,23 +521,42 @@ def test_index_builders_bit_exact():
     np.testing.assert_array_equal(got.cpu().numpy(), O.build_hca_topk_idxs(cuq.cpu(), offs.cpu(), Tn, 16, 128))
 
 
+def _indexer_on_cores(q, ck, cuq, offs, n_win, top_k, m):
+    """build_csa_topk_idxs with the dot products on CUDA cores: the C entry
+    point without a score workspace."""
+    Tn, H, D = q.shape
+    K = n_win + top_k
+    out = torch.full((Tn, K), -1, dtype=torch.int32, device=DEV)
+    L = T.lib()
+    st = T.stream_of(q)
+    T.check(L.tak_build_window_idxs(T.ptr(cuq), cuq.numel() - 1, Tn, n_win, T.ptr(out), K, st))
+    mc = int((offs[1:] - offs[:-1]).max())
+    T.check(L.tak_csa_indexer_topk(T.ptr(q), T.strides(q), T.ptr(ck), T.strides(ck), T.ptr(cuq), None, T.ptr(offs),
+                                   cuq.numel() - 1, Tn, H, ck.shape[1], D, n_win, top_k, m, mc, T.ptr(out), K,
+                                   T.dtype_code(q), None, 0, ck.shape[0], st))
+    return out
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("top_k", [16, 48, 300])
-@pytest.mark.parametrize("rows", ["many", "few"])
+@pytest.mark.parametrize("rows", ["many", "few", "many-cores"])
 def test_csa_indexer_bit_exact(dtype, top_k, rows):
     """Lightning indexer on 512-dim compressed keys; ties and fewer-than-k
     causal slots included (short sequences).  top_k 16 takes the
     repeated-argmax selection, 48 and 300 the sorted one (up to 525 slots).
-    "many" (2856 query rows) runs the 256-thread kernel, "few" (271 rows, under
-    two per SM) the 512-thread one."""
-    lens = [3, 40, 200, 513, 2100] if rows == "many" else [3, 8, 260]
+    "many" (2856 query rows) and "few" (271 rows: the 512-thread selection)
+    score on the tensor cores; "many-cores" scores each row on CUDA cores."""
+    lens = [3, 40, 200, 513, 2100] if rows != "few" else [3, 8, 260]
     Tn = sum(lens)
     g = torch.Generator().manual_seed(41)
     q = torch.randn(Tn, 4, 512, generator=g).to(DEV, dtype)
     k = torch.randn(Tn, 1, 512, generator=g).to(DEV, dtype)
     cuq = _cu_t(lens)
     ck, cv, offs = CSA.compress_kv_overlap(k, k, cuq, 4)
-    got = CSA.build_csa_topk_idxs(q, ck, cuq, offs, 8, top_k, 4)
+    if rows == "many-cores":
+        got = _indexer_on_cores(q, ck, cuq, offs, 8, top_k, 4)
+    else:
+        got = CSA.build_csa_topk_idxs(q, ck, cuq, offs, 8, top_k, 4)
     name = "bfloat16" if dtype == torch.bfloat16 else "float16"
     ref = O.build_csa_topk_idxs(npy(q), npy(ck), cuq.cpu(), offs.cpu(), 8, top_k, 4, name)
     assert_topk_match(got.cpu().numpy(), ref, npy(q), npy(ck), lambda t: Tn, 8,

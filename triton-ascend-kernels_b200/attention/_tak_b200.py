@@ -50,7 +50,8 @@ _SIGS = {
     "tak_build_decode_topk_idxs": ([_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P], _I32),
     "tak_comp_offsets": ([_P, _I64, _I32, _I64, _I64, _P, _P], _I32),
     "tak_csa_indexer_topk": ([_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
-                              _P, _I64, _I32, _P], _I32),
+                              _P, _I64, _I32, _P, _I64, _I64, _P], _I32),
+    "tak_csa_indexer_workspace_size": ([_I64, _I64, _I32], _I64),
 }
 
 

@@ -64,10 +64,13 @@ def build_csa_topk_idxs(q, compressed_k, cu_seqlens, comp_offsets, n_win, top_k,
         _t.check(L.tak_build_window_idxs(_t.ptr(cu), num_seqs, total_tokens, n_win, _t.ptr(out), K, st))
     mc = _t.max_comp_per_seq(offs, compressed_k.shape[0])
     if total_tokens and top_k and mc:
+        # score scratch: the dot products run as tensor-core GEMM tiles (CSA:144's matmul)
+        ws_bytes = L.tak_csa_indexer_workspace_size(total_tokens, mc, _t.dtype_code(q))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
         _t.check(L.tak_csa_indexer_topk(
             _t.ptr(q), _t.strides(q), _t.ptr(compressed_k), _t.strides(compressed_k), _t.ptr(cu), None, _t.ptr(offs),
             num_seqs, total_tokens, num_q_heads, num_kv_heads, head_dim, n_win, top_k, m, mc, _t.ptr(out), K,
-            _t.dtype_code(q), st))
+            _t.dtype_code(q), _t.ptr(ws), ws_bytes, compressed_k.shape[0], st))
     return out
 
 
@@ -117,6 +120,7 @@ def csa_decode_forward(q, k_cache, v_cache, block_tables, context_lens,
     if top_k and mc:
         _t.check(L.tak_csa_indexer_topk(
             _t.ptr(q), _t.strides(q), _t.ptr(ck), _t.strides(ck), None, _t.ptr(cl), _t.ptr(offs), num_seqs,
-            num_seqs, num_q_heads, num_kv_heads, head_dim, n_win, top_k, m, mc, _t.ptr(idx), K, _t.dtype_code(q), st))
+            num_seqs, num_q_heads, num_kv_heads, head_dim, n_win, top_k, m, mc, _t.ptr(idx), K, _t.dtype_code(q),
+            None, 0, ck.shape[0], st))
     return sparse_attn_decode(q, k_cache, v_cache, ck, cv, block_tables, idx, cl, num_win=n_win,
                               block_size=block_size, attn_sink=attn_sink, return_lse=return_lse)

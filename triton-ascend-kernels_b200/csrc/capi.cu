@@ -477,7 +477,8 @@ int tak_csa_indexer_topk(const void* q, const int64_t* q_strides, const void* co
                          const int64_t* ck_strides, const int32_t* cu_seqlens, const int32_t* context_lens,
                          const int32_t* comp_offsets, int64_t num_seqs, int64_t total_tokens, int64_t num_q_heads,
                          int64_t num_kv_heads, int64_t head_dim, int64_t n_win, int64_t top_k, int64_t m,
-                         int64_t max_comp_per_seq, int32_t* out, int64_t ld, int dtype, void* stream) {
+                         int64_t max_comp_per_seq, int32_t* out, int64_t ld, int dtype, void* workspace,
+                         int64_t workspace_bytes, int64_t compressed_rows, void* stream) {
   TAK_REQUIRE(dtype >= 0 && dtype <= 2, "csa indexer: unknown dtype");
   TAK_REQUIRE(q && q_strides && comp_offsets && out && (cu_seqlens || context_lens), "csa indexer: null pointer");
   TAK_REQUIRE(max_comp_per_seq == 0 || (compressed_k && ck_strides), "csa indexer: null compressed_k");
@@ -502,8 +503,16 @@ int tak_csa_indexer_topk(const void* q, const int64_t* q_strides, const void* co
   a.out = out;
   a.ld = ld;
   a.dtype = dtype;
+  a.ws = workspace;
+  a.ws_bytes = workspace ? workspace_bytes : 0;
+  a.comp_rows = compressed_rows;
   const int r = csa_indexer_launch(a, static_cast<cudaStream_t>(stream));
   return r ? r : check_launch("csa indexer");
+}
+
+int64_t tak_csa_indexer_workspace_size(int64_t total_tokens, int64_t max_comp_per_seq, int dtype) {
+  if (total_tokens <= 0 || max_comp_per_seq <= 0) return 0;
+  return csa_scores_ws_bytes(total_tokens, static_cast<int>(max_comp_per_seq), dtype);
 }
 
 }  // extern "C"

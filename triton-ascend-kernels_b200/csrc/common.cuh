@@ -50,6 +50,7 @@ template <> struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ float2 unpack2(uint32_t u) {
     return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
   }
+  static __device__ __forceinline__ uint32_t bits(__nv_bfloat16 x) { return __bfloat16_as_ushort(x); }
 };
 template <> struct Elem<__half> {
   static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
@@ -62,6 +63,7 @@ template <> struct Elem<__half> {
     __half2 h = *reinterpret_cast<__half2*>(&u);
     return __half22float2(h);
   }
+  static __device__ __forceinline__ uint32_t bits(__half x) { return __half_as_ushort(x); }
 };
 template <> struct Elem<float> {
   static __device__ __forceinline__ float to_f(float x) { return x; }

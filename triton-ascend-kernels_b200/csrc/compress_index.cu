@@ -639,7 +639,11 @@ __global__ void __launch_bounds__(NT) csa_indexer_kernel(const IndexerArgs a) {
     vec = a.sq[2] == 1 && a.sck[2] == 1 && a.head_dim % 8 == 0 && a.sck[0] % 8 == 0 &&
           ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(ck)) & 15) == 0;
   }
-  if (vec) {
+  if (a.scores) {
+    // scores computed on the tensor cores (already rounded to T)
+    const T* srow = reinterpret_cast<const T*>(a.scores) + static_cast<int64_t>(row) * a.sld;
+    for (int i = threadIdx.x; i < n_valid; i += NT) sc[i] = Elem<T>::to_f(srow[i]);
+  } else if (vec) {
     // 16-byte loads: lane l owns dims [8l, 8l+8) and [8l+256, 8l+264); a warp
     // scores SPW slots per step with all their loads in flight at once
     if constexpr (sizeof(T) == 2) {
@@ -833,13 +837,26 @@ int csa_indexer_launch(const IndexerArgs& a, cudaStream_t st) {
     if (n_pad * sizeof(unsigned long long) > smem) smem = n_pad * sizeof(unsigned long long);
   }
   if (smem > 200 * 1024) return set_error(2, "csa indexer: more than 51200 compressed slots in one sequence");
+  IndexerArgs b = a;
+  if (!a.scores) {
+    // prefill rows: the dot products as one tensor-core GEMM per tile, then selection
+    int64_t sld = 0;
+    int err = 0;
+    if (csa_scores_tc_launch(a, st, &sld, &err)) {
+      if (err) return err;
+      b.scores = a.ws;
+      b.sld = sld;
+      // up to 1024 slots per sequence: one warp per row sorts in registers
+      if (csa_select_warp_launch(b, st)) return 0;
+    }
+  }
   // few rows (decode): wider CTAs with more score loads in flight
   const bool wide = rows < 2 * num_sms();
-  if (a.dtype == kBF16) return wide ? launch_indexer<__nv_bfloat16, 512, 8>(a, rows, smem, st)
-                                    : launch_indexer<__nv_bfloat16, 256, 4>(a, rows, smem, st);
-  if (a.dtype == kF16) return wide ? launch_indexer<__half, 512, 8>(a, rows, smem, st)
-                                   : launch_indexer<__half, 256, 4>(a, rows, smem, st);
-  return launch_indexer<float, 256, 4>(a, rows, smem, st);
+  if (a.dtype == kBF16) return wide ? launch_indexer<__nv_bfloat16, 512, 8>(b, rows, smem, st)
+                                    : launch_indexer<__nv_bfloat16, 256, 4>(b, rows, smem, st);
+  if (a.dtype == kF16) return wide ? launch_indexer<__half, 512, 8>(b, rows, smem, st)
+                                   : launch_indexer<__half, 256, 4>(b, rows, smem, st);
+  return launch_indexer<float, 256, 4>(b, rows, smem, st);
 }
 
 }  // namespace tak

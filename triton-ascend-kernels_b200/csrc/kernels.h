@@ -135,7 +135,18 @@ struct IndexerArgs {
   int max_comp_per_seq;  // largest comp_offsets[s+1] - comp_offsets[s]
   int32_t* out; int64_t ld;
   int dtype;
+  int64_t comp_rows;     // rows of compressed_k
+  void* ws; int64_t ws_bytes;      // scratch for tensor-core scores (prefill), may be null
+  const void* scores; int64_t sld;  // scores provided: [rows, sld] in the input dtype
 };
 int csa_indexer_launch(const IndexerArgs& a, cudaStream_t st);
+// Scratch bytes for the tensor-core scores of total_tokens prefill rows.
+int64_t csa_scores_ws_bytes(int64_t total_tokens, int max_comp_per_seq, int dtype);
+// Scores of prefill rows on the tensor cores into a.ws ([total_tokens, *ld]);
+// false when the shapes or the scratch do not allow it (nothing launched).
+bool csa_scores_tc_launch(const IndexerArgs& a, cudaStream_t st, int64_t* ld, int* err);
+// Top-k selection of prefill rows from provided scores, one warp per row
+// (at most 1024 slots per sequence); false when it does not apply.
+bool csa_select_warp_launch(const IndexerArgs& a, cudaStream_t st);
 
 }  // namespace tak
