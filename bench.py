@@ -811,9 +811,12 @@ class CsaDecodeWL(Workload):
         T.check(L.tak_build_decode_topk_idxs(T.ptr(self.ctx), T.ptr(offs), B, self.n_win, self.top_k, 0,
                                              T.ptr(idx), K, st))
         mc = min(T.max_slots_per_seq(self.bt, self.P, self.m), ck.shape[0])
+        ws_bytes = L.tak_csa_indexer_workspace_size(B, mc, T.dtype_code(self.q))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
         T.check(L.tak_csa_indexer_topk(T.ptr(self.q), T.strides(self.q), T.ptr(ck), T.strides(ck), None,
                                        T.ptr(self.ctx), T.ptr(offs), B, B, 64, 1, 512, self.n_win, self.top_k,
-                                       self.m, mc, T.ptr(idx), K, T.dtype_code(self.q), None, 0, ck.shape[0], st))
+                                       self.m, mc, T.ptr(idx), K, T.dtype_code(self.q), T.ptr(ws), ws_bytes,
+                                       ck.shape[0], st))
         ev[2].record()
         CSA.sparse_attn_decode(self.q, self.kc, self.kc, ck, cv, self.bt, idx, self.ctx, self.n_win, self.P,
                                self.sink)

@@ -252,9 +252,11 @@ int tak_comp_offsets(const int32_t* lens, int64_t num_seqs, int is_cu, int64_t s
  * to the lower slot; masked slots appended in ascending order when fewer than
  * min(top_k, n_c) are causal.  max_comp_per_seq bounds n_c (<= 51200).
  * workspace (may be NULL) of at least tak_csa_indexer_workspace_size bytes
- * lets prefill rows compute the scores as tensor-core GEMM tiles (the
- * reference's matmul, CSA:144) before the selection; without it each row's
- * dot products run on CUDA cores.  compressed_rows = rows of compressed_k.
+ * (for the rows: total_tokens in prefill, num_seqs in decode) holds the
+ * scores before the selection: prefill rows compute them as tensor-core GEMM
+ * tiles (the reference's matmul, CSA:144), decode rows split each row's dot
+ * products over many CTAs; without it one CTA per row scores on CUDA cores.
+ * compressed_rows = rows of compressed_k.
  */
 int tak_csa_indexer_topk(const void* q, const int64_t* q_strides, const void* compressed_k,
                          const int64_t* ck_strides, const int32_t* cu_seqlens, const int32_t* context_lens,
@@ -263,8 +265,9 @@ int tak_csa_indexer_topk(const void* q, const int64_t* q_strides, const void* co
                          int64_t max_comp_per_seq, int32_t* out, int64_t ld, int dtype, void* workspace,
                          int64_t workspace_bytes, int64_t compressed_rows, void* stream);
 
-/* Bytes of the score scratch of tak_csa_indexer_topk for total_tokens prefill
- * rows: total_tokens x max_comp_per_seq rounded up to 128 x the element size. */
+/* Bytes of the score scratch of tak_csa_indexer_topk for `total_tokens` rows
+ * (prefill tokens, or decode sequences): rows x max_comp_per_seq rounded up
+ * to 128 x the element size. */
 int64_t tak_csa_indexer_workspace_size(int64_t total_tokens, int64_t max_comp_per_seq, int dtype);
 
 #ifdef __cplusplus

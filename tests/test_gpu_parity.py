@@ -585,6 +585,41 @@ def test_csa_hca_forward_latent512(dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_csa_decode_indexer_split_scores(dtype):
+    """Decode index rows with the scores split over CTAs (score workspace) equal
+    the rows of one CTA per request scoring on its own (no workspace), bit for
+    bit (same dot-product order), and match the oracle's csa_decode_idxs (up to
+    one-rounding-step swaps); contexts up to 4000 tokens (1000 slots), empty and
+    short ones included."""
+    ctx = [4000, 0, 1, 7, 2049, 3333, 512, 90]
+    P, m, n_win, top_k = 64, 4, 16, 300
+    _, kc, _, _, _, bt, _, cl, _ = _sparse_decode_case(ctx, 8, 1, 512, 512, P, 1, 1, 1, dtype, 73,
+                                                       shared_latent=True)
+    g = torch.Generator().manual_seed(74)
+    q = torch.randn(len(ctx), 8, 512, generator=g).to(DEV, dtype)
+    ck, _, offs, lens, offs_h = T.compress_paged(kc, kc, bt, cl, P, m, 2 * m)
+    B, K = len(ctx), n_win + top_k
+    mc = max(offs_h[i + 1] - offs_h[i] for i in range(B))
+    L = T.lib()
+    st = T.stream_of(q)
+    rows = []
+    for with_ws in (True, False):
+        idx = torch.empty((B, K), dtype=torch.int32, device=DEV)
+        T.check(L.tak_build_decode_topk_idxs(T.ptr(cl), T.ptr(offs), B, n_win, top_k, 0, T.ptr(idx), K, st))
+        nb = L.tak_csa_indexer_workspace_size(B, mc, T.dtype_code(q)) if with_ws else 0
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=DEV)
+        T.check(L.tak_csa_indexer_topk(T.ptr(q), T.strides(q), T.ptr(ck), T.strides(ck), None, T.ptr(cl),
+                                       T.ptr(offs), B, B, 8, 1, 512, n_win, top_k, m, mc, T.ptr(idx), K,
+                                       T.dtype_code(q), T.ptr(ws) if with_ws else None, nb, ck.shape[0], st))
+        rows.append(idx.cpu().numpy())
+    np.testing.assert_array_equal(rows[0], rows[1])
+    name = "bfloat16" if dtype == torch.bfloat16 else "float16"
+    ref = O.csa_decode_idxs(npy(q), npy(ck), cl.cpu(), offs.cpu(), n_win, top_k, m, name)
+    assert_topk_match(rows[0], ref, npy(q), npy(ck), lambda b: int(cl[b]), n_win,
+                      2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_csa_hca_decode_latent512(dtype):
     """MLA-style decode: one paged 512-dim latent cache passed as both K and V
     (pooled once, compressed V a view of compressed K, the shared-latent

@@ -118,9 +118,11 @@ def csa_decode_forward(q, k_cache, v_cache, block_tables, context_lens,
     else:
         mc = min(_t.max_slots_per_seq(block_tables, block_size, m), ck.shape[0])
     if top_k and mc:
+        ws_bytes = L.tak_csa_indexer_workspace_size(num_seqs, mc, _t.dtype_code(q))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
         _t.check(L.tak_csa_indexer_topk(
             _t.ptr(q), _t.strides(q), _t.ptr(ck), _t.strides(ck), None, _t.ptr(cl), _t.ptr(offs), num_seqs,
             num_seqs, num_q_heads, num_kv_heads, head_dim, n_win, top_k, m, mc, _t.ptr(idx), K, _t.dtype_code(q),
-            None, 0, ck.shape[0], st))
+            _t.ptr(ws), ws_bytes, ck.shape[0], st))
     return sparse_attn_decode(q, k_cache, v_cache, ck, cv, block_tables, idx, cl, num_win=n_win,
                               block_size=block_size, attn_sink=attn_sink, return_lse=return_lse)

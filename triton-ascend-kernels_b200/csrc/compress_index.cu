@@ -604,6 +604,85 @@ __device__ __forceinline__ float round_to_t<float>(float x) {
 constexpr int kIdxRoundsMax = 16;
 constexpr int kIdxSortMax = 8192;
 
+// Unscaled dot products q . ck[i] for slots i in [i_begin, i_end), rounded to
+// T, handed to sink(i, score): 16-byte loads, lane l owns dims [8l, 8l+8) and
+// [8l+256, 8l+264) (head_dim <= 512); a warp scores SPW slots per step with all
+// their loads in flight.  Warp w of nwarps starts at slot i_begin + w * SPW.
+template <typename T, int SPW, class Sink>
+__device__ __forceinline__ void score_slots_vec(const T* q, const T* ck, int64_t sck0, int head_dim, int i_begin,
+                                                int i_end, int warp, int nwarps, int lane, Sink&& sink) {
+  const int nch = head_dim / 8;
+  float qv[16];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int ch = lane + 32 * c;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (ch < nch) u = *reinterpret_cast<const uint4*>(q + ch * 8);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = Elem<T>::unpack2(w[e]);
+      qv[c * 8 + 2 * e] = f.x;
+      qv[c * 8 + 2 * e + 1] = f.y;
+    }
+  }
+  for (int i0 = i_begin + warp * SPW; i0 < i_end; i0 += nwarps * SPW) {
+    uint4 kv[SPW][2];
+#pragma unroll
+    for (int si = 0; si < SPW; ++si)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int ch = lane + 32 * c;
+        kv[si][c] = make_uint4(0, 0, 0, 0);
+        if (i0 + si < i_end && ch < nch)
+          kv[si][c] = *reinterpret_cast<const uint4*>(ck + static_cast<int64_t>(i0 + si) * sck0 + ch * 8);
+      }
+    float acc[SPW];
+#pragma unroll
+    for (int si = 0; si < SPW; ++si) {
+      float sacc = 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint32_t w[4] = {kv[si][c].x, kv[si][c].y, kv[si][c].z, kv[si][c].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = Elem<T>::unpack2(w[e]);
+          sacc = fmaf(qv[c * 8 + 2 * e], f.x, sacc);
+          sacc = fmaf(qv[c * 8 + 2 * e + 1], f.y, sacc);
+        }
+      }
+      acc[si] = warp_sum(sacc);
+    }
+    // lanes 0..SPW-1 hand over the scores (selects, not a register-indexed load)
+    float mine = acc[0];
+#pragma unroll
+    for (int si = 1; si < SPW; ++si)
+      if (lane == si) mine = acc[si];
+    if (lane < SPW && i0 + lane < i_end) sink(i0 + lane, round_to_t<T>(mine));
+  }
+}
+
+// Decode rows (one query per sequence, each against its own slots): the
+// scores of a row split over CTAs of 256 slots each, written rounded to T into
+// a scratch [rows, sld] that the selection (csa_indexer_kernel) reads -- one
+// CTA per row alone leaves most SMs idle and its loads latency-bound.
+template <typename T>
+__global__ void __launch_bounds__(256) csa_decode_scores_kernel(const IndexerArgs a, T* scores, int64_t sld) {
+  const int row = blockIdx.x;
+  const int pos = a.context_lens[row];
+  const int c0 = a.comp_offsets[row];
+  const int nc = min(a.comp_offsets[row + 1] - c0, a.max_comp_per_seq);
+  const int n_valid = pos <= 0 ? 0 : min(nc, (pos + a.m - 1) / a.m);
+  const int i_begin = blockIdx.y * 256, i_end = min(n_valid, i_begin + 256);
+  if (i_begin >= i_end) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* q = reinterpret_cast<const T*>(a.q) + static_cast<int64_t>(row) * a.sq[0] + (a.num_q_heads - 1) * a.sq[1];
+  const T* ck = reinterpret_cast<const T*>(a.ck) + static_cast<int64_t>(c0) * a.sck[0] + (a.num_kv_heads - 1) * a.sck[1];
+  T* out = scores + static_cast<int64_t>(row) * sld;
+  score_slots_vec<T, 4>(q, ck, a.sck[0], a.head_dim, i_begin, i_end, warp, 8, lane,
+                        [&](int i, float v) { out[i] = Elem<T>::from_f(v); });
+}
+
 // NT threads; SPW slots scored per warp step (all their loads in flight at
 // once): 256 x 4 when there are many rows, 512 x 8 for the few long rows of
 // decode, where one CTA per row leaves most SMs idle and the score loads are
@@ -646,57 +725,9 @@ __global__ void __launch_bounds__(NT) csa_indexer_kernel(const IndexerArgs a) {
   } else if (vec) {
     // 16-byte loads: lane l owns dims [8l, 8l+8) and [8l+256, 8l+264); a warp
     // scores SPW slots per step with all their loads in flight at once
-    if constexpr (sizeof(T) == 2) {
-      const int nch = a.head_dim / 8;
-      float qv[16];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int ch = lane + 32 * c;
-        uint4 u = make_uint4(0, 0, 0, 0);
-        if (ch < nch) u = *reinterpret_cast<const uint4*>(q + ch * 8);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = Elem<T>::unpack2(w[e]);
-          qv[c * 8 + 2 * e] = f.x;
-          qv[c * 8 + 2 * e + 1] = f.y;
-        }
-      }
-      for (int i0 = warp * SPW; i0 < n_valid; i0 += nwarps * SPW) {
-        uint4 kv[SPW][2];
-#pragma unroll
-        for (int si = 0; si < SPW; ++si)
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int ch = lane + 32 * c;
-            kv[si][c] = make_uint4(0, 0, 0, 0);
-            if (i0 + si < n_valid && ch < nch)
-              kv[si][c] = *reinterpret_cast<const uint4*>(ck + static_cast<int64_t>(i0 + si) * a.sck[0] + ch * 8);
-          }
-        float acc[SPW];
-#pragma unroll
-        for (int si = 0; si < SPW; ++si) {
-          float sacc = 0.f;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const uint32_t w[4] = {kv[si][c].x, kv[si][c].y, kv[si][c].z, kv[si][c].w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = Elem<T>::unpack2(w[e]);
-              sacc = fmaf(qv[c * 8 + 2 * e], f.x, sacc);
-              sacc = fmaf(qv[c * 8 + 2 * e + 1], f.y, sacc);
-            }
-          }
-          acc[si] = warp_sum(sacc);
-        }
-        // lanes 0..SPW-1 write the scores (selects, not a register-indexed load)
-        float mine = acc[0];
-#pragma unroll
-        for (int si = 1; si < SPW; ++si)
-          if (lane == si) mine = acc[si];
-        if (lane < SPW && i0 + lane < n_valid) sc[i0 + lane] = round_to_t<T>(mine);
-      }
-    }
+    if constexpr (sizeof(T) == 2)
+      score_slots_vec<T, SPW>(q, ck, a.sck[0], a.head_dim, 0, n_valid, warp, nwarps, lane,
+                              [&](int i, float v) { sc[i] = v; });
   } else {
     float qr[16];
 #pragma unroll
@@ -848,6 +879,19 @@ int csa_indexer_launch(const IndexerArgs& a, cudaStream_t st) {
       b.sld = sld;
       // up to 1024 slots per sequence: one warp per row sorts in registers
       if (csa_select_warp_launch(b, st)) return 0;
+    } else if (!a.cu_seqlens && a.dtype != kF32 && a.ws && a.head_dim % 8 == 0 && a.head_dim <= 512 &&
+               a.sq[2] == 1 && a.sck[2] == 1 && a.sq[0] % 8 == 0 && a.sq[1] % 8 == 0 && a.sck[0] % 8 == 0 &&
+               a.sck[1] % 8 == 0 && ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.ck)) & 15) == 0 &&
+               a.ws_bytes >= csa_scores_ws_bytes(rows, a.max_comp_per_seq, a.dtype)) {
+      // decode rows: the scores split over CTAs of 256 slots, then the selection
+      const int64_t ld = (static_cast<int64_t>(a.max_comp_per_seq) + 127) / 128 * 128;
+      const dim3 grid(rows, static_cast<unsigned>((a.max_comp_per_seq + 255) / 256));
+      if (a.dtype == kBF16)
+        csa_decode_scores_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a, reinterpret_cast<__nv_bfloat16*>(a.ws), ld);
+      else
+        csa_decode_scores_kernel<__half><<<grid, 256, 0, st>>>(a, reinterpret_cast<__half*>(a.ws), ld);
+      b.scores = a.ws;
+      b.sld = ld;
     }
   }
   // few rows (decode): wider CTAs with more score loads in flight

@@ -326,18 +326,25 @@ __global__ void __launch_bounds__(320, 1)
       // pass 2: P = 2^(s*scale - m), 32 scores at a time; the 16 packed columns
       // of chunk c land on S columns [16c, 16c+16), already consumed
       float ls0 = 0.f, ls1 = 0.f;
+      uint64_t lsx2 = 0;  // packed row-sum pair of the interior path (two +0.0f)
+      const uint64_t sl2x2 = (static_cast<uint64_t>(__float_as_uint(sl2)) << 32) | __float_as_uint(sl2);
+      const uint64_t nmux2 = (static_cast<uint64_t>(__float_as_uint(-mu)) << 32) | __float_as_uint(-mu);
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         uint32_t sr[32], pk[16];
         tmem_ld32(s_tmem + c4 * 32, sr);
         tmem_ld_wait();
         if (interior) {
+          // two scores per packed fp32 FMA and per packed row-sum add (same
+          // rounding as the scalar forms)
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const float a = fast_exp2(fmaf(__uint_as_float(sr[2 * c]), sl2, -mu));
-            const float bb = fast_exp2(fmaf(__uint_as_float(sr[2 * c + 1]), sl2, -mu));
-            ls0 += a;
-            ls1 += bb;
+            uint64_t x = (static_cast<uint64_t>(sr[2 * c + 1]) << 32) | sr[2 * c];
+            asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(x) : "l"(sl2x2), "l"(nmux2));
+            const float a = fast_exp2(__uint_as_float(static_cast<uint32_t>(x)));
+            const float bb = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
+            const uint64_t ab = (static_cast<uint64_t>(__float_as_uint(bb)) << 32) | __float_as_uint(a);
+            asm("add.rn.f32x2 %0, %0, %1;" : "+l"(lsx2) : "l"(ab));
             pk[c] = Elem<T>::pack2(a, bb);
           }
         } else {
@@ -353,6 +360,8 @@ __global__ void __launch_bounds__(320, 1)
         }
         tmem_st16(s_tmem + 16 * c4, pk);
       }
+      ls0 += __uint_as_float(static_cast<uint32_t>(lsx2));
+      ls1 += __uint_as_float(static_cast<uint32_t>(lsx2 >> 32));
       l += ls0 + ls1;
       tmem_st_wait();
       tc_fence_before();
