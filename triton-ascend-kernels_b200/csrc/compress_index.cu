@@ -892,6 +892,8 @@ int csa_indexer_launch(const IndexerArgs& a, cudaStream_t st) {
         csa_decode_scores_kernel<__half><<<grid, 256, 0, st>>>(a, reinterpret_cast<__half*>(a.ws), ld);
       b.scores = a.ws;
       b.sld = ld;
+      // up to 2048 slots: the hybrid register / shared-memory sort
+      if (csa_select_block_launch(b, rows, st)) return 0;
     }
   }
   // few rows (decode): wider CTAs with more score loads in flight

@@ -342,6 +342,91 @@ bool csa_select_warp_launch(const IndexerArgs& a, cudaStream_t st) {
   return true;
 }
 
+// Rows of up to 2048 causal slots with few rows (decode): one 512-thread CTA
+// per row, thread t holding keys 4t .. 4t+3 of a 2048-key bitonic network.
+// Partners closer than 4 keys are in the same thread, closer than 128 one
+// shuffle away; only the 10 passes with partners in another warp exchange
+// through shared memory (one 16-byte store and load per thread).
+template <typename T>
+__global__ void __launch_bounds__(512) csa_select_block_kernel(const IndexerArgs a) {
+  constexpr int E = 4, N = 512 * E;
+  __shared__ uint4 xk[512];
+  const int row = blockIdx.x;  // decode: sequence = row
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int pos = a.context_lens[row];
+  const int c0 = a.comp_offsets[row];
+  const int nc = min(a.comp_offsets[row + 1] - c0, a.max_comp_per_seq);
+  if (nc <= 0) return;
+  const int k_sel = min(a.top_k, nc);
+  const int n_valid = pos <= 0 ? 0 : min(nc, (pos + a.m - 1) / a.m);
+  const int n_pick = min(k_sel, n_valid);
+  const int64_t base = static_cast<int64_t>(pos) + c0;
+  int32_t* out = a.out + static_cast<int64_t>(row) * a.ld + a.n_win;
+  if (n_pick > 0) {
+    const T* srow = reinterpret_cast<const T*>(a.scores) + static_cast<int64_t>(row) * a.sld;
+    uint32_t k[E];
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+      const int i = tid * E + r;
+      k[r] = i < n_valid ? it_key<T>(srow[i], i) : 0u;
+    }
+#pragma unroll
+    for (int kk = 2; kk <= N; kk <<= 1) {
+#pragma unroll
+      for (int j = kk >> 1; j > 0; j >>= 1) {
+        if (j >= 32 * E) {
+          const int tm = j / E;  // partner thread = tid ^ tm (another warp)
+          xk[tid] = make_uint4(k[0], k[1], k[2], k[3]);
+          __syncthreads();
+          const uint4 o4 = xk[tid ^ tm];
+          __syncthreads();
+          const uint32_t o[E] = {o4.x, o4.y, o4.z, o4.w};
+          const bool lower = (tid & tm) == 0;
+#pragma unroll
+          for (int r = 0; r < E; ++r) {
+            const bool desc = ((tid * E + r) & kk) == 0;
+            k[r] = (desc == lower) ? max(k[r], o[r]) : min(k[r], o[r]);
+          }
+        } else if (j >= E) {
+          const int lm = j / E;
+          const bool lower = (lane & lm) == 0;
+#pragma unroll
+          for (int r = 0; r < E; ++r) {
+            const uint32_t o = __shfl_xor_sync(0xffffffffu, k[r], lm);
+            const bool desc = ((tid * E + r) & kk) == 0;
+            k[r] = (desc == lower) ? max(k[r], o) : min(k[r], o);
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < E; ++r) {
+            if (r & j) continue;
+            const int r2 = r | j;
+            const bool desc = ((tid * E + r) & kk) == 0;
+            const uint32_t hi = max(k[r], k[r2]), lo = min(k[r], k[r2]);
+            k[r] = desc ? hi : lo;
+            k[r2] = desc ? lo : hi;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+      const int rank = tid * E + r;
+      if (rank < n_pick) out[rank] = static_cast<int32_t>(base + (0xffffu - (k[r] & 0xffffu)));
+    }
+  }
+  for (int r = n_pick + tid; r < k_sel; r += 512) out[r] = static_cast<int32_t>(base + r);
+}
+
+bool csa_select_block_launch(const IndexerArgs& a, int rows, cudaStream_t st) {
+  if (a.cu_seqlens || !a.scores || a.dtype == kF32 || a.max_comp_per_seq > 2048) return false;
+  if (a.dtype == kBF16)
+    csa_select_block_kernel<__nv_bfloat16><<<rows, 512, 0, st>>>(a);
+  else
+    csa_select_block_kernel<__half><<<rows, 512, 0, st>>>(a);
+  return true;
+}
+
 // 2-D view [rows, cols] of a 16-bit tensor, box {64 columns, 128 rows}, 128-byte swizzle.
 static int it_encode(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t row_stride) {
   const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};

@@ -148,5 +148,8 @@ bool csa_scores_tc_launch(const IndexerArgs& a, cudaStream_t st, int64_t* ld, in
 // Top-k selection of prefill rows from provided scores, one warp per row
 // (at most 1024 slots per sequence); false when it does not apply.
 bool csa_select_warp_launch(const IndexerArgs& a, cudaStream_t st);
+// Top-k selection of decode rows (one per sequence) from provided scores, one
+// 512-thread CTA per row (at most 2048 slots); false when it does not apply.
+bool csa_select_block_launch(const IndexerArgs& a, int rows, cudaStream_t st);
 
 }  // namespace tak
