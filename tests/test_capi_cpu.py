@@ -113,3 +113,27 @@ def test_comp_offsets_host_matches_oracle():
 
     for lens, st in (([0, 3, 4, 5, 130], 4), ([256, 512, 384], 128), ([], 4), ([1], 128)):
         assert T.comp_offsets_host(lens, st) == O.comp_offsets_for(lens, st).tolist()
+
+
+def test_indexer_workspace_size_is_host_only():
+    if not os.path.exists(T.LIB_PATH):
+        pytest.skip("libtak_b200.so not built")
+    L = T.lib()
+    # rows x max slots rounded up to 128 x element size (bf16 = 1, fp32 = 2)
+    assert L.tak_csa_indexer_workspace_size(65536, 1024, 1) == 65536 * 1024 * 2
+    assert L.tak_csa_indexer_workspace_size(64, 2042, 1) == 64 * 2048 * 2
+    assert L.tak_csa_indexer_workspace_size(10, 1, 2) == 10 * 128 * 4
+    assert L.tak_csa_indexer_workspace_size(0, 100, 1) == 0
+
+
+def test_prefix_view_and_slot_bounds():
+    kc = torch.zeros(6, 1, 16, 576)
+    assert T.is_prefix_view(kc, kc)
+    assert T.is_prefix_view(kc[..., :512], kc)              # MLA: V = the first 512 latent columns
+    assert not T.is_prefix_view(kc[..., 64:], kc)           # another offset
+    assert not T.is_prefix_view(torch.zeros(6, 1, 16, 512), kc)
+    assert not T.is_prefix_view(kc[:3], kc)                 # fewer pages
+    bt = torch.zeros(4, 64, dtype=torch.int32)
+    assert T.max_slots_per_seq(bt, 128, 4) == 2048          # 64 pages x 128 rows / m
+    assert T.max_slots_per_seq(bt, 128, 128) == 64
+    assert T.max_slots_per_seq(torch.zeros(4, 0, dtype=torch.int32), 16, 4) == 1
