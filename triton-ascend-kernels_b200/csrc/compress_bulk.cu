@@ -296,6 +296,291 @@ __global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a
   }
 }
 
+// ---------------------------------------------------------------------------
+// CSA (window 2m, stride m) and HCA (window = stride = m') pooling of the same
+// TND rows in one pass, gated (softmax of the gate logits over each window) or
+// plain mean (all logits 0): compress_kv_overlap (CSA:9-69) and
+// compress_kv_simple (HCA:9-69) on one K/V stream.  One CTA per (HCA slot, KV
+// head): its m' rows and the m-row halo of its last CSA window stream through
+// the same bulk-copy ring as compress_bulk_kernel.  While the producer's first
+// copies are in flight the consumer warps load the slot's gate logits and turn
+// them into row weights 2^(g - block max), per-block sums, the two merge
+// factors of every CSA slot (its blocks b and b+1) and the factor of every
+// block in the HCA slot, all in shared memory; rows are then accumulated per
+// m-row block, each CSA slot written as its second block completes, and the
+// HCA slot at the end.  With slots of m' rows the grid has one CTA per slot,
+// and four CTAs per SM keep every slot of a long batch resident at once.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cb_consumer_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// MC = 4 (the reference's CSA stride) with chunks a multiple of 8 rows: every
+// full chunk is whole block pairs, summed into two register sets that swap
+// roles, with no per-row tests.
+template <typename T, int MC>
+__global__ void __launch_bounds__(288) compress_dual_kernel(const CompressArgs csa, const CompressArgs hca, int ch,
+                                                            int nst, int span) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const CompressArgs& a = csa;  // K, V, gate, cu_seqlens, input strides and head dims are shared
+  const int nk = a.head_dim / 8, nv = a.head_dim_v / 8;
+  const int ncw = (nk + nv + 31) / 32;  // consumer warps; warp ncw is the producer
+  const uint32_t kbytes = nk * 16, vbytes = nv * 16, row_bytes = kbytes + vbytes;
+  const uint32_t stage_bytes = row_bytes * ch;
+  const int m = csa.stride, mp = hca.stride;
+  const int rows_max = mp + m, nb_max = rows_max / m + 1;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + nst * stage_bytes);
+  uint64_t* empty = full + nst;
+  float* gw = reinterpret_cast<float*>(empty + nst);  // [rows_max] logits, then row weights
+  float* bm = gw + rows_max;                          // [nb_max] block max logit
+  float* bs = bm + nb_max;                            // [nb_max] block weight sum
+  // [nb_max] CSA slot j: factors of blocks j, j + 1 (8-byte aligned: gw is 16-byte aligned)
+  float2* fab = reinterpret_cast<float2*>(gw + ((rows_max + 2 * nb_max + 1) & ~1));
+  float* bh = reinterpret_cast<float*>(fab + nb_max);  // [nb_max] HCA factor of block b
+
+  const int u = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (u >= hca.comp_offsets[hca.num_seqs]) return;  // num_compressed may be a capacity
+  const int s = find_slot_seq(hca.comp_offsets, hca.num_seqs, u);
+  const int i = u - hca.comp_offsets[s];
+  const int64_t tok0 = a.cu_seqlens[s];
+  const int L = a.cu_seqlens[s + 1] - a.cu_seqlens[s];
+  const int r_begin = i * mp;
+  const int nrows_h = min(mp, L - r_begin);    // rows of the HCA slot
+  const int nrows = min(mp + m, L - r_begin);  // plus the halo of its last CSA window
+  const int nb = (nrows + m - 1) / m, nbh = (nrows_h + m - 1) / m;
+  const int c0 = csa.comp_offsets[s];
+  const int j_begin = r_begin / m;  // local CSA slot j is slot j_begin + j of the sequence
+  const int nj = max(0, min(mp / m, csa.comp_offsets[s + 1] - c0 - j_begin));
+
+  if (tid == 0) {
+    for (int q = 0; q < nst; ++q) {
+      mbar_init(&full[q], 1);
+      mbar_init(&empty[q], ncw);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == ncw) {
+    // ---------------- producer: chunk q (rows [q*ch, q*ch + n)) -> stage q % nst ----------------
+    const T* kb = reinterpret_cast<const T*>(a.k) + (tok0 + r_begin) * a.sk[0] + h * a.sk[1];
+    const T* vb = reinterpret_cast<const T*>(a.v) + (tok0 + r_begin) * a.sv[0] + h * a.sv[1];
+    int issued = 0;
+    for (int r0 = 0; r0 < nrows; r0 += ch, ++issued) {
+      const int st = issued % nst;
+      if (issued >= nst && !mbar_wait_sleep(&empty[st], ((issued / nst) - 1) & 1, 2000)) break;
+      const int n = min(ch, nrows - r0);
+      uint8_t* dst = smem + st * stage_bytes;
+      uint8_t* vdst = dst + ch * kbytes;
+      if (lane == 0) mbar_arrive_expect_tx(&full[st], n * row_bytes);
+      __syncwarp();
+      if (span) {  // rows of a sequence are contiguous: one copy per tensor
+        if (lane == 0) {
+          bulk_copy_g2s(dst, kb + r0 * a.sk[0], n * kbytes, &full[st]);
+          if (vbytes) bulk_copy_g2s(vdst, vb + r0 * a.sv[0], n * vbytes, &full[st]);
+        }
+      } else if (lane < n) {
+        bulk_copy_g2s(dst + lane * kbytes, kb + (r0 + lane) * a.sk[0], kbytes, &full[st]);
+        if (vbytes) bulk_copy_g2s(vdst + lane * vbytes, vb + (r0 + lane) * a.sv[0], vbytes, &full[st]);
+      }
+    }
+    // leave no copy in flight into this CTA's shared memory (bounded waits)
+    if (lane == 0)
+      for (int q = max(0, issued - nst); q < issued; ++q) mbar_wait(&full[q % nst], (q / nst) & 1);
+    return;
+  }
+
+  // ---------------- consumers: window weights from the gate logits ----------------
+  const int nct = ncw * 32;
+  for (int r = tid; r < nrows; r += nct)
+    gw[r] = a.gate ? __ldg(a.gate + (tok0 + r_begin + r) * a.sg[0]) : 0.f;
+  cb_consumer_sync(nct);
+  for (int b = tid; b < nb; b += nct) {
+    const int r0 = b * m, r1 = min(r0 + m, nrows);
+    float mx = -INFINITY;
+    for (int r = r0; r < r1; ++r) mx = fmaxf(mx, gw[r]);
+    float sum = 0.f;
+    for (int r = r0; r < r1; ++r) {
+      const float w = __expf(gw[r] - mx);
+      gw[r] = w;
+      sum += w;
+    }
+    bm[b] = mx;
+    bs[b] = sum;
+  }
+  cb_consumer_sync(nct);
+  if (warp == 0) {
+    // HCA slot: softmax over its rows = blocks [0, nbh) merged at their maxima
+    float mh = -INFINITY;
+    for (int b = lane; b < nbh; b += 32) mh = fmaxf(mh, bm[b]);
+    mh = warp_max(mh);
+    float hs = 0.f;
+    for (int b = lane; b < nbh; b += 32) {
+      const float f = __expf(bm[b] - mh);
+      bh[b] = f;
+      hs += f * bs[b];
+    }
+    hs = warp_sum(hs);
+    const float hinv = hs > 0.f ? 1.f / hs : 0.f;
+    for (int b = lane; b < nbh; b += 32) bh[b] *= hinv;
+    // CSA slot j: blocks j and j + 1 (the second missing at the sequence end)
+    for (int j = lane; j < nj; j += 32) {
+      const bool two = j + 1 < nb;
+      const float ma = bm[j], mb = two ? bm[j + 1] : -INFINITY, Mx = fmaxf(ma, mb);
+      const float fa = __expf(ma - Mx), fb = two ? __expf(mb - Mx) : 0.f;
+      const float den = bs[j] * fa + (two ? bs[j + 1] * fb : 0.f);
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      fab[j] = make_float2(fa * inv, fb * inv);
+    }
+  }
+  cb_consumer_sync(nct);
+
+  // ---------------- consumers: thread tid owns 16-byte vector tid of the [K | V] row ----------------
+  const bool active = tid < nk + nv;
+  const bool is_k = tid < nk;
+  const int d0 = (is_k ? tid : tid - nk) * 8;
+  const uint32_t col_off = !active ? 0u : is_k ? tid * 16u : ch * kbytes + (tid - nk) * 16u;
+  const uint32_t pitch = (active && !is_k) ? vbytes : kbytes;
+  const int64_t so0 = is_k ? csa.sck[0] : csa.scv[0];
+  T* csa_out = reinterpret_cast<T*>(is_k ? csa.ck : csa.cv) + (static_cast<int64_t>(c0) + j_begin) * so0 +
+               h * (is_k ? csa.sck[1] : csa.scv[1]) + d0;
+  T* hca_out = reinterpret_cast<T*>(is_k ? hca.ck : hca.cv) +
+               static_cast<int64_t>(hca.comp_offsets[s] + i) * (is_k ? hca.sck[0] : hca.scv[0]) +
+               h * (is_k ? hca.sck[1] : hca.scv[1]) + d0;
+  auto store8 = [&](T* dst, const float* o) {
+    uint4 q;
+    q.x = Elem<T>::pack2(o[0], o[1]);
+    q.y = Elem<T>::pack2(o[2], o[3]);
+    q.z = Elem<T>::pack2(o[4], o[5]);
+    q.w = Elem<T>::pack2(o[6], o[7]);
+    __stcg(reinterpret_cast<uint4*>(dst), q);
+  };
+  float prev[8], cur[8], hacc[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) prev[e] = cur[e] = hacc[e] = 0.f;
+  int blk = 0, blk_end = min(m, nrows);
+  // one row into an accumulator (first: overwrite)
+  auto row_acc = [&](float* acc, const uint8_t* src, float w, bool first) {
+    const uint4 u4 = *reinterpret_cast<const uint4*>(src);
+    const uint32_t wd[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f2 = Elem<T>::unpack2(wd[e]);
+      acc[2 * e] = first ? w * f2.x : fmaf(w, f2.x, acc[2 * e]);
+      acc[2 * e + 1] = first ? w * f2.y : fmaf(w, f2.y, acc[2 * e + 1]);
+    }
+  };
+  // block b (in c, the previous block in pv) is complete: CSA slot b - 1, HCA share
+  auto finish = [&](int b, const float* pv, const float* c) {
+    if (b >= 1 && b - 1 < nj && active) {
+      const float2 f = fab[b - 1];
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = fmaf(pv[e], f.x, c[e] * f.y);
+      store8(csa_out + static_cast<int64_t>(b - 1) * so0, o);
+    }
+    if (b < nbh) {
+      const float hf = bh[b];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hacc[e] = fmaf(c[e], hf, hacc[e]);
+    }
+  };
+  int q = 0;
+  for (int r0 = 0; r0 < nrows; r0 += ch, ++q) {
+    const int st = q % nst;
+    if (!mbar_wait_sleep(&full[st], (q / nst) & 1, 2000)) break;
+    const int n = min(ch, nrows - r0);
+    const uint8_t* src = smem + st * stage_bytes + col_off;
+    int k = 0;
+    if (MC == 4) {
+      // whole block pairs: A = block blk, B = block blk + 1; prev holds block blk - 1
+      for (; k + 8 <= n; k += 8) {
+        const float4 wa = *reinterpret_cast<const float4*>(gw + r0 + k);
+        const float4 wb = *reinterpret_cast<const float4*>(gw + r0 + k + 4);
+        row_acc(cur, src + (k + 0) * pitch, wa.x, true);
+        row_acc(cur, src + (k + 1) * pitch, wa.y, false);
+        row_acc(cur, src + (k + 2) * pitch, wa.z, false);
+        row_acc(cur, src + (k + 3) * pitch, wa.w, false);
+        finish(blk, prev, cur);
+        row_acc(prev, src + (k + 4) * pitch, wb.x, true);
+        row_acc(prev, src + (k + 5) * pitch, wb.y, false);
+        row_acc(prev, src + (k + 6) * pitch, wb.z, false);
+        row_acc(prev, src + (k + 7) * pitch, wb.w, false);
+        finish(blk + 1, cur, prev);
+        blk += 2;
+      }
+      blk_end = min((blk + 1) * m, nrows);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) cur[e] = 0.f;
+    }
+    for (; k < n; ++k) {
+      const int r = r0 + k;
+      row_acc(cur, src + k * pitch, gw[r], false);
+      if (r + 1 == blk_end) {
+        finish(blk, prev, cur);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          prev[e] = cur[e];
+          cur[e] = 0.f;
+        }
+        ++blk;
+        blk_end = min((blk + 1) * m, nrows);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  if (!active) return;
+  // the last CSA slot whose second block is past the sequence end
+  if (nb - 1 < nj) {
+    const float fa = fab[nb - 1].x;
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = prev[e] * fa;
+    store8(csa_out + static_cast<int64_t>(nb - 1) * so0, o);
+  }
+  store8(hca_out, hacc);
+}
+
+// One-pass CSA + HCA pooling on the bulk-copy pipeline; false (nothing
+// launched) for shapes it does not take.
+template <typename T>
+static bool compress_dual_typed(const CompressArgs& csa, const CompressArgs& hca, cudaStream_t st, int* err) {
+  const CompressArgs& a = csa;
+  if (!a.cu_seqlens || !hca.cu_seqlens) return false;
+  if (csa.window != 2 * csa.stride || hca.window != hca.stride || hca.stride % csa.stride) return false;
+  if (csa.stride > 64 || hca.stride + csa.stride > 2048) return false;
+  const int nk = a.head_dim / 8, nv = a.head_dim_v / 8;
+  if (a.head_dim % 8 || a.head_dim_v % 8 || nk + nv > 256 || nk == 0 || !a.v) return false;
+  if (a.sk[2] != 1 || a.sv[2] != 1 || a.sk[0] % 8 || a.sk[1] % 8 || a.sv[0] % 8 || a.sv[1] % 8) return false;
+  if ((reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v)) & 15) return false;
+  for (const CompressArgs* o : {&csa, &hca}) {
+    if (o->sck[2] != 1 || o->scv[2] != 1 || o->sck[0] % 8 || o->sck[1] % 8 || o->scv[0] % 8 || o->scv[1] % 8)
+      return false;
+    if ((reinterpret_cast<uintptr_t>(o->ck) | reinterpret_cast<uintptr_t>(o->cv)) & 15) return false;
+  }
+  const int row_bytes = (nk + nv) * 16;
+  const int ch = max(8, min(32, cb::kChunkBytes / row_bytes));
+  const int nst = max(2, min(cb::kMaxStages, cb::kRingBytes / (row_bytes * ch)));
+  const int rows_max = hca.stride + csa.stride, nb_max = rows_max / csa.stride + 1;
+  const int smem = nst * row_bytes * ch + 2 * nst * 8 + (rows_max + 6 * nb_max + 4) * 4;
+  const int threads = ((nk + nv + 31) / 32 + 1) * 32;
+  const int span = (a.sk[0] * 2 == nk * 16 && a.sv[0] * 2 == nv * 16) ? 1 : 0;
+  auto kern = (csa.stride == 4 && ch % 8 == 0) ? compress_dual_kernel<T, 4> : compress_dual_kernel<T, 0>;
+  if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
+  kern<<<dim3(static_cast<unsigned>(hca.num_compressed), a.num_kv_heads), threads, smem, st>>>(csa, hca, ch, nst,
+                                                                                              span);
+  return true;
+}
+
+bool compress_dual_launch(const CompressArgs& csa, const CompressArgs& hca, cudaStream_t st, int* err) {
+  *err = 0;
+  if (csa.dtype == kBF16) return compress_dual_typed<__nv_bfloat16>(csa, hca, st, err);
+  if (csa.dtype == kF16) return compress_dual_typed<__half>(csa, hca, st, err);
+  return false;
+}
+
 // Takes plain-mean pooling of 16-bit rows whose every stride is a multiple of
 // 8 elements, with windows of one or two strides.  Returns false (nothing
 // launched) for anything else.

@@ -599,6 +599,8 @@ static int compress_csa_hca_typed(const CompressArgs& csa, const CompressArgs& h
 
 int compress_csa_hca_launch(const CompressArgs& csa, const CompressArgs& hca, cudaStream_t st) {
   if (hca.num_compressed == 0 || csa.num_kv_heads == 0) return 0;
+  int err = 0;
+  if (compress_dual_launch(csa, hca, st, &err)) return err;
   bool handled = false;
   int r = 0;
   if (csa.dtype == kBF16) r = compress_csa_hca_typed<__nv_bfloat16>(csa, hca, st, &handled);

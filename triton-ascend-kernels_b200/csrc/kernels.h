@@ -109,6 +109,9 @@ int compress_launch(const CompressArgs& a, cudaStream_t st);
 // gate).  Returns false, launching nothing, for other shapes; *err is the
 // launch status when it returns true.
 bool compress_bulk_launch(const CompressArgs& a, cudaStream_t st, int* err);
+// CSA + HCA pooling of the same TND rows in one pass on the bulk-copy
+// pipeline (one CTA per HCA slot); false (nothing launched) when it does not apply.
+bool compress_dual_launch(const CompressArgs& csa, const CompressArgs& hca, cudaStream_t st, int* err);
 // CSA (window 2m, stride m) and HCA (window = stride = m') pooling of the same
 // K/V/gate in one pass; falls back to two compress_launch calls for shapes the
 // fused kernel does not take.
