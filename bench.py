@@ -575,7 +575,7 @@ class SparseWL(Workload):
 
 
 class CompressWL(Workload):
-    name, unit, bound, peak_key, kernel = "compress", "GB/s", "hbm", "hbm_gbs", "compress_csa_hca_kernel"
+    name, unit, bound, peak_key, kernel = "compress", "GB/s", "hbm", "hbm_gbs", "compress_dual_kernel"
     desc = ("CSA + HCA KV compression: 65536 tokens (16 sequences x 4096) x 512 dims bf16 K and V plus per-token "
             "fp32 gate logits; CSA stride 4 (8-token windows, as the reference's csa.py) and HCA 128-token "
             "windows, gate-softmax-weighted sums")
