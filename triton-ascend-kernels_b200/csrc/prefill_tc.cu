@@ -293,8 +293,16 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32(s_tmem + hh * 64 + 32, sr + 32);
         tmem_ld_wait();
         if (interior) {
+          // four independent chains of three-input maxima (two scores each)
+          float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+          for (int c = 0; c < 64; c += 8) {
+            mx = fmax3(mx, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+            m1 = fmax3(m1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+            m2 = fmax3(m2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+            m3 = fmax3(m3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+          }
+          mx = fmax3(mx, m1, fmaxf(m2, m3));
         } else {
 #pragma unroll
           for (int c = 0; c < 64; ++c) mx = fmaxf(mx, hh * 64 + c < nvalid ? __uint_as_float(sr[c]) : -INFINITY);
