@@ -349,10 +349,24 @@ __global__ void __launch_bounds__(288, 1)
       uint32_t sr[32];
       tmem_ld16x2(taddr + s_lane + b * 64, sr);
       tmem_ld_wait();
+      // every column of the warp's tile valid (the common case): no per-score tests
+      const bool all_valid = __all_sync(0xffffffffu, vbits == 0xffffffffu);
       float mx = -INFINITY;
+      if (all_valid) {
+        float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        if ((vbits >> c) & 1u) mx = fmaxf(mx, __uint_as_float(sr[c]));
+        for (int c = 0; c < 32; c += 8) {
+          mx = fmax3(mx, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+          m1 = fmax3(m1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+          m2 = fmax3(m2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+          m3 = fmax3(m3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+        }
+        mx = fmax3(mx, m1, fmaxf(m2, m3));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if ((vbits >> c) & 1u) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
       const float m_new = fmaxf(m_run, mx * p.scale_log2);
       const bool need = m_new != -INFINITY && m_new > m_used + 8.f;
@@ -378,13 +392,32 @@ __global__ void __launch_bounds__(288, 1)
       const float mu = m_used == -INFINITY ? 0.f : m_used;
       uint32_t pk[16];
       float ls = 0.f;
+      if (all_valid) {
+        // two scores per packed fp32 FMA (same rounding as the scalar form) and per packed row-sum add
+        const uint64_t sl2x2 = (static_cast<uint64_t>(__float_as_uint(p.scale_log2)) << 32) |
+                               __float_as_uint(p.scale_log2);
+        const uint64_t nmux2 = (static_cast<uint64_t>(__float_as_uint(-mu)) << 32) | __float_as_uint(-mu);
+        uint64_t lsx2 = 0;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const float a = ((vbits >> (2 * c)) & 1u) ? fast_exp2(__uint_as_float(sr[2 * c]) * p.scale_log2 - mu) : 0.f;
-        const float bb =
-            ((vbits >> (2 * c + 1)) & 1u) ? fast_exp2(__uint_as_float(sr[2 * c + 1]) * p.scale_log2 - mu) : 0.f;
-        ls += a + bb;
-        pk[c] = Elem<T>::pack2(a, bb);
+        for (int c = 0; c < 16; ++c) {
+          uint64_t x = (static_cast<uint64_t>(sr[2 * c + 1]) << 32) | sr[2 * c];
+          asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(x) : "l"(sl2x2), "l"(nmux2));
+          const float a = fast_exp2(__uint_as_float(static_cast<uint32_t>(x)));
+          const float bb = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
+          const uint64_t ab = (static_cast<uint64_t>(__float_as_uint(bb)) << 32) | __float_as_uint(a);
+          asm("add.rn.f32x2 %0, %0, %1;" : "+l"(lsx2) : "l"(ab));
+          pk[c] = Elem<T>::pack2(a, bb);
+        }
+        ls = __uint_as_float(static_cast<uint32_t>(lsx2)) + __uint_as_float(static_cast<uint32_t>(lsx2 >> 32));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float a = ((vbits >> (2 * c)) & 1u) ? fast_exp2(__uint_as_float(sr[2 * c]) * p.scale_log2 - mu) : 0.f;
+          const float bb =
+              ((vbits >> (2 * c + 1)) & 1u) ? fast_exp2(__uint_as_float(sr[2 * c + 1]) * p.scale_log2 - mu) : 0.f;
+          ls += a + bb;
+          pk[c] = Elem<T>::pack2(a, bb);
+        }
       }
       l += ls;
       if (j >= 1 && !(ok = mbar_wait(p_free, (j - 1) & 1))) break;
