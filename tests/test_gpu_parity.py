@@ -468,16 +468,19 @@ def test_compress_csa_hca(dtype, gated):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("gated", [False, True])
-@pytest.mark.parametrize("shape", ["ragged", "latent512", "strided", "m3"])
+@pytest.mark.parametrize("shape", ["ragged", "latent512", "heads2x256", "strided", "m3"])
 def test_compress_csa_hca_one_pass(dtype, gated, shape):
     """CSA + HCA pooling of the same K/V in one launch vs the oracle's two
     separate poolings: ragged lengths (empty, shorter than m, chunk-straddling
-    tails), 512-dim latent rows, a strided K/V view, and m = 3 (m' = 128 not a
-    multiple of m: the two-pass path)."""
+    tails), 512-dim latent rows, two KV heads of 256-dim K and V (1 KB rows:
+    the block-pair path of the bulk kernel on a multi-head grid), a strided
+    K/V view, and m = 3 (m' = 128 not a multiple of m: the two-pass path)."""
     g = torch.Generator().manual_seed(71)
     m, mp, hkv, D, Dv = 4, 128, 2, 128, 256
     if shape == "latent512":
         lens, hkv, D, Dv = [4096, 77, 4096], 1, 512, 512
+    elif shape == "heads2x256":
+        lens, hkv, D, Dv = [300, 0, 1, 1030, 129], 2, 256, 256
     else:
         lens = [0, 3, 4, 5, 130, 257, 1, 0, 132]
     if shape == "m3":
