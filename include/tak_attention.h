@@ -192,11 +192,13 @@ int tak_compress_kv_paged(const void* k_cache, const int64_t* k_strides, const v
  * outputs of compress_kv_overlap (attention/csa.py:9-69, window 2m, stride m,
  * offsets csa_offsets) and the HCA outputs of compress_kv_simple
  * (attention/hca.py:9-69, window = stride = m_prime, offsets hca_offsets),
- * which the reference computes with two separate passes over K/V.  Shapes the
- * single-pass kernel does not take (fp32, m_prime not a multiple of m,
- * m_prime + m > 256, head dims not multiples of 128, unaligned strides) run as
- * two tak_compress_kv passes with the same results.  total_tokens = rows of
- * K/V/gate. */
+ * which the reference computes with two separate passes over K/V.  One pass
+ * runs on the bulk-copy kernel when the inputs are 16-bit with strides in
+ * multiples of 8 elements, m_prime is a multiple of m, m <= 64, m_prime + m
+ * <= 2048 and head_dim + head_dim_v <= 2048; else on the TMA-box kernel when
+ * m_prime + m <= 256 and the head dims are multiples of 128; other shapes
+ * (fp32 among them) run as two tak_compress_kv passes with the same results.
+ * total_tokens = rows of K/V/gate. */
 int tak_compress_kv_csa_hca(const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
                             const float* gate, int64_t gate_stride, const int32_t* cu_seqlens, int64_t num_seqs,
                             int64_t total_tokens, const int32_t* csa_offsets, int64_t num_csa, void* csa_k,
