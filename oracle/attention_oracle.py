@@ -273,6 +273,8 @@ def compress_kv(k, v, cu_seqlens, stride, window, gate=None, acc=np.float64):
     (HCA:49-55).  ``gate=None`` gives the reference's plain mean; ``gate [T]``
     (fp32 logits) gives the softmax(gate)-weighted sum over the window's rows --
     an extension with no counterpart in the reference (parity unpinned there).
+    A -inf logit masks its row (weight 0); a window whose logits are all -inf
+    pools to zeros.
     Returns (ck [Nc,H_kv,D], cv [Nc,H_kv,Dv], comp_offsets [S+1] int32).
     """
     k, v = _np(k, acc), _np(v, acc)
@@ -290,7 +292,10 @@ def compress_kv(k, v, cu_seqlens, stride, window, gate=None, acc=np.float64):
                 ck[offs[si] + i] = k[a:b].mean(0)
                 cv[offs[si] + i] = v[a:b].mean(0)
             else:
-                w = np.exp(g[a:b] - g[a:b].max())
+                gmax = g[a:b].max()
+                if gmax == -np.inf:  # every row masked
+                    continue
+                w = np.exp(g[a:b] - gmax)
                 w = w / w.sum()
                 ck[offs[si] + i] = np.tensordot(w, k[a:b], 1)
                 cv[offs[si] + i] = np.tensordot(w, v[a:b], 1)

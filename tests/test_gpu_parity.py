@@ -503,6 +503,43 @@ def test_compress_csa_hca_one_pass(dtype, gated, shape):
         close(gv, rv, 1e-2)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("one_pass", [True, False])
+def test_compress_masked_gates(dtype, one_pass):
+    """Gate logits of -inf mask their rows: a partly masked window pools its
+    other rows, a window (here also a whole HCA slot and a whole short
+    sequence) with every row masked pools to zeros -- in the one-pass
+    compressor, in the separate CSA and HCA compressors and in the oracle."""
+    lens = [300, 9, 256, 131]
+    Tn = sum(lens)
+    g = torch.Generator().manual_seed(91)
+    k = torch.randn(Tn, 1, 512, generator=g).to(DEV, dtype)
+    v = torch.randn(Tn, 1, 512, generator=g).to(DEV, dtype)
+    gate = torch.randn(Tn, generator=g)
+    ninf = float("-inf")
+    gate[0:8] = ninf               # the first CSA window of sequence 0, entirely
+    gate[20] = ninf                # single rows
+    gate[50:53] = ninf
+    gate[300:309] = ninf           # all of sequence 1
+    gate[309:309 + 128] = ninf     # the first HCA slot of sequence 2
+    gate[Tn - 1] = ninf
+    gate = gate.to(DEV)
+    cuq = _cu_t(lens)
+    if one_pass:
+        (ck, cv, co), (hk, hv, ho) = CSA.compress_kv_csa_hca(k, v, cuq, 4, 128, gate=gate)
+    else:
+        ck, cv, co = CSA.compress_kv_overlap(k, v, cuq, 4, gate=gate)
+        hk, hv, ho = HCA.compress_kv_simple(k, v, cuq, 128, gate=gate)
+    tol = TOL32 if dtype == torch.float32 else 1e-2
+    for (gk, gv, go), (stride, window) in (((ck, cv, co), (4, 8)), ((hk, hv, ho), (128, 128))):
+        rk, rv, roffs = O.compress_kv(npy(k), npy(v), cuq.cpu(), stride, window, gate.cpu())
+        np.testing.assert_array_equal(go.cpu().numpy(), roffs)
+        assert torch.isfinite(gk).all() and torch.isfinite(gv).all()
+        close(gk, rk, tol)
+        close(gv, rv, tol)
+    assert float(ck[0].abs().max()) == 0.0 and float(hk[3].abs().max()) == 0.0  # all-masked windows
+
+
 def test_compress_paged_matches_tnd():
     q, kc, vc, bt, cl = _paged_case(5, 8, 2, 128, 16, 300, 120, torch.bfloat16, 33, [0, 17, 300, 64, 1])
     ck, cv, offs, lens, _ = T.compress_paged(kc, vc, bt, cl, 16, 4, 8)

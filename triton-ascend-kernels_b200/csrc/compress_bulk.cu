@@ -402,7 +402,8 @@ __global__ void __launch_bounds__(288) compress_dual_kernel(const CompressArgs c
     for (int r = r0; r < r1; ++r) mx = fmaxf(mx, gw[r]);
     float sum = 0.f;
     for (int r = r0; r < r1; ++r) {
-      const float w = __expf(gw[r] - mx);
+      // a block whose logits are all -inf (masked rows) carries no weight
+      const float w = mx == -INFINITY ? 0.f : __expf(gw[r] - mx);
       gw[r] = w;
       sum += w;
     }
@@ -417,7 +418,7 @@ __global__ void __launch_bounds__(288) compress_dual_kernel(const CompressArgs c
     mh = warp_max(mh);
     float hs = 0.f;
     for (int b = lane; b < nbh; b += 32) {
-      const float f = __expf(bm[b] - mh);
+      const float f = bm[b] == -INFINITY ? 0.f : __expf(bm[b] - mh);
       bh[b] = f;
       hs += f * bs[b];
     }
@@ -428,7 +429,8 @@ __global__ void __launch_bounds__(288) compress_dual_kernel(const CompressArgs c
     for (int j = lane; j < nj; j += 32) {
       const bool two = j + 1 < nb;
       const float ma = bm[j], mb = two ? bm[j + 1] : -INFINITY, Mx = fmaxf(ma, mb);
-      const float fa = __expf(ma - Mx), fb = two ? __expf(mb - Mx) : 0.f;
+      const float fa = ma == -INFINITY ? 0.f : __expf(ma - Mx);
+      const float fb = mb == -INFINITY ? 0.f : __expf(mb - Mx);
       const float den = bs[j] * fa + (two ? bs[j + 1] * fb : 0.f);
       const float inv = den > 0.f ? 1.f / den : 0.f;
       fab[j] = make_float2(fa * inv, fb * inv);

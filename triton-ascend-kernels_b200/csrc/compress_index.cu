@@ -55,13 +55,17 @@ __global__ void compress_kernel(const CompressArgs a) {
       gmax = fmaxf(gmax, g);
     }
     gsum = 0.f;
-    for (int r = r0; r < r1; ++r) {
-      const float g = paged ? a.gate[a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]] * a.sg[0] +
-                                     (r % a.block_size) * a.sg[1]]
-                            : a.gate[(a.cu_seqlens[s] + r) * a.sg[0]];
-      gsum += __expf(g - gmax);
+    // a window whose logits are all -inf (every row masked) pools to zeros
+    if (gmax != -INFINITY) {
+      for (int r = r0; r < r1; ++r) {
+        const float g = paged ? a.gate[a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]] * a.sg[0] +
+                                       (r % a.block_size) * a.sg[1]]
+                              : a.gate[(a.cu_seqlens[s] + r) * a.sg[0]];
+        gsum += __expf(g - gmax);
+      }
     }
   }
+  const bool all_masked = a.gate && gmax == -INFINITY;
   float acc[VEC];
 #pragma unroll
   for (int e = 0; e < VEC; ++e) acc[e] = 0.f;
@@ -71,11 +75,11 @@ __global__ void compress_kernel(const CompressArgs a) {
     if (paged) {
       const int64_t page = a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]];
       row = base + page * st[0] + h * st[1] + (r % a.block_size) * st[2];
-      if (a.gate) w = __expf(a.gate[page * a.sg[0] + (r % a.block_size) * a.sg[1]] - gmax);
+      if (a.gate) w = all_masked ? 0.f : __expf(a.gate[page * a.sg[0] + (r % a.block_size) * a.sg[1]] - gmax);
     } else {
       const int64_t tok = a.cu_seqlens[s] + r;
       row = base + tok * st[0] + h * st[1];
-      if (a.gate) w = __expf(a.gate[tok * a.sg[0]] - gmax);
+      if (a.gate) w = all_masked ? 0.f : __expf(a.gate[tok * a.sg[0]] - gmax);
     }
     if constexpr (VEC == 8) {
       const uint4 u = *reinterpret_cast<const uint4*>(row + d0);
@@ -176,7 +180,7 @@ __global__ void __launch_bounds__(128) compress_stream_kernel(const CompressArgs
             for (int e = 0; e < 8; ++e) cur[e] *= f;
             cm = gv[k];
           }
-          w = __expf(gv[k] - cm);
+          w = gv[k] == -INFINITY ? 0.f : __expf(gv[k] - cm);  // a -inf logit masks its row
           cs += w;
         }
         const uint32_t* pw = reinterpret_cast<const uint32_t*>(&u[k]);
@@ -194,7 +198,8 @@ __global__ void __launch_bounds__(128) compress_stream_kernel(const CompressArgs
             if (a.gate) {
               float M = cm, S = cs;
               if (WIN_BLOCKS == 2) M = fmaxf(pm, cm);
-              const float fc = __expf(cm - M), fp = WIN_BLOCKS == 2 ? __expf(pm - M) : 0.f;
+              const float fc = cm == -INFINITY ? 0.f : __expf(cm - M);
+              const float fp = (WIN_BLOCKS == 2 && pm != -INFINITY) ? __expf(pm - M) : 0.f;
               S = cs * fc + (WIN_BLOCKS == 2 ? ps * fp : 0.f);
               const float inv = S > 0.f ? 1.f / S : 0.f;
 #pragma unroll
@@ -321,7 +326,7 @@ __global__ void __launch_bounds__(512) compress_split_kernel(const CompressArgs 
           for (int e = 0; e < 8; ++e) acc[e] *= f;
           gm = gv[k];
         }
-        w = __expf(gv[k] - gm);
+        w = gv[k] == -INFINITY ? 0.f : __expf(gv[k] - gm);  // a -inf logit masks its row
         gs += w;
       }
       const uint32_t* pw = reinterpret_cast<const uint32_t*>(&u[k]);
