@@ -579,14 +579,16 @@ def _indexer_on_cores(q, ck, cuq, offs, n_win, top_k, m):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("top_k", [16, 48, 300])
-@pytest.mark.parametrize("rows", ["many", "few", "many-cores"])
+@pytest.mark.parametrize("rows", ["many", "few", "many-cores", "long"])
 def test_csa_indexer_bit_exact(dtype, top_k, rows):
     """Lightning indexer on 512-dim compressed keys; ties and fewer-than-k
     causal slots included (short sequences).  top_k 16 takes the
     repeated-argmax selection, 48 and 300 the sorted one (up to 525 slots).
     "many" (2856 query rows) and "few" (271 rows: the 512-thread selection)
-    score on the tensor cores; "many-cores" scores each row on CUDA cores."""
-    lens = [3, 40, 200, 513, 2100] if rows != "few" else [3, 8, 260]
+    score on the tensor cores; "many-cores" scores each row on CUDA cores;
+    "long" has a 6000-token sequence (1500 slots: past the one-warp-per-row
+    selection, so the tensor-core scores go to the shared-memory sort)."""
+    lens = {"few": [3, 8, 260], "long": [6000, 37]}.get(rows, [3, 40, 200, 513, 2100])
     Tn = sum(lens)
     g = torch.Generator().manual_seed(41)
     q = torch.randn(Tn, 4, 512, generator=g).to(DEV, dtype)
