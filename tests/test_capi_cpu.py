@@ -137,3 +137,84 @@ def test_prefix_view_and_slot_bounds():
     assert T.max_slots_per_seq(bt, 128, 4) == 2048          # 64 pages x 128 rows / m
     assert T.max_slots_per_seq(bt, 128, 128) == 64
     assert T.max_slots_per_seq(torch.zeros(4, 0, dtype=torch.int32), 16, 4) == 1
+
+
+def _header_params():
+    """{entry point: [parameter names]} parsed from tak_attention.h."""
+    src = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(tak_\w+)\s*\(([^)]*)\)\s*;", src):
+        ps = [p.strip() for p in params.split(",") if p.strip() and p.strip() != "void"]
+        out[name] = [re.findall(r"(\w+)\s*$", p)[0] for p in ps]
+    return out
+
+
+def _call_invalid(name, **vals):
+    """Call entry point `name` with null pointers, zero sizes and `vals`."""
+    params = _header_params()[name]
+    argtypes = T._SIGS[name][0]
+    assert len(params) == len(argtypes), name
+    unknown = set(vals) - set(params)
+    assert not unknown, (name, unknown)
+    args = [vals.get(p, None if t is T._P else (1.0 if t is T._F32 else 0)) for p, t in zip(params, argtypes)]
+    rc = getattr(T.lib(), name)(*args)
+    return rc, T.lib().tak_last_error().decode()
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="argument checks only, on a machine without a GPU")
+@pytest.mark.parametrize("name,vals,msg", [
+    ("tak_flash_attention_prefill", dict(dtype=5, num_q_heads=8, num_kv_heads=2, head_dim=128), "unknown dtype"),
+    ("tak_flash_attention_prefill", dict(dtype=1, num_q_heads=8, num_kv_heads=3, head_dim=128), "heads"),
+    ("tak_flash_attention_prefill", dict(dtype=1, num_q_heads=8, num_kv_heads=2, head_dim=1000), "head_dim"),
+    ("tak_flash_attention_prefill", dict(dtype=1, num_q_heads=8, num_kv_heads=2, head_dim=128, num_seqs=1,
+                                         total_tokens=4), "null"),
+    ("tak_paged_attention_decode", dict(dtype=1, num_q_heads=32, num_kv_heads=8, head_dim=128, block_size=256,
+                                        cache_rows=128), "block_size"),
+    ("tak_paged_attention_decode", dict(dtype=1, num_q_heads=32, num_kv_heads=8, head_dim=128, block_size=16,
+                                        cache_rows=16, num_seqs=2, max_blocks=4, num_blocks=8), "null"),
+    ("tak_sparse_attn_prefill", dict(dtype=1, total_tokens=4, num_q_heads=64, num_kv_heads=1, head_dim=576,
+                                     head_dim_v=0), "head dims"),
+    ("tak_sparse_attn_decode", dict(dtype=1, num_seqs=2, num_q_heads=64, num_kv_heads=1, head_dim=512,
+                                    head_dim_v=512, k_topk=-1), "negative"),
+    ("tak_compress_kv", dict(dtype=1, stride=0, window=8, num_kv_heads=1, head_dim=512, num_compressed=4),
+     "stride"),
+    # no V given but a V head dim: the K-only form needs head_dim_v = 0
+    ("tak_compress_kv_paged", dict(dtype=1, stride=4, window=8, num_kv_heads=1, head_dim=512, head_dim_v=512,
+                                   num_compressed=4), "head sizes"),
+    ("tak_compress_kv_csa_hca", dict(dtype=1, m=0, m_prime=128, num_csa=4, num_kv_heads=1, head_dim=512,
+                                     head_dim_v=512), "null v"),
+    ("tak_build_window_idxs", dict(num_seqs=1, total_tokens=4, n_win=8, ld=4), "bad arguments"),
+    ("tak_build_decode_topk_idxs", dict(num_seqs=1, n_win=8, n_comp_cols=4, ld=8), "decode idxs"),
+    ("tak_comp_offsets", dict(num_seqs=1, stride=0), "comp offsets"),
+    ("tak_csa_indexer_topk", dict(dtype=1, m=4, top_k=32, n_win=8, ld=16, num_q_heads=8, num_kv_heads=1,
+                                  head_dim=512), "null pointer"),
+    ("tak_build_token_to_seq", dict(num_seqs=-1, total_tokens=4), "token_to_seq"),
+])
+def test_c_abi_rejects_invalid_arguments(name, vals, msg):
+    """Every entry point validates its arguments before touching the device:
+    status 1 (invalid argument) and a message naming the problem, the C-side
+    counterpart of the reference wrappers' asserts (FP:124-133, PD:120-129,
+    SA:274-280, SA:337-343)."""
+    if not os.path.exists(T.LIB_PATH):
+        pytest.skip("libtak_b200.so not built")
+    rc, err = _call_invalid(name, **vals)
+    assert rc == 1, (name, rc, err)
+    assert msg in err, (name, err)
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="argument checks only, on a machine without a GPU")
+@pytest.mark.parametrize("name,vals", [
+    ("tak_sparse_attn_prefill", dict(total_tokens=0)),
+    ("tak_sparse_attn_decode", dict(num_seqs=0)),
+    ("tak_compress_kv", dict(num_compressed=0)),
+    ("tak_compress_kv_paged", dict(num_compressed=0)),
+    ("tak_compress_kv_csa_hca", dict(num_csa=0, num_hca=0)),
+])
+def test_c_abi_empty_inputs_succeed(name, vals):
+    """Empty inputs (no tokens, requests or slots) return 0 with nothing
+    launched and no pointer read, where the reference's host loops simply do
+    nothing."""
+    if not os.path.exists(T.LIB_PATH):
+        pytest.skip("libtak_b200.so not built")
+    rc, err = _call_invalid(name, **vals)
+    assert rc == 0, (name, rc, err)
