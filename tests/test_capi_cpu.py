@@ -89,6 +89,25 @@ def test_cpu_tensors_rejected_like_the_reference():
         SA.sparse_attn_prefill(q, q[:, :1], q[:, :1], torch.zeros(4, 2, dtype=torch.int32), None)
 
 
+def test_missing_library_raises(monkeypatch):
+    """Without libtak_b200.so the first call raises: there is no fallback."""
+    monkeypatch.setattr(T, "LIB_PATH", os.path.join(REPO, "no-such-dir", "libtak_b200.so"))
+    monkeypatch.setattr(T, "_lib", None)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        T.lib()
+
+
+def test_product_modules_do_not_use_the_oracle():
+    """The drop-in modules and the C ABI sources neither import nor name the
+    CPU oracle (it is test infrastructure only)."""
+    pkg = os.path.join(REPO, "triton-ascend-kernels_b200")
+    for root, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".h")):
+                src = open(os.path.join(root, f)).read()
+                assert "oracle" not in src, f"{f} names the oracle"
+
+
 def test_paged_decode_block_n_assertion():
     import paged_attention_decode as PD
 
