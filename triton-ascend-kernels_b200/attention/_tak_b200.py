@@ -118,9 +118,9 @@ _ws = {}
 
 
 def workspace(device, stream_handle, nbytes):
-    """Per-(device, stream) scratch buffer, grown on demand.  Zero-filled when
-    allocated: the decode kernel keeps its arrival counters in it and leaves
-    them zero after every call."""
+    """Per-(device, stream) scratch buffer, grown on demand.  Its contents do
+    not matter between calls: the decode combine only reads split partials
+    written earlier in the same call (the zero fill is not relied on)."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), int(stream_handle.value or 0))
     buf = _ws.get(key)
     if buf is None or buf.numel() < nbytes:
