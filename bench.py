@@ -316,7 +316,7 @@ def run_decode_ours(args, rank, world, device):
     gbs = nbytes_all / (ms * 1e-3) / 1e9
     per_launch_gbs = nbytes / (ms * 1e-3) / 1e9
     hbm = pk["hbm_gbs"]
-    traffic = profile_traffic("paged_decode_tc_kernel.md")
+    traffic = profile_traffic("paged_decode_tc_kernel_decode_b64_ctx8k.md")
     res = {
         "metric": METRIC,
         "value": round(gbs, 1),
@@ -423,6 +423,9 @@ class Workload:
     sample of it on host inputs through the numpy oracle (CPU baseline and the
     reference arm)."""
     name = unit = bound = peak_key = kernel = desc = ""
+    # ncu summary under profiles/ whose capture is this workload's dominant
+    # launch ("" = none: the roofline's traffic is then null)
+    profile = ""
     graph_free = True  # steps run eagerly (set per run: False while CUDA graphs replay them)
 
     def reference_sample(self):
@@ -462,6 +465,7 @@ def _loguniform_lengths(n, lo, hi, g):
 
 class PrefillWL(Workload):
     name, unit, bound, peak_key, kernel = "prefill", "TFLOP/s", "tensor", "bf16_tflops", "prefill_tc_kernel"
+    profile = "prefill_tc_kernel_varlen_32seq.md"
     desc = ("varlen causal prefill: 32 sequences (one GPU's share of 256), lengths log-uniform in [512, 32768], "
             "64 q heads / 8 KV heads, head_dim 128, bf16")
 
@@ -516,6 +520,7 @@ class PrefillWL(Workload):
 
 class SparseWL(Workload):
     name, unit, bound, peak_key, kernel = "sparse", "TFLOP/s", "tensor", "bf16_tflops", "sparse_tc_kernel"
+    profile = "sparse_tc_kernel_mla_16x4096_top2048.md"
     desc = ("top-k sparse attention with sinks: 16 sequences x 4096 query tokens over a 32768-token latent KV, "
             "MQA 64 heads, QK dim 576 (512 + 64 rope), V dim 512 (view of the latent), bf16, 2048 sorted unique "
             "causal indices per query, per-head sink logits")
@@ -578,6 +583,7 @@ class SparseWL(Workload):
 
 class CompressWL(Workload):
     name, unit, bound, peak_key, kernel = "compress", "GB/s", "hbm", "hbm_gbs", "compress_dual_kernel"
+    profile = "compress_dual_kernel_csa_hca_65536tok.md"
     desc = ("CSA + HCA KV compression: 65536 tokens (16 sequences x 4096) x 512 dims bf16 K and V plus per-token "
             "fp32 gate logits; CSA stride 4 (8-token windows, as the reference's csa.py) and HCA 128-token "
             "windows, gate-softmax-weighted sums")
@@ -767,6 +773,7 @@ def csa_decode_bytes(ctx, n_idx, B, H, D, n_win, top_k, m):
 
 class CsaDecodeWL(Workload):
     name, unit, bound, peak_key, kernel = "csa_decode", "GB/s", "hbm", "hbm_gbs", "compress_bulk_kernel"
+    profile = "compress_bulk_kernel_csa_decode_64req.md"
     desc = ("CSA decode forward over a paged latent cache: 64 requests (one query token each, 64 query heads), "
             "one 512-dim latent KV head used as K and V, bf16, contexts uniform in [1, 8192], page 128; "
             "pooling straight from the pages (m = 4, 8-token windows), Lightning-indexer top-512 + 128-token "
@@ -1130,7 +1137,7 @@ def run_workload_ours(args, rank, world, device, W):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
         "config": dict({"workload": w.desc, "parallelism": f"sequence sharding x{world} (weak scaling)"}, **w.config),
         "roofline": {"bound": w.bound, "achieved": round(per_gpu, 1), "peak": peak, "unit": w.unit,
-                     "frac": round(per_gpu / peak, 4), "traffic": profile_traffic(f"{w.kernel}.md"),
+                     "frac": round(per_gpu / peak, 4), "traffic": profile_traffic(w.profile) if w.profile else None,
                      "peak_source": (f"{pk_kind} {w.peak_key} (burst)" if w.peak_key else
                                      f"{pk_kind} bf16_tflops (burst) for prefill + hbm_gbs for decode"),
                      "algorithmic_work_per_step": w.work,

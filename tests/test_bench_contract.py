@@ -32,3 +32,20 @@ def test_reference_arm_json_line(workload):
     e = d["e2e"]
     assert e["value"] == d["value"] and e["unit"] == d["unit"]
     assert e["h2d_bytes_per_step"] == 0 and e["d2h_bytes_per_step"] == 0
+
+
+def test_roofline_traffic_comes_from_the_workloads_own_capture():
+    """Each workload's roofline `traffic` is read from the ncu summary of that
+    workload's own dominant launch; a workload without one reports null."""
+    sys.path.insert(0, REPO)
+    import bench
+
+    assert bench.profile_traffic("paged_decode_tc_kernel_decode_b64_ctx8k.md") > 1e9
+    for name, w in bench.WORKLOADS.items():
+        if not w.profile:
+            continue
+        path = os.path.join(REPO, "profiles", w.profile)
+        assert os.path.exists(path), (name, w.profile)
+        assert w.kernel in open(path).readline(), (name, w.profile)
+        assert bench.profile_traffic(w.profile) > 0, (name, w.profile)
+    assert not bench.WORKLOADS["csa"].profile     # its summary holds no per-launch traffic of the attention
