@@ -14,7 +14,9 @@ script rebuilds that runner's inputs on the CPU -- same seed, same sequence of
   * ``<case>/out`` (+ ``rows``) the reference output, fp16; for large outputs
                            only the token rows listed in ``rows`` are kept;
   * index tensors (top-k rows, compression offsets) in full, and the compressed
-    K/V of the CSA/HCA runners.
+    K/V of the CSA/HCA runners;
+  * in ``reference_edges.npz``: the index builders and mean compressors on edge
+    lengths and strides (``main_edges``), inputs included.
 
 The reference's Triton kernels need an Ascend NPU and are not run; the torch
 reference functions are what the reference's tests compare them against.
@@ -170,5 +172,50 @@ def main(ref_dir):
     print(f"wrote {len(store)} arrays for {len(meta)} cases")
 
 
+# Edge configurations of the integer index builders and the mean compressors:
+# lengths 0 / 1 / just below, at and above a stride or window, strides 1 to 128,
+# windows longer than every sequence, top_k above the slot count.
+EDGE_LENS = [1, 2, 0, 3, 4, 5, 7, 8, 9, 127, 128, 129, 300]
+EDGE_CSA_M = (1, 3, 4)
+EDGE_HCA_M = (1, 5, 16, 128)
+EDGE_NWIN = (1, 4, 130)
+EDGE_CSA_IDX = ((4, 4, 6), (4, 1, 64), (3, 130, 16))     # (m, n_win, top_k)
+
+
+def main_edges(ref_dir):
+    """reference_edges.npz: inputs (fp16, seed 1) and the reference's own
+    compress_kv_overlap / compress_kv_simple / build_hca_topk_idxs /
+    build_csa_topk_idxs results on EDGE_LENS."""
+    sys.path.insert(0, ref_dir)
+    import csa as CSA
+    import hca as HCA
+
+    g = torch.Generator().manual_seed(1)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(EDGE_LENS)]), dtype=torch.int32)
+    T = int(cu[-1])
+    k = torch.randn(T, 1, 8, generator=g).half()
+    v = torch.randn(T, 1, 8, generator=g).half()
+    q = torch.randn(T, 2, 8, generator=g).half()
+    store = {"cu_seqlens": cu.numpy(), "k": k.numpy(), "v": v.numpy(), "q": q.numpy()}
+    for m in EDGE_CSA_M:
+        ck, cv, offs = CSA.compress_kv_overlap(k, v, cu, m)
+        store[f"csa_m{m}/ck"], store[f"csa_m{m}/cv"], store[f"csa_m{m}/comp_offsets"] = \
+            ck.numpy(), cv.numpy(), offs.numpy()
+    for mp in EDGE_HCA_M:
+        ck, cv, offs = HCA.compress_kv_simple(k, v, cu, mp)
+        store[f"hca_m{mp}/ck"], store[f"hca_m{mp}/cv"], store[f"hca_m{mp}/comp_offsets"] = \
+            ck.numpy(), cv.numpy(), offs.numpy()
+        if mp > 1:
+            for nw in EDGE_NWIN:
+                store[f"hca_m{mp}/topk_idxs_w{nw}"] = HCA.build_hca_topk_idxs(cu, offs, T, nw, mp).numpy()
+    for m, nw, tk in EDGE_CSA_IDX:
+        ck, _, offs = CSA.compress_kv_overlap(k, v, cu, m)
+        store[f"csa_idx_m{m}_w{nw}_k{tk}"] = CSA.build_csa_topk_idxs(q, ck, cu, offs, nw, tk, m).numpy()
+    np.savez_compressed(os.path.join(HERE, "reference_edges.npz"), **store)
+    print(f"wrote {len(store)} edge arrays")
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/attention")
+    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference/attention"
+    main(ref)
+    main_edges(ref)
