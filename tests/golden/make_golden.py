@@ -211,8 +211,73 @@ def main_edges(ref_dir):
     for m, nw, tk in EDGE_CSA_IDX:
         ck, _, offs = CSA.compress_kv_overlap(k, v, cu, m)
         store[f"csa_idx_m{m}_w{nw}_k{tk}"] = CSA.build_csa_topk_idxs(q, ck, cu, offs, nw, tk, m).numpy()
+    _attention_edges(store, g)
     np.savez_compressed(os.path.join(HERE, "reference_edges.npz"), **store)
     print(f"wrote {len(store)} edge arrays")
+
+
+def _attention_edges(store, g):
+    """The reference's torch attention functions on edge lengths: sequences of
+    0, 1, 2 and 63-65 / 129 tokens (prefill, causal and not); contexts of 1,
+    P - 1, P, P + 1 and whole tables (paged decode, P = 16); -1 padding, an
+    all -1 row, with and without sinks (sparse prefill); contexts below the
+    window and compressed rows (sparse decode).  fp16, GQA 4 / 2 or MQA."""
+    import flash_attention_prefill as FP
+    import paged_attention_decode as PD
+    import sparse_attn_fwd as SA
+
+    lens = [1, 2, 0, 63, 64, 65, 129]
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32)
+    T = int(cu[-1])
+    q, k, v = (torch.randn(T, h, 16, generator=g).half() for h in (4, 2, 2))
+    store.update({"fp/cu_seqlens": cu.numpy(), "fp/q": q.numpy(), "fp/k": k.numpy(), "fp/v": v.numpy()})
+    for causal in (True, False):
+        store[f"fp/out_c{int(causal)}"] = FP.torch_prefill_tnd_reference(q, k, v, cu, causal=causal).numpy()
+
+    P = 16
+    ctx = torch.tensor([1, 15, 16, 17, 48, 96], dtype=torch.int32)
+    kc, vc = (torch.randn(40, 2, P, 16, generator=g).half() for _ in range(2))
+    bt = torch.randperm(40, generator=g)[:36].view(6, 6).to(torch.int32)
+    qd = torch.randn(6, 4, 16, generator=g).half()
+    store.update({"pd/q": qd.numpy(), "pd/k_cache": kc.numpy(), "pd/v_cache": vc.numpy(),
+                  "pd/block_tables": bt.numpy(), "pd/context_lens": ctx.numpy()})
+    store["pd/out"] = PD.torch_paged_attention_reference(qd, kc, vc, bt, ctx, P).numpy()
+
+    rows, n_tok = 50, 5
+    ks = torch.randn(rows, 1, 16, generator=g).half()
+    qs = torch.randn(n_tok, 4, 16, generator=g).half()
+    idx = torch.stack([torch.sort(torch.randperm(rows, generator=g)[:12]).values for _ in range(n_tok)])
+    idx = idx.to(torch.int32)
+    idx[1, 6:] = -1
+    idx[2, :] = -1
+    sink = torch.randn(4, generator=g)
+    store.update({"sap/q": qs.numpy(), "sap/k": ks.numpy(), "sap/topk_idxs": idx.numpy(),
+                  "sap/attn_sink": sink.numpy()})
+    cu_s = torch.tensor([0, n_tok], dtype=torch.int32)
+    for s_on in (0, 1):
+        store[f"sap/out_s{s_on}"] = SA.torch_sparse_prefill_reference(
+            qs, ks, ks, idx, cu_s, attn_sink=sink if s_on else None).numpy()
+
+    ctx_d = torch.tensor([1, 3, 16, 17], dtype=torch.int32)
+    n_win, n_comp, K = 4, 9, 10
+    kcd, vcd = (torch.randn(12, 1, P, 16, generator=g).half() for _ in range(2))
+    btd = torch.randperm(12, generator=g)[:8].view(4, 2).to(torch.int32)
+    ck, cv = (torch.randn(n_comp, 1, 16, generator=g).half() for _ in range(2))
+    qdd = torch.randn(4, 4, 16, generator=g).half()
+    idd = torch.full((4, K), -1, dtype=torch.int32)
+    for b in range(4):
+        c = int(ctx_d[b])
+        for i in range(n_win):
+            if c - n_win + i >= 0:
+                idd[b, i] = c - n_win + i
+        pick = torch.sort(torch.randperm(n_comp, generator=g)[:K - n_win - b % 2]).values
+        idd[b, n_win:n_win + pick.shape[0]] = c + pick.to(torch.int32)
+    store.update({"sad/q": qdd.numpy(), "sad/k_cache": kcd.numpy(), "sad/v_cache": vcd.numpy(),
+                  "sad/compressed_k": ck.numpy(), "sad/compressed_v": cv.numpy(), "sad/block_tables": btd.numpy(),
+                  "sad/topk_idxs": idd.numpy(), "sad/context_lens": ctx_d.numpy(), "sad/attn_sink": sink.numpy()})
+    for s_on in (0, 1):
+        store[f"sad/out_s{s_on}"] = SA.torch_sparse_decode_reference(
+            qdd, kcd, vcd, ck, cv, btd, idd, ctx_d, block_size=P, attn_sink=sink if s_on else None).numpy()
 
 
 if __name__ == "__main__":

@@ -8,6 +8,12 @@ Sequence lengths 0, 1, 2, 3, 4, 5, 7, 8, 9, 127, 128, 129 and 300; CSA strides
 most sequences (attention/hca.py:76-146); CSA top-k above the slot count
 (attention/csa.py:76-164).  Offsets and HCA index rows must match bit for bit;
 compressed rows within one fp16 rounding.
+
+The same fixture holds the reference's torch attention functions on edge
+lengths: 0 / 1 / 2 / 63-65 / 129-token sequences in prefill, contexts of 1,
+P - 1, P, P + 1 and whole tables in paged decode, -1 padding and an all -1
+row with and without sinks in sparse prefill, contexts shorter than the
+window in sparse decode.
 """
 import os
 
@@ -67,3 +73,50 @@ def test_csa_index_rows_edges(m, n_win, top_k):
         return torch.matmul(kf16[torch.from_numpy(idxs - T).long()], qlast[t]).numpy()
 
     assert_topk_equivalent(mine, ref, n_win, causal, score_of)
+
+
+# ---------------------------------------------------------------------------
+# attention on edge lengths: the reference's torch functions
+# (flash_attention_prefill.py:177-229, paged_attention_decode.py:157-202,
+# sparse_attn_fwd.py:389-470), fp16; the reference's runner tolerance
+# ---------------------------------------------------------------------------
+
+ATOL = RTOL = 1e-2
+
+
+def _e(name):
+    return EDGE[name].astype(np.float64) if EDGE[name].dtype == np.float16 else EDGE[name]
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_prefill_edge_lengths(causal):
+    cu = EDGE["fp/cu_seqlens"]
+    assert 0 in np.diff(cu) and 1 in np.diff(cu) and 129 in np.diff(cu)
+    out, lse = O.prefill(_e("fp/q"), _e("fp/k"), _e("fp/v"), cu, causal)
+    np.testing.assert_allclose(out, _e(f"fp/out_c{int(causal)}"), atol=ATOL, rtol=RTOL)
+    assert np.isfinite(lse).all()
+
+
+def test_paged_decode_edge_contexts():
+    out, _ = O.paged_decode(_e("pd/q"), _e("pd/k_cache"), _e("pd/v_cache"), EDGE["pd/block_tables"],
+                            EDGE["pd/context_lens"], 16)
+    np.testing.assert_allclose(out, _e("pd/out"), atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("with_sink", [False, True])
+def test_sparse_prefill_padding_and_empty_rows(with_sink):
+    k = _e("sap/k")
+    sink = _e("sap/attn_sink") if with_sink else None
+    out, lse = O.sparse_prefill(_e("sap/q"), k, k, EDGE["sap/topk_idxs"], None, sink)
+    np.testing.assert_allclose(out, _e(f"sap/out_s{int(with_sink)}"), atol=ATOL, rtol=RTOL)
+    assert np.all(out[2] == 0)                 # an all -1 row: zeros, as the reference's l_safe gives
+    assert np.isneginf(lse[2]).all() != with_sink
+
+
+@pytest.mark.parametrize("with_sink", [False, True])
+def test_sparse_decode_short_contexts(with_sink):
+    sink = _e("sad/attn_sink") if with_sink else None
+    out, _ = O.sparse_decode(_e("sad/q"), _e("sad/k_cache"), _e("sad/v_cache"), _e("sad/compressed_k"),
+                             _e("sad/compressed_v"), EDGE["sad/block_tables"], EDGE["sad/topk_idxs"],
+                             EDGE["sad/context_lens"], 4, 16, sink)
+    np.testing.assert_allclose(out, _e(f"sad/out_s{int(with_sink)}"), atol=ATOL, rtol=RTOL)
