@@ -136,6 +136,11 @@ int tak_sparse_attn_prefill(const void* q, const int64_t* q_strides, const void*
  * attention/sparse_attn_fwd.py:317-382 (Triton launch at :359), with its
  * slot-position rule (:151-210): slots < num_win address the paged cache and
  * need 0 <= idx < ctx; later slots address compressed rows idx - ctx.
+ * Precondition, as in the reference kernel (its block-table and cache loads
+ * at :159-170 are bounded by the same two tests only): every valid window
+ * slot lies inside its block-table row (idx < block-table width * block_size)
+ * and that row's entry is a page of the cache.  Neither is checked here;
+ * unlike tak_paged_attention_decode, which ignores rows past the table.
  */
 int tak_sparse_attn_decode(const void* q, const int64_t* q_strides, const void* k_cache, const int64_t* k_strides,
                            const void* v_cache, const int64_t* v_strides, const void* compressed_k,
