@@ -183,7 +183,10 @@ int tak_compress_kv(const void* k, const int64_t* k_strides, const void* v, cons
  * compress of csa_decode_forward (attention/csa.py:225-256) and
  * hca_decode_forward (attention/hca.py:204-232).  gate (optional) is
  * float32 [num_blocks, P] with strides gate_strides[2].  v_cache = NULL
- * pools K alone, as for tak_compress_kv.
+ * pools K alone, as for tak_compress_kv.  Precondition: each sequence's
+ * block-table row covers its context (context_lens[s] <= table width * P)
+ * with valid page ids; the reference's gather raises an IndexError past the
+ * row (attention/csa.py:229-245); this entry point does not check it.
  */
 int tak_compress_kv_paged(const void* k_cache, const int64_t* k_strides, const void* v_cache,
                           const int64_t* v_strides, const float* gate, const int64_t* gate_strides,
