@@ -13,6 +13,9 @@
  *     pointer to a small host array (e.g. q_strides[3] for q[T, H, D]).
  *   - dtype: TAK_F16, TAK_BF16 or TAK_F32; q, k, v and out share it.
  *   - Index tensors (cu_seqlens, block tables, top-k rows, offsets) are int32.
+ *   - cu_seqlens is cumulative: cu_seqlens[0] = 0, non-decreasing, last entry
+ *     <= the row count of the tensors it indexes.  Kernels read it on the
+ *     device and do not check this (nor does the reference).
  *   - lse (optional, may be NULL) is float32 [rows, H] contiguous: the natural
  *     log of the softmax denominator, sink term included; -inf for a row with
  *     no key.  The reference has no LSE output; it is an addition.
