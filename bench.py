@@ -144,28 +144,41 @@ class Clocks:
 DEC = dict(batch=64, q_heads=32, kv_heads=8, head_dim=128, page=128, pool=5000, max_ctx=8192)
 
 
-def decode_inputs(seed, device):
+def decode_inputs(seed, device, world=1, rank=0):
+    """One global batch of 64 x world requests drawn from one seed (context
+    lengths, q), assigned to ranks by the longest-processing-time rule on
+    context length (sharding.shard_requests: the bytes each request streams).
+    Returns this rank's (q, k_cache, v_cache, block_tables, context_lens) and
+    every rank's global request ids.  Each rank holds its own 5000-page pool;
+    its requests' pages are drawn in order from one random permutation of it.
+    At world = 1 this is the single-GPU batch: requests 0..63 in order."""
+    import sharding
     c = DEC
     g = torch.Generator().manual_seed(seed)
-    ctx = torch.randint(1, c["max_ctx"] + 1, (c["batch"],), generator=g, dtype=torch.int64).to(torch.int32)
+    n = c["batch"] * world
+    ctx_all = torch.randint(1, c["max_ctx"] + 1, (n,), generator=g, dtype=torch.int64).to(torch.int32)
     maxb = c["max_ctx"] // c["page"]
     perm = torch.randperm(c["pool"], generator=g).to(torch.int32)
-    bt = torch.zeros(c["batch"], maxb, dtype=torch.int32)
+    q_all = torch.randn(n, c["q_heads"], c["head_dim"], generator=g).to(torch.bfloat16)
+    ids = [sharding.shard_requests(ctx_all, world, r) for r in range(world)]
+    mine = ids[rank]
+    ctx, q = ctx_all[mine], q_all[mine]
+    bt = torch.zeros(ctx.numel(), maxb, dtype=torch.int32)
     i = 0
-    for b in range(c["batch"]):
-        n = (int(ctx[b]) + c["page"] - 1) // c["page"]
-        bt[b, :n] = perm[i:i + n]
-        i += n
-    q = torch.randn(c["batch"], c["q_heads"], c["head_dim"], generator=g).to(torch.bfloat16)
+    for b in range(ctx.numel()):
+        npg = (int(ctx[b]) + c["page"] - 1) // c["page"]
+        bt[b, :npg] = perm[i:i + npg]
+        i += npg
+    assert i <= c["pool"]
     shape = (c["pool"], c["kv_heads"], c["page"], c["head_dim"])
     if device is None:
-        return q, None, None, bt, ctx
+        return q, None, None, bt, ctx, ids
     kc = torch.empty(shape, dtype=torch.bfloat16, device=device)
     vc = torch.empty(shape, dtype=torch.bfloat16, device=device)
-    gd = torch.Generator(device=device).manual_seed(seed + 1000)
+    gd = torch.Generator(device=device).manual_seed(seed + 1000 + rank)
     kc.normal_(generator=gd)
     vc.normal_(generator=gd)
-    return q, kc, vc, bt, ctx
+    return q, kc, vc, bt, ctx, ids
 
 
 def decode_bytes(ctx):
@@ -220,14 +233,84 @@ def host_pages(kc, vc, bt, ctx, sample):
     return out
 
 
+class PipelinedE2E:
+    """End-to-end steps through a public API with host buffers, pipelined:
+    step i's host-to-device copies run on a copy stream while step i - 1
+    computes, and step i - 1's device-to-host copy on a second copy stream
+    while step i computes (two device buffer sets, ordered by events).  The
+    timed region starts before the first copy in and ends after the last copy
+    back, so every step's copies are inside it.  `compute` takes the device
+    copies of `host_inputs` and returns one output tensor or a tuple of them;
+    `outputs` lists their (shape, dtype).  The copies back of consecutive
+    steps are ordered on their stream, so one pinned host set receives them."""
+
+    def __init__(self, host_inputs, compute, outputs, device, copy_back=True):
+        self.hin = [t if t.is_pinned() else t.pin_memory() for t in host_inputs]
+        self.sets = [[torch.empty(t.shape, dtype=t.dtype, device=device) for t in self.hin] for _ in range(2)]
+        self.compute = compute
+        self.copy_back = copy_back
+        self.hout = [torch.empty(sh, dtype=dt).pin_memory() for sh, dt in outputs] if copy_back else None
+        self.h2d = torch.cuda.Stream(device)
+        self.d2h = torch.cuda.Stream(device)
+        self.comp = torch.cuda.current_stream(device)
+        self.ev_in = [torch.cuda.Event() for _ in range(2)]
+        self.ev_done = [torch.cuda.Event() for _ in range(2)]
+        self.device = device
+        self.i = 0
+
+    def h2d_bytes(self):
+        return sum(t.numel() * t.element_size() for t in self.hin)
+
+    def d2h_bytes(self):
+        return sum(t.numel() * t.element_size() for t in self.hout) if self.copy_back else 0
+
+    def step(self):
+        b = self.i % 2
+        with torch.cuda.stream(self.h2d):
+            if self.i >= 2:
+                self.h2d.wait_event(self.ev_done[b])  # step i - 2 has finished with this buffer set
+            for d, h in zip(self.sets[b], self.hin):
+                d.copy_(h, non_blocking=True)
+            self.ev_in[b].record(self.h2d)
+        self.comp.wait_event(self.ev_in[b])
+        o = self.compute(*self.sets[b])
+        outs = o if isinstance(o, (tuple, list)) else (o,)
+        self.ev_done[b].record(self.comp)
+        if self.copy_back:
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(self.ev_done[b])
+                for h, d in zip(self.hout, outs):
+                    h.copy_(d, non_blocking=True)
+            for d in outs:
+                d.record_stream(self.d2h)
+        self.i += 1
+
+    def timed(self, steps, warmup, world):
+        for _ in range(warmup):
+            self.step()
+        torch.cuda.synchronize(self.device)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(self.device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.h2d)
+        for _ in range(steps):
+            self.step()
+        e1.record(self.d2h if self.copy_back else self.comp)
+        torch.cuda.synchronize(self.device)
+        return e0.elapsed_time(e1) / steps
+
+
 def run_decode_ours(args, rank, world, device):
     import paged_attention_decode as PD
     import _tak_b200 as T
+    import sharding
 
     pk, pk_kind = peaks()
-    q, kc, vc, bt, ctx = decode_inputs(1234 + rank, device)
+    q, kc, vc, bt, ctx, ids = decode_inputs(1234, device, world, rank)
     qd, btd, ctxd = q.to(device), bt.to(device), ctx.to(device)
     stream = torch.cuda.current_stream(device)
+    B = q.shape[0]
 
     def step():
         return PD.paged_attention_decode(qd, kc, vc, btd, ctxd, DEC["page"], DEC["page"])
@@ -241,9 +324,9 @@ def run_decode_ours(args, rank, world, device):
     torch.cuda.synchronize(device)
     # launches per step: main kernel (+ split-KV combine when there are splits)
     L = T.lib()
-    ws = L.tak_paged_attention_decode_workspace_size(DEC["batch"], DEC["q_heads"], DEC["kv_heads"], DEC["head_dim"],
+    ws = L.tak_paged_attention_decode_workspace_size(B, DEC["q_heads"], DEC["kv_heads"], DEC["head_dim"],
                                                      DEC["page"], bt.shape[1], 0)
-    launches_per_step = 2 if ws > 256 + DEC["batch"] * DEC["q_heads"] * (DEC["head_dim"] + 2) * 4 else 1
+    launches_per_step = 2 if ws > 0 else 1
 
     if world > 1:
         torch.distributed.barrier()
@@ -263,51 +346,49 @@ def run_decode_ours(args, rank, world, device):
         torch.distributed.barrier()
     nbytes = decode_bytes(ctx)
 
-    # end to end through the public API with host buffers: q / block tables /
-    # context lengths copied in from pinned memory, output copied back, every step
-    qh, bth, ctxh = q.pin_memory(), bt.pin_memory(), ctx.pin_memory()
-    outh = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-    qe, bte, ctxe = torch.empty_like(qd), torch.empty_like(btd), torch.empty_like(ctxd)
-
-    def e2e_step():
-        qe.copy_(qh, non_blocking=True)
-        bte.copy_(bth, non_blocking=True)
-        ctxe.copy_(ctxh, non_blocking=True)
-        o = PD.paged_attention_decode(qe, kc, vc, bte, ctxe, DEC["page"], DEC["page"])
-        outh.copy_(o, non_blocking=True)
-
-    for _ in range(args.warmup):
-        e2e_step()
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize(device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    h2d = qh.numel() * qh.element_size() + bth.numel() * 4 + ctxh.numel() * 4
-    d2h = outh.numel() * outh.element_size()
-
+    # the output gather over NCCL (N > 1): one all_gather_into_tensor of
+    # fixed-size blocks, sizes and placement from the sharding plan
+    gather = sharding.PlannedGather([len(i) for i in ids], ids) if world > 1 else None
     gather_ms = None
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms, float(nbytes)], dtype=torch.float64, device=device)
-        mx = t.clone()
-        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
-        tot = t.clone()
-        torch.distributed.all_reduce(tot, op=torch.distributed.ReduceOp.SUM)
-        ms, e2e_ms, nbytes_all = float(mx[0]), float(mx[1]), float(tot[2])
-        import sharding
-        sharding.concat_rows(out[:1])  # first use of the collectives, untimed
+    if gather is not None:
+        for _ in range(3):
+            gather(out)
         torch.cuda.synchronize(device)
+        torch.distributed.barrier()
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
         g0.record(stream)
-        sharding.concat_rows(out)
+        for _ in range(reps):
+            gather(out)
         g1.record(stream)
         torch.cuda.synchronize(device)
-        gather_ms = g0.elapsed_time(g1)
+        gather_ms = g0.elapsed_time(g1) / reps
+
+    # end to end through the public API with host buffers: q / block tables /
+    # context lengths copied in from pinned memory every step, the output
+    # (gathered from every rank at N > 1) copied back to rank 0's host
+    def e2e_compute(qe, bte, ctxe):
+        o = PD.paged_attention_decode(qe, kc, vc, bte, ctxe, DEC["page"], DEC["page"])
+        return gather(o) if gather is not None else o
+
+    n_all = sum(len(i) for i in ids)
+    e2e = PipelinedE2E([q, bt, ctx], e2e_compute, [((n_all,) + tuple(q.shape[1:]), q.dtype)], device,
+                       copy_back=rank == 0)
+    e2e_ms = e2e.timed(args.steps, args.warmup, world)
+    h2d, d2h = e2e.h2d_bytes(), e2e.d2h_bytes()
+
+    per_rank = None
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, float(nbytes), float(h2d), float(d2h), float(B)], dtype=torch.float64,
+                         device=device)
+        allv = torch.empty(world, t.numel(), dtype=torch.float64, device=device)
+        torch.distributed.all_gather_into_tensor(allv, t)
+        allv = allv.cpu()
+        per_rank = [{"rank": r, "ms": round(float(allv[r, 0]), 4), "e2e_ms": round(float(allv[r, 1]), 4),
+                     "gb": round(float(allv[r, 2]) / 1e9, 4), "requests": int(allv[r, 5])} for r in range(world)]
+        ms, e2e_ms = float(allv[:, 0].max()), float(allv[:, 1].max())
+        nbytes_all = float(allv[:, 2].sum())
+        h2d, d2h = int(allv[:, 3].sum()), int(allv[:, 4].sum())
     else:
         nbytes_all = float(nbytes)
 
@@ -331,11 +412,13 @@ def run_decode_ours(args, rank, world, device):
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) K/V and q, context lengths U[1,8192])",
         "config": {
-            "workload": "paged decode: batch 64 x 1 token, 32 q heads / 8 KV heads, head_dim 128, bf16, "
-                        "ctx U[1,8192], page 128, 5000-page pool, random-permutation block tables",
+            "workload": "paged decode: batch 64 x 1 token per GPU, 32 q heads / 8 KV heads, head_dim 128, bf16, "
+                        "ctx U[1,8192], page 128, 5000-page pool per GPU, random-permutation block tables",
             "per_gpu_batch": DEC["batch"], "kv_pool_bytes": 2 * DEC["pool"] * DEC["kv_heads"] * DEC["page"]
             * DEC["head_dim"] * 2, "l2_policy": "inputs larger than L2 (1.07 GB read per step, 2.6 GB pool)",
-            "parallelism": f"request sharding x{world} (weak scaling)",
+            "parallelism": (f"request sharding x{world}: one batch of {64 * world} requests from one seed, "
+                            "assigned by longest-processing-time on context length (weak scaling)"
+                            if world > 1 else "one GPU"),
             "pct_of_hbm_peak": round(100 * per_launch_gbs / hbm, 1), "pct_of_spec_8tbs": round(per_launch_gbs / 80, 1),
         },
         "roofline": {"bound": "hbm", "achieved": round(per_launch_gbs, 1), "peak": hbm, "unit": "GB/s",
@@ -346,14 +429,21 @@ def run_decode_ours(args, rank, world, device):
                                  else "")},
         "e2e": {"value": round(nbytes_all / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "note": "public paged_attention_decode() with q / block tables / context lengths copied from "
-                        "pinned host memory and the output copied back every step; the KV cache is resident"},
+                "note": "public paged_attention_decode() with q / block tables / context lengths copied from pinned "
+                        "host memory and the output copied back every step, copies on two copy streams overlapping "
+                        "the neighbouring steps' kernels (two buffer sets); the KV cache is resident"
+                        + ("; includes the NCCL all-gather of every rank's output and rank 0's copy of the whole "
+                           "result" if world > 1 else "")},
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clk.summary(),
     }
     if gather_ms is not None:
-        res["config"]["output_all_gather_ms"] = round(gather_ms, 3)
-    if not args.no_cpu_baseline:
+        res["config"]["output_all_gather_ms"] = round(gather_ms, 4)
+        res["config"]["output_all_gather"] = (f"one all_gather_into_tensor of {max(len(i) for i in ids)}-request "
+                                              "blocks (sizes from the sharding plan) + one index_select into "
+                                              "request order, CUDA events over 20 calls")
+        res["config"]["per_rank"] = per_rank
+    if not args.no_cpu_baseline and world == 1:
         threads = os.cpu_count() or 1
         sample = list(range(0, DEC["batch"], 8))
         v, n, dt = cpu_decode_sample(q, ctx, host_pages(kc, vc, bt, ctx, sample), args.cpu_seconds, threads)
@@ -373,7 +463,7 @@ def run_decode_reference(args):
     from oracle import attention_oracle as O
 
     c = DEC
-    q, _, _, bt, ctx = decode_inputs(1234, None)
+    q, _, _, bt, ctx, _ = decode_inputs(1234, None)
     threads = os.cpu_count() or 1
     g = np.random.default_rng(7)
     sample = list(range(0, c["batch"], 4))
@@ -471,9 +561,15 @@ class PrefillWL(Workload):
 
     def setup(self, rank, device):
         import flash_attention_prefill as FP
+        import sharding
         self.FP = FP
-        g = torch.Generator().manual_seed(4321 + rank)
-        self.lens = _loguniform_lengths(4 if SMALL else 32, 512, 32768, g)
+        # one batch of 32 x world sequences from one seed, assigned to ranks by
+        # longest-processing-time on causal attention cost L(L+1)/2
+        g = torch.Generator().manual_seed(4321)
+        lens_all = _loguniform_lengths((4 if SMALL else 32) * self.world, 512, 32768, g)
+        owner = sharding.lpt_assign(sharding.prefill_costs(lens_all), self.world)
+        self.lens = [L for L, o in zip(lens_all, owner) if o == rank]
+        self.rows_per_rank = [sum(L for L, o in zip(lens_all, owner) if o == r) for r in range(self.world)]
         T = sum(self.lens)
         cu = [0]
         for L in self.lens:
@@ -488,24 +584,19 @@ class PrefillWL(Workload):
         self.launches = 1
         self.config = {"sequences": len(self.lens), "total_tokens": T, "max_len": max(self.lens),
                        "l2_policy": f"inputs larger than L2 ({(T * 80 * 128 * 2) / 1e9:.2f} GB of q/k/v)"}
+        if self.world > 1:
+            self.config["assignment"] = (f"one batch of {len(lens_all)} sequences, longest-processing-time on "
+                                         "L(L+1)/2 across ranks")
 
     def step(self):
         return self.FP.flash_attention_prefill(self.q, self.k, self.v, self.cu, True)
 
-    def e2e_setup(self):
-        self.hq, self.hk, self.hv = (t.cpu().pin_memory() for t in (self.q, self.k, self.v))
-        self.hcu = self.cu_h.pin_memory()
-        self.hout = torch.empty(self.q.shape, dtype=self.q.dtype).pin_memory()
-        self.dq, self.dk, self.dv = (torch.empty_like(t) for t in (self.q, self.k, self.v))
-        self.dcu = torch.empty_like(self.cu)
-        return (sum(t.numel() * t.element_size() for t in (self.hq, self.hk, self.hv, self.hcu)),
-                self.hout.numel() * self.hout.element_size())
-
-    def e2e_step(self):
-        for d, h in ((self.dq, self.hq), (self.dk, self.hk), (self.dv, self.hv), (self.dcu, self.hcu)):
-            d.copy_(h, non_blocking=True)
-        o = self.FP.flash_attention_prefill(self.dq, self.dk, self.dv, self.dcu, True)
-        self.hout.copy_(o, non_blocking=True)
+    def e2e_pipeline(self):
+        """Host q / k / v / cu_seqlens in, the output back, through the public
+        flash_attention_prefill()."""
+        def fn(q, k, v, cu):
+            return self.FP.flash_attention_prefill(q, k, v, cu, True)
+        return [self.q.cpu(), self.k.cpu(), self.v.cpu(), self.cu_h], fn, [(tuple(self.q.shape), self.q.dtype)]
 
     def reference_sample(self):
         from oracle import attention_oracle as O
@@ -531,6 +622,7 @@ class SparseWL(Workload):
         S, QT, KVL, K = (1 if SMALL else 16), 4096, 32768, 2048
         gd = torch.Generator(device=device).manual_seed(77 + rank)
         T = S * QT
+        self.rows_per_rank = [T] * self.world  # every rank serves 16 equal sequences
         self.q = torch.empty(T, 64, 576, device=device, dtype=torch.bfloat16).normal_(generator=gd)
         self.kv = torch.empty(S * KVL, 1, 576, device=device, dtype=torch.bfloat16).normal_(generator=gd)
         self.sink = torch.empty(64, device=device).normal_(generator=gd)
@@ -554,18 +646,13 @@ class SparseWL(Workload):
     def step(self):
         return self.SA.sparse_attn_prefill(self.q, self.kv, self.kv[..., :512], self.idx, self.cu, self.sink)
 
-    def e2e_setup(self):
-        self.hq, self.hkv, self.hidx = (t.cpu().pin_memory() for t in (self.q, self.kv, self.idx))
-        self.hout = torch.empty(self.q.shape[0], 64, 512, dtype=self.q.dtype).pin_memory()
-        self.dq, self.dkv, self.didx = (torch.empty_like(t) for t in (self.q, self.kv, self.idx))
-        return (sum(t.numel() * t.element_size() for t in (self.hq, self.hkv, self.hidx)),
-                self.hout.numel() * self.hout.element_size())
-
-    def e2e_step(self):
-        for d, h in ((self.dq, self.hq), (self.dkv, self.hkv), (self.didx, self.hidx)):
-            d.copy_(h, non_blocking=True)
-        o = self.SA.sparse_attn_prefill(self.dq, self.dkv, self.dkv[..., :512], self.didx, self.cu, self.sink)
-        self.hout.copy_(o, non_blocking=True)
+    def e2e_pipeline(self):
+        """Host q / latent KV / index rows in, the output back, through the
+        public sparse_attn_prefill()."""
+        def fn(q, kv, idx):
+            return self.SA.sparse_attn_prefill(q, kv, kv[..., :512], idx, self.cu, self.sink)
+        return ([self.q.cpu(), self.kv.cpu(), self.idx.cpu()], fn,
+                [((self.q.shape[0], 64, 512), self.q.dtype)])
 
     def reference_sample(self):
         from oracle import attention_oracle as O
@@ -594,6 +681,7 @@ class CompressWL(Workload):
         self.CSA, self.HCA = CSA, HCA
         gd = torch.Generator(device=device).manual_seed(55 + rank)
         T = 65536
+        self.rows_per_rank = [T // 4] * self.world  # CSA slots per rank (16 equal sequences)
         self.k = torch.empty(T, 1, 512, device=device, dtype=torch.bfloat16).normal_(generator=gd)
         self.v = torch.empty(T, 1, 512, device=device, dtype=torch.bfloat16).normal_(generator=gd)
         self.gate = torch.empty(T, device=device).normal_(generator=gd)
@@ -646,21 +734,14 @@ class CompressWL(Workload):
             self.use_outputs(self.set_i)
         return out
 
-    def e2e_setup(self):
-        self.hk, self.hv, self.hg = (t.cpu().pin_memory() for t in (self.k, self.v, self.gate))
-        # pinned host buffers for all four outputs (CSA K/V, HCA K/V)
-        self.hout = [torch.empty(n, 1, 512, dtype=torch.bfloat16).pin_memory()
-                     for n in (65536 // 4, 65536 // 4, 65536 // 128, 65536 // 128)]
-        self.dk, self.dv, self.dg = (torch.empty_like(t) for t in (self.k, self.v, self.gate))
-        return (sum(t.numel() * t.element_size() for t in (self.hk, self.hv, self.hg)),
-                sum(t.numel() * t.element_size() for t in self.hout))
-
-    def e2e_step(self):
-        for d, h in ((self.dk, self.hk), (self.dv, self.hv), (self.dg, self.hg)):
-            d.copy_(h, non_blocking=True)
-        (ck, cv, _), (hk, hv, _) = self.CSA.compress_kv_csa_hca(self.dk, self.dv, self.cu_h, 4, 128, gate=self.dg)
-        for h, d in zip(self.hout, (ck, cv, hk, hv)):
-            h.copy_(d, non_blocking=True)
+    def e2e_pipeline(self):
+        """Host K / V / gates in, all four outputs (CSA K/V, HCA K/V) back,
+        through the public compress_kv_csa_hca()."""
+        def fn(k, v, g):
+            (ck, cv, _), (hk, hv, _) = self.CSA.compress_kv_csa_hca(k, v, self.cu_h, 4, 128, gate=g)
+            return ck, cv, hk, hv
+        outs = [((n, 1, 512), torch.bfloat16) for n in (65536 // 4, 65536 // 4, 65536 // 128, 65536 // 128)]
+        return [self.k.cpu(), self.v.cpu(), self.gate.cpu()], fn, outs
 
     def reference_sample(self):
         from oracle import attention_oracle as O
@@ -864,7 +945,8 @@ class CsaDecodeWL(Workload):
         for _ in range(self.out_sets):
             ck = torch.empty(self.cap, 1, 512, device=device, dtype=torch.bfloat16)
             sets.append((ck, (T.ptr(self.kc), T.strides(self.kc), None, None, None, None, T.ptr(self.bt),
-                              T.strides(self.bt), T.ptr(self.ctx), self.P, T.ptr(offs), self.ctx.shape[0], self.cap,
+                              T.strides(self.bt), T.ptr(self.ctx), self.P, self.bt.shape[1], self.kc.shape[0],
+                              T.ptr(offs), self.ctx.shape[0], self.cap,
                               T.ptr(ck), T.strides(ck), None, None, 1, 512, 0, self.m, 2 * self.m, T.dtype_code(ck),
                               T.stream_of(ck))))
         ring = itertools.cycle(sets)
@@ -947,6 +1029,7 @@ class MixedWL(Workload):
         mine_d = [b for b in range(n_dec) if owner[n_pre + b] == rank]
         # prefill share
         self.lens = [lens[i] for i in mine_p]
+        self.rows_per_rank = [sum(lens[i] for i in range(n_pre) if owner[i] == r) for r in range(world)]
         T = sum(self.lens)
         cu = [0]
         for L in self.lens:
@@ -1097,9 +1180,18 @@ def run_workload_ours(args, rank, world, device, W):
         step_fn = lambda: next(ring).replay()  # noqa: E731
     with Clocks(device.index) as clk:
         ms = w.timed(step_fn, args.steps, args.warmup, device)
+    pipelined = False
     if args.no_e2e:
         h2d = d2h = 0
         e2e_ms = float("nan")
+    elif hasattr(w, "e2e_pipeline"):
+        hin, fn, outs = w.e2e_pipeline()
+        pe = PipelinedE2E(hin, fn, outs, device)
+        del hin
+        e2e_ms = pe.timed(max(3, args.steps // 4), 2, world)
+        h2d, d2h = pe.h2d_bytes(), pe.d2h_bytes()
+        del pe
+        pipelined = True
     else:
         h2d, d2h = w.e2e_setup()
         if world > 1:
@@ -1107,24 +1199,32 @@ def run_workload_ours(args, rank, world, device, W):
         e2e_ms = w.timed(w.e2e_step, max(2, args.steps // 4), 1, device)
     work_all = float(w.work)
     gather_ms = None
+    per_rank = None
     if world > 1:
-        # outputs to rank 0 over NCCL, after and outside the timed regions
+        # outputs to rank 0 over NCCL, after and outside the timed regions:
+        # one gather of fixed-size blocks whose sizes come from the sharding plan
         import sharding
         out = w.step()
-        sharding.concat_rows(out[:1], dst=0)  # first use of the collectives, untimed
+        if hasattr(w, "rows_per_rank"):
+            gather = sharding.PlannedGather(w.rows_per_rank, dst=0)
+        else:
+            gather = lambda x: sharding.concat_rows(x, dst=0)  # noqa: E731  (sizes exchanged first)
+        gather(out)  # first use of the collective, untimed
         torch.distributed.barrier()
         torch.cuda.synchronize(device)
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record()
-        sharding.concat_rows(out, dst=0)  # ranks' shares may differ in length
+        gather(out)
         g1.record()
         torch.cuda.synchronize(device)
         gather_ms = g0.elapsed_time(g1)
+        del out, gather
         t = torch.tensor([ms, e2e_ms, float(w.work)], dtype=torch.float64, device=device)
-        mx, tot = t.clone(), t.clone()
-        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
-        torch.distributed.all_reduce(tot, op=torch.distributed.ReduceOp.SUM)
-        ms, e2e_ms, work_all = float(mx[0]), float(mx[1]), float(tot[2])
+        allv = torch.empty(world, 3, dtype=torch.float64, device=device)
+        torch.distributed.all_gather_into_tensor(allv, t)
+        allv = allv.cpu()
+        per_rank = [{"rank": r, "ms": round(float(allv[r, 0]), 4), "work": float(allv[r, 2])} for r in range(world)]
+        ms, e2e_ms, work_all = float(allv[:, 0].max()), float(allv[:, 1].max()), float(allv[:, 2].sum())
     if rank != 0:
         return None
     scale = w.scale()
@@ -1144,7 +1244,11 @@ def run_workload_ours(args, rank, world, device, W):
                      "timed": f"{w.kernel} per step (public API, device-resident inputs), CUDA events"
                  + ("; each step a CUDA-graph replay of the call" if graph is not None else "")},
         "e2e": {"value": round(work_all / (e2e_ms * 1e-3) / scale, 2), "unit": w.unit, "ms_per_step": round(e2e_ms, 3),
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "note": ("public API with inputs copied from pinned host memory and outputs copied back every step"
+                         + ("; copies on two copy streams overlapping the neighbouring steps' kernels"
+                            if pipelined else "; copies in series with the kernels")
+                         + ("; per GPU, each rank copying its own share" if world > 1 else ""))},
         "gpu_launches": args.steps * w.launches,
         "clocks": clk.summary(),
     }
@@ -1152,6 +1256,7 @@ def run_workload_ours(args, rank, world, device, W):
         res["e2e"] = None
     if gather_ms is not None:
         res["config"]["output_gather_to_rank0_ms"] = round(gather_ms, 3)
+        res["config"]["per_rank"] = per_rank
     if hasattr(w, "phases"):
         res["config"]["phases"] = w.phases(device)
     if hasattr(w, "kernel_roofline"):
@@ -1169,7 +1274,7 @@ def run_workload_ours(args, rank, world, device, W):
         # figure of the same file is the matching denominator
         res["roofline"]["peak_sustained"] = sus
         res["roofline"]["frac_of_sustained"] = round(per_gpu / sus, 4)
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         from threadpoolctl import threadpool_limits
         threads = os.cpu_count() or 1
         with threadpool_limits(limits=threads):
@@ -1192,6 +1297,10 @@ def main():
     ap.add_argument("--small", action="store_true", help="reduced workload instance (profiling captures)")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch each device-timed step eagerly instead of replaying a CUDA graph of it")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="decode only: skip the prefill / sparse / compression lines added to the default run")
+    ap.add_argument("--workload-cpu-seconds", type=float, default=5.0,
+                    help="CPU-baseline seconds of each added workload")
     args = ap.parse_args()
     global SMALL
     SMALL = args.small
@@ -1218,6 +1327,23 @@ def main():
                                              device_id=device)
     if args.workload == "decode":
         res = run_decode_ours(args, rank, world, device)
+        if not args.no_workloads:
+            # the metric's other figures (prefill / sparse TFLOP/s, compression
+            # GB/s), each measured like the headline: same steps and warm-up,
+            # own roofline, clocks, end-to-end leg and CPU baseline
+            sub_args = argparse.Namespace(**vars(args))
+            sub_args.cpu_seconds = args.workload_cpu_seconds
+            wl = {}
+            for name in ("prefill", "sparse", "compress"):
+                torch.cuda.empty_cache()
+                r = run_workload_ours(sub_args, rank, world, device, WORKLOADS[name])
+                if rank == 0:
+                    for k in ("metric", "n_gpus", "steps", "warmup", "higher_is_better", "scaling", "vs_baseline",
+                              "data"):
+                        r.pop(k, None)
+                    wl[name] = r
+            if rank == 0:
+                res["workloads"] = wl
     else:
         res = run_workload_ours(args, rank, world, device, WORKLOADS[args.workload])
     if rank == 0:

@@ -53,6 +53,15 @@ int tak_read_device_error(void* stream);
  * Process-wide; returns the previous value. */
 int tak_set_kernel_path(int path);
 
+/* Name of the main kernel that the calling thread's last attention or
+ * pooling call launched: "prefill_tc", "prefill_generic", "sparse_tc",
+ * "sparse_generic", "paged_decode_tc", "paged_decode_generic",
+ * "compress_bulk", "compress_dual", "compress_csa_hca", "compress_stream",
+ * "compress_split" or "compress_rows"; "" when the call launched nothing (an
+ * empty problem, an error).  Lets a caller see whether a shape took the
+ * tensor-core kernels or fell back to the CUDA-core ones. */
+const char* tak_last_kernel(void);
+
 /*
  * Varlen flash prefill.  Replaces flash_attention_prefill(q, k, v, cu_seqlens,
  * causal) of attention/flash_attention_prefill.py:108-171 (Triton launch at
@@ -77,7 +86,9 @@ int tak_flash_attention_prefill(const void* q, const int64_t* q_strides, const v
  * bytes for the split-KV partials (may be NULL if that size is 0); no
  * initialisation needed.  Calls that share a workspace must not overlap on the
  * GPU (issue them on one stream).  Context rows past the block table
- * (ctx > max_blocks * block_size) are ignored.
+ * (ctx > max_blocks * block_size) are ignored; a block-table entry outside
+ * [0, num_blocks) is never read: its rows count as zero keys and values
+ * (score 0, value 0).
  * split_pages: pages per split-KV work unit, 0 = automatic.
  */
 size_t tak_paged_attention_decode_workspace_size(int64_t num_seqs, int64_t num_q_heads, int64_t num_kv_heads,
@@ -100,10 +111,13 @@ int tak_paged_attention_decode(const void* q, const int64_t* q_strides, const vo
  * the workspace: the split-KV scratch is a 32 MiB array inside the library
  * (held by every GPU that loads the library until exit).  Sizes whose scratch
  * would exceed 32 MiB are rejected with status 2 (a larger split_pages lowers
- * the need).  All calls on a GPU share the array: calls that overlap on the
- * GPU race; nothing in it needs clearing between calls.  The first call with
- * a given GPU current looks up the array's device address; make it before any
- * stream capture.
+ * the need; fp32 caches, unaligned strides and single-split sizes run
+ * kernels that need no scratch and are never rejected for size).  Arguments
+ * are validated as for tak_paged_attention_decode.  All calls on a GPU share
+ * the array: calls that overlap on the GPU race; nothing in it needs clearing
+ * between calls.  The first call with a given GPU current, and the first after
+ * that GPU's context was recreated (cudaDeviceReset), looks up the array's
+ * device address; make those calls before any stream capture.
  */
 int tak_paged_attention_decode_static_scratch(const void* q, const int64_t* q_strides, const void* k_cache,
                                               const int64_t* k_strides, const void* v_cache,
@@ -139,11 +153,11 @@ int tak_sparse_attn_prefill(const void* q, const int64_t* q_strides, const void*
  * attention/sparse_attn_fwd.py:317-382 (Triton launch at :359), with its
  * slot-position rule (:151-210): slots < num_win address the paged cache and
  * need 0 <= idx < ctx; later slots address compressed rows idx - ctx.
- * Precondition, as in the reference kernel (its block-table and cache loads
- * at :159-170 are bounded by the same two tests only): every valid window
- * slot lies inside its block-table row (idx < block-table width * block_size)
- * and that row's entry is a page of the cache.  Neither is checked here;
- * unlike tak_paged_attention_decode, which ignores rows past the table.
+ * block_tables is [num_seqs, max_blocks] and the caches have num_blocks pages.
+ * A window slot is masked unless it also lies inside its block-table row
+ * (idx < max_blocks * block_size) and that row's entry is a page of the cache
+ * (0 <= page < num_blocks); the reference's kernel reads past both unchecked
+ * (:159-170).
  */
 int tak_sparse_attn_decode(const void* q, const int64_t* q_strides, const void* k_cache, const int64_t* k_strides,
                            const void* v_cache, const int64_t* v_strides, const void* compressed_k,
@@ -153,7 +167,7 @@ int tak_sparse_attn_decode(const void* q, const int64_t* q_strides, const void* 
                            void* out, const int64_t* out_strides, float* lse, int64_t num_seqs,
                            int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t head_dim_v,
                            int64_t num_compressed, int64_t k_topk, int64_t num_win, int64_t block_size,
-                           float scale, int dtype, void* stream);
+                           int64_t max_blocks, int64_t num_blocks, float scale, int dtype, void* stream);
 
 /* token -> sequence map (0 for tokens outside every sequence).  Replaces
  * build_token_to_seq of attention/sparse_attn_fwd.py:253-260. */
@@ -182,20 +196,21 @@ int tak_compress_kv(const void* k, const int64_t* k_strides, const void* v, cons
 
 /*
  * Same pooling, reading each sequence's first context_lens[s] rows straight
- * from a paged cache [num_blocks,H_kv,P,D].  Replaces the page gather +
- * compress of csa_decode_forward (attention/csa.py:225-256) and
- * hca_decode_forward (attention/hca.py:204-232).  gate (optional) is
- * float32 [num_blocks, P] with strides gate_strides[2].  v_cache = NULL
- * pools K alone, as for tak_compress_kv.  Precondition: each sequence's
- * block-table row covers its context (context_lens[s] <= table width * P)
- * with valid page ids; the reference's gather raises an IndexError past the
- * row (attention/csa.py:229-245); this entry point does not check it.
+ * from a paged cache [num_blocks,H_kv,P,D] through block_tables
+ * [num_seqs, max_blocks].  Replaces the page gather + compress of
+ * csa_decode_forward (attention/csa.py:225-256) and hca_decode_forward
+ * (attention/hca.py:204-232).  gate (optional) is float32 [num_blocks, P]
+ * with strides gate_strides[2].  v_cache = NULL pools K alone, as for
+ * tak_compress_kv.  A context row past its block-table row (row >=
+ * max_blocks * P), or on a page id outside [0, num_blocks), is never read: it
+ * pools as a zero row with gate logit 0 (the reference's gather raises an
+ * IndexError past the row, attention/csa.py:229-245, and reads any page id).
  */
 int tak_compress_kv_paged(const void* k_cache, const int64_t* k_strides, const void* v_cache,
                           const int64_t* v_strides, const float* gate, const int64_t* gate_strides,
                           const int32_t* block_tables, const int64_t* bt_strides, const int32_t* context_lens,
-                          int64_t block_size, const int32_t* comp_offsets, int64_t num_seqs,
-                          int64_t num_compressed, void* compressed_k, const int64_t* ck_strides,
+                          int64_t block_size, int64_t max_blocks, int64_t num_blocks, const int32_t* comp_offsets,
+                          int64_t num_seqs, int64_t num_compressed, void* compressed_k, const int64_t* ck_strides,
                           void* compressed_v, const int64_t* cv_strides, int64_t num_kv_heads, int64_t head_dim,
                           int64_t head_dim_v, int64_t stride, int64_t window, int dtype, void* stream);
 

@@ -112,6 +112,44 @@ def prefill(q, k, v, cu_seqlens, causal=True, acc=np.float64):
     return out, lse
 
 
+def prefill_rows(q, k, v, cu_seqlens, rows, causal=True, acc=np.float64):
+    """The rows ``rows`` (global token indices) of :func:`prefill`, computed
+    without the full [L, L] score matrix -- the same math (FP:177-229: scores
+    ``scale * q k^T``, causal ``triu`` mask FP:218, softmax, ``@ v``), so that
+    sequences of tens of thousands of tokens can be checked row by row.
+
+    Returns (out [len(rows), H, Dv], lse [len(rows), H]); a row outside every
+    sequence gives out = 0, lse = -inf (FP:189).
+    """
+    rows = np.asarray(rows, dtype=np.int64)
+    T, H, D = q.shape
+    Hkv, Dv = k.shape[1], v.shape[2]
+    G = H // Hkv
+    scale = 1.0 / math.sqrt(D)
+    bounds = _bounds(cu_seqlens)
+    out = np.zeros((rows.shape[0], H, Dv), acc)
+    lse = np.full((rows.shape[0], H), NEG_INF, acc)
+    for start, end in bounds:
+        sel = np.nonzero((rows >= start) & (rows < end))[0]
+        if sel.size == 0:
+            continue
+        pos = rows[sel] - start                                           # position in the sequence
+        kl = end if not causal else start + int(pos.max()) + 1            # keys any selected row sees
+        qs = _np(q[rows[sel]], acc)                                       # [n, H, D]
+        ks = _np(k[start:kl], acc)                                        # [Lk, Hkv, D]
+        vs = _np(v[start:kl], acc)
+        for g in range(Hkv):
+            qg = qs[:, g * G:(g + 1) * G, :].transpose(1, 0, 2)           # [G, n, D]
+            s = (qg @ ks[:, g, :].T) * scale                              # [G, n, Lk]
+            if causal:
+                s = np.where(np.arange(kl - start)[None, None, :] > pos[None, :, None], NEG_INF, s)
+            p, l, m = _softmax_rows(s)
+            o, ls = _finish(p, l, m, vs[:, g, :])
+            out[sel, g * G:(g + 1) * G, :] = o.transpose(1, 0, 2)
+            lse[sel, g * G:(g + 1) * G] = ls.T
+    return out, lse
+
+
 # ---------------------------------------------------------------------------
 # Paged decode  (PD:157-202; kernel PD:11-98)
 # ---------------------------------------------------------------------------

@@ -1,8 +1,9 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Run in a container that has the reference checkout (it is read-only there):
+Run where a checkout of the reference is available, passing its attention/
+folder (the script only reads it):
 
-    python tests/golden/make_golden.py /root/reference/attention
+    python tests/golden/make_golden.py <reference checkout>/attention
 
 For each test runner of the reference (``run_*test`` in attention/*.py) this
 script rebuilds that runner's inputs on the CPU -- same seed, same sequence of
@@ -281,6 +282,8 @@ def _attention_edges(store, g):
 
 
 if __name__ == "__main__":
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference/attention"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout>/attention")
+    ref = sys.argv[1]
     main(ref)
     main_edges(ref)

@@ -168,6 +168,11 @@ def _header_params():
     return out
 
 
+# a host stride array for arguments whose values are copied before the checked one
+# (the pointers given with it are never dereferenced: validation fails first)
+_S4 = (ctypes.c_int64 * 4)(0, 0, 0, 0)
+
+
 def _call_invalid(name, **vals):
     """Call entry point `name` with null pointers, zero sizes and `vals`."""
     params = _header_params()[name]
@@ -195,11 +200,25 @@ def _call_invalid(name, **vals):
                                      head_dim_v=0), "head dims"),
     ("tak_sparse_attn_decode", dict(dtype=1, num_seqs=2, num_q_heads=64, num_kv_heads=1, head_dim=512,
                                     head_dim_v=512, k_topk=-1), "negative"),
+    ("tak_sparse_attn_decode", dict(dtype=1, num_seqs=2, num_q_heads=64, num_kv_heads=1, head_dim=512,
+                                    head_dim_v=512, k_topk=4, topk_idxs=8, topk_strides=_S4, q=8, q_strides=_S4,
+                                    out=8, out_strides=_S4, k_cache=8, k_strides=_S4, v_cache=8, v_strides=_S4,
+                                    block_tables=8, bt_strides=_S4, context_lens=8, block_size=16, max_blocks=-1),
+     "max_blocks"),
     ("tak_compress_kv", dict(dtype=1, stride=0, window=8, num_kv_heads=1, head_dim=512, num_compressed=4),
      "stride"),
     # no V given but a V head dim: the K-only form needs head_dim_v = 0
     ("tak_compress_kv_paged", dict(dtype=1, stride=4, window=8, num_kv_heads=1, head_dim=512, head_dim_v=512,
                                    num_compressed=4), "head sizes"),
+    ("tak_compress_kv_paged", dict(dtype=1, stride=4, window=8, num_kv_heads=1, head_dim=512, num_compressed=4,
+                                   k_cache=8, k_strides=_S4, comp_offsets=8, compressed_k=8, ck_strides=_S4,
+                                   block_tables=8, bt_strides=_S4, context_lens=8, block_size=16, num_blocks=-1),
+     "num_blocks"),
+    ("tak_paged_attention_decode_static_scratch", dict(dtype=7, num_q_heads=32, num_kv_heads=8, head_dim=128),
+     "unknown dtype"),
+    ("tak_paged_attention_decode_static_scratch", dict(dtype=1, num_q_heads=32, num_kv_heads=8, head_dim=-4,
+                                                       num_seqs=4096, max_blocks=64, block_size=128,
+                                                       cache_rows=128), "head_dim"),
     ("tak_compress_kv_csa_hca", dict(dtype=1, m=0, m_prime=128, num_csa=4, num_kv_heads=1, head_dim=512,
                                      head_dim_v=512), "null v"),
     ("tak_build_window_idxs", dict(num_seqs=1, total_tokens=4, n_win=8, ld=4), "bad arguments"),

@@ -107,6 +107,25 @@ def test_prefill_lse_is_log_of_row_sums():
         assert abs(lse[i, 0] - math.log(sum(math.exp(x) for x in s))) < 1e-12
 
 
+@pytest.mark.parametrize("causal", [True, False])
+def test_prefill_rows_equals_full_prefill(causal):
+    """The row-sampled prefill (used to check sequences too long for the full
+    score matrix) gives exactly the full oracle's rows, including rows of
+    empty sequences' neighbours and rows outside every sequence."""
+    rng = np.random.default_rng(12)
+    lens = [5, 0, 300, 1, 77]
+    T = sum(lens) + 2
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    q = rng.standard_normal((T, 8, 32)).astype(np.float32)
+    k = rng.standard_normal((T, 2, 32)).astype(np.float32)
+    v = rng.standard_normal((T, 2, 24)).astype(np.float32)
+    out, lse = O.prefill(q, k, v, cu, causal)
+    rows = np.array([0, 4, 5, 6, 100, 255, 256, 257, 304, 305, 306, 350, T - 2, T - 1])
+    ro, rl = O.prefill_rows(q, k, v, cu, rows, causal)
+    _close(ro, out[rows])
+    _close(rl, lse[rows])
+
+
 # ---------------------------------------------------------------------------
 # paged decode (attention/paged_attention_decode.py:11-98)
 # ---------------------------------------------------------------------------

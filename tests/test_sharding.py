@@ -148,6 +148,36 @@ def test_three_rank_concat_uneven_blocks(tmp_path):
     assert torch.equal(res["a"], want) and torch.equal(res["b"], want)
 
 
+def _planned_worker(rank, world, port, q_path):
+    _init(rank, world, port)
+    try:
+        # the decode sharding plan, computed identically on every rank
+        ctx = [1, 8192, 77, 4096, 0, 3000, 129, 64, 5000, 2]
+        ids = [S.shard_requests(ctx, world, r) for r in range(world)]
+        gather = S.PlannedGather([len(i) for i in ids], ids)
+        local = ids[rank].to(torch.float32)[:, None] * torch.ones(1, 3) + 0.5
+        a = gather(local)
+        b = gather(local * 2)        # buffers reused
+        c = S.PlannedGather([2, 0, 3][:world])(torch.full(([2, 0, 3][rank], 2), float(rank)))  # rank order
+        d = S.PlannedGather([len(i) for i in ids], ids, dst=0)(local)  # to rank 0 only
+        assert (d is None) == (rank != 0)
+        if rank == 0:
+            torch.save({"a": a, "b": b, "c": c, "d": d}, q_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_three_rank_planned_gather(tmp_path):
+    """One collective, sizes from the sharding plan: rows land in global
+    request order; without row numbers, blocks are concatenated by rank."""
+    res = _run(_planned_worker, 3, tmp_path)
+    want = torch.arange(10, dtype=torch.float32)[:, None] * torch.ones(1, 3) + 0.5
+    assert torch.equal(res["a"], want)
+    assert torch.equal(res["b"], want * 2)
+    assert torch.equal(res["d"], want)
+    assert torch.equal(res["c"], torch.tensor([[0.0, 0.0], [0.0, 0.0], [2.0, 2.0], [2.0, 2.0], [2.0, 2.0]]))
+
+
 def _run(worker, world, tmp_path):
     path = str(tmp_path / "result.pt")
     mp.spawn(worker, args=(world, _free_port(), path), nprocs=world, join=True)

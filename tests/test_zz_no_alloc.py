@@ -69,8 +69,9 @@ def test_static_scratch_matches_workspace_entry_point():
     out2 = torch.empty_like(q2)
     lse2 = torch.empty(q2.shape[:2], dtype=torch.float32, device=DEV)
     assert _static_call(q2, kc2, vc2, bt2, cl2, P2, out2, lse2) == 0
-    ref2 = PD.paged_attention_decode(q2, kc2, vc2, bt2, cl2, P2, P2)
+    ref2, ref_lse2 = PD.paged_attention_decode(q2, kc2, vc2, bt2, cl2, P2, P2, return_lse=True)
     assert (out2.float() - ref2.float()).abs().max().item() <= TOL16
+    assert (lse2 - ref_lse2).abs().max().item() <= TOL_LSE
     assert T.read_device_error() == 0
 
 
@@ -90,3 +91,21 @@ def test_static_scratch_rejects_oversized_problem():
     assert rc == 2
     msg = T.lib().tak_last_error().decode()
     assert "static scratch" in msg and "33554432" in msg
+
+
+def test_static_scratch_larger_split_pages_fits():
+    """The remedy the rejection names: 256 requests with 64-page tables need
+    272 MB of partials at one page per split (rejected) but 17 MB at 16 pages
+    per split (4 splits), which runs and matches the workspace entry point."""
+    q, kc, vc, bt, cl, P = _inputs(7, B=256, H=32, Hkv=8, P=16, max_ctx=1024)
+    out = torch.empty_like(q)
+    lse = torch.empty(q.shape[:2], dtype=torch.float32, device=DEV)
+    assert _static_call(q, kc, vc, bt, cl, P, out, lse, split_pages=1) == 2
+    need = T.lib().tak_paged_attention_decode_workspace_size(256, 32, 8, 128, P, bt.shape[1], 16)
+    assert 0 < need <= 32 << 20
+    assert _static_call(q, kc, vc, bt, cl, P, out, lse, split_pages=16) == 0, T.lib().tak_last_error().decode()
+    ref, ref_lse = PD.paged_attention_decode(q, kc, vc, bt, cl, P, P, return_lse=True, split_pages=16)
+    torch.cuda.synchronize()
+    assert (out.float() - ref.float()).abs().max().item() <= TOL16
+    assert (lse - ref_lse).abs().max().item() <= TOL_LSE
+    assert T.read_device_error() == 0

@@ -27,6 +27,7 @@ _SIGS = {
     "tak_last_error": ([], ctypes.c_char_p),
     "tak_read_device_error": ([_P], _I32),
     "tak_set_kernel_path": ([_I32], _I32),
+    "tak_last_kernel": ([], ctypes.c_char_p),
     "tak_flash_attention_prefill": ([_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _F32,
                                      _I32, _I32, _P], _I32),
     "tak_paged_attention_decode_workspace_size": ([_I64, _I64, _I64, _I64, _I64, _I64, _I32], _SZ),
@@ -37,12 +38,12 @@ _SIGS = {
     "tak_sparse_attn_prefill": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                  _I64, _I64, _F32, _I32, _P], _I32),
     "tak_sparse_attn_decode": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64,
-                                _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F32, _I32, _P], _I32),
+                                _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F32, _I32, _P], _I32),
     "tak_build_token_to_seq": ([_P, _I64, _I64, _P, _P], _I32),
     "tak_compress_kv": ([_P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
                          _I64, _I32, _P], _I32),
-    "tak_compress_kv_paged": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _P, _P, _P, _P, _I64,
-                               _I64, _I64, _I64, _I64, _I32, _P], _I32),
+    "tak_compress_kv_paged": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P,
+                               _P, _I64, _I64, _I64, _I64, _I64, _I32, _P], _I32),
     "tak_compress_kv_csa_hca": ([_P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _P,
                                  _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I32, _P], _I32),
     "tak_build_window_idxs": ([_P, _I64, _I64, _I64, _P, _I64, _P], _I32),
@@ -132,6 +133,13 @@ def workspace(device, stream_handle, nbytes):
 def set_kernel_path(path):
     """0 = tensor-core kernels where the shape allows (default), 1 = generic CUDA-core kernels."""
     return lib().tak_set_kernel_path(int(path))
+
+
+def last_kernel():
+    """Name of the main kernel the calling thread's last attention or pooling
+    call launched ("" when it launched none), e.g. "prefill_tc" or
+    "sparse_generic"."""
+    return lib().tak_last_kernel().decode()
 
 
 def read_device_error(device=None):
@@ -271,7 +279,8 @@ def compress_paged(k_cache, v_cache, block_tables, context_lens, block_size, str
         vv, cvv = (None, None) if k_only else (v_cache, cv)
         check(lib().tak_compress_kv_paged(
             ptr(k_cache), strides(k_cache), ptr(vv), None if vv is None else strides(vv), None, None, ptr(bt),
-            strides(bt), ptr(cl), block_size, ptr(offs_t), cl.shape[0], nc, ptr(ck), strides(ck), ptr(cvv),
+            strides(bt), ptr(cl), block_size, bt.shape[1], k_cache.shape[0], ptr(offs_t), cl.shape[0], nc, ptr(ck),
+            strides(ck), ptr(cvv),
             None if cvv is None else strides(cvv), hkv, k_cache.shape[3], 0 if k_only else v_cache.shape[3],
             stride, window, dtype_code(k_cache), stream_of(k_cache)))
     return ck, cv, offs_t, lens, offs

@@ -146,3 +146,69 @@ def concat_rows(local, group=None, dst=None):
     dist.all_gather(counts, n, group=group)
     counts = [int(c) for c in counts]
     return gather_rows(local, sum(counts[:me]), sum(counts), group=group, dst=dst)
+
+
+class PlannedGather:
+    """All-gather of row blocks whose sizes every rank already knows from the
+    sharding plan (``lpt_assign`` runs identically on every rank), in ONE
+    collective with no count exchange and no host synchronisation.
+
+    Rank r contributes ``counts[r]`` rows, padded to ``max(counts)``; the
+    padded blocks are all-gathered into one tensor (``all_gather_into_tensor``)
+    and, when ``row_index`` is given (``row_index[r]``: global row of each of
+    rank r's rows), placed in global row order by one ``index_select`` with a
+    precomputed index.  Without ``row_index`` the blocks are concatenated in
+    rank order.  With ``dst=k`` the blocks go to rank k only (``gather``, for
+    results too large to replicate) and the other ranks get None.  Buffers are
+    allocated on first use and reused across calls."""
+
+    def __init__(self, counts, row_index=None, group=None, dst=None):
+        self.counts = [int(c) for c in counts]
+        self.group = group
+        self.dst = dst
+        self.mx = max(self.counts) if self.counts else 0
+        src = []  # position in the padded gather buffer of each global row
+        if row_index is None:
+            for r, c in enumerate(self.counts):
+                src += [r * self.mx + i for i in range(c)]
+        else:
+            total = sum(self.counts)
+            pos = [0] * total
+            for r, rows in enumerate(row_index):
+                rows = _host_list(rows)
+                assert len(rows) == self.counts[r]
+                for i, g in enumerate(rows):
+                    pos[g] = r * self.mx + i
+            src = pos
+        self._src = torch.tensor(src, dtype=torch.int64)
+        self._bufs = {}
+
+    def _buffers(self, local):
+        key = (local.device, local.dtype, tuple(local.shape[1:]))
+        b = self._bufs.get(key)
+        if b is None:
+            world = len(self.counts)
+            send = local.new_zeros((self.mx,) + tuple(local.shape[1:]))
+            receive = self.dst is None or dist.get_rank(self.group) == self.dst
+            recv = local.new_empty(((world if receive else 1) * self.mx,) + tuple(local.shape[1:]))
+            b = (send, recv, self._src.to(local.device))
+            self._bufs[key] = b
+        return b
+
+    def __call__(self, local):
+        """The [sum(counts), ...] result (on every rank, or on rank dst only)."""
+        send, recv, src = self._buffers(local)
+        n = local.shape[0]
+        if n == self.mx:
+            send = local.contiguous()
+        else:
+            send[:n].copy_(local)
+        if self.dst is None:
+            dist.all_gather_into_tensor(recv, send, group=self.group)
+        else:
+            me = dist.get_rank(self.group)
+            parts = list(recv.chunk(len(self.counts))) if me == self.dst else None
+            dist.gather(send, parts, dst=self.dst, group=self.group)
+            if me != self.dst:
+                return None
+        return recv.index_select(0, src)

@@ -115,6 +115,6 @@ def sparse_attn_decode(q, k_cache, v_cache, compressed_k, compressed_v,
         _t.ptr(q), _t.strides(q), _t.ptr(k_cache), _t.strides(k_cache), _t.ptr(v_cache), _t.strides(v_cache),
         _t.ptr(ck), _t.strides(ck), _t.ptr(cv), _t.strides(cv), _t.ptr(bt), _t.strides(bt), _t.ptr(idx),
         _t.strides(idx), _t.ptr(cl), _t.ptr(sink), _t.ptr(out), _t.strides(out), _t.ptr(lse), num_seqs,
-        num_q_heads, num_kv_heads, head_dim, head_dim_v, ck.shape[0], idx.shape[1], num_win, block_size, scale,
-        _t.dtype_code(q), _t.stream_of(q)))
+        num_q_heads, num_kv_heads, head_dim, head_dim_v, ck.shape[0], idx.shape[1], num_win, block_size,
+        bt.shape[1], k_cache.shape[0], scale, _t.dtype_code(q), _t.stream_of(q)))
     return (out, lse) if return_lse else out

@@ -15,6 +15,7 @@ namespace tak {
 __device__ int g_tak_device_error = 0;
 
 static thread_local char t_err[512] = "";
+static thread_local const char* t_kernel = "";
 static int g_kernel_path = 0;
 
 int set_error(int code, const char* msg) {
@@ -22,7 +23,9 @@ int set_error(int code, const char* msg) {
   return code;
 }
 
-static int check_launch(const char* what) {
+void note_kernel(const char* name) { t_kernel = name; }
+
+int check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     char buf[400];
@@ -117,6 +120,10 @@ using namespace tak;
     if (!(cond)) return set_error(1, msg); \
   } while (0)
 
+// every entry point that launches attention or pooling kernels starts with no
+// kernel recorded for tak_last_kernel()
+#define TAK_ENTRY() (t_kernel = "")
+
 static void copy_strides(int64_t* dst, const int64_t* src, int n) {
   for (int i = 0; i < n; ++i) dst[i] = src ? src[i] : 0;
 }
@@ -126,6 +133,8 @@ extern "C" {
 const char* tak_version(void) { return "tak-b200 0.1"; }
 
 const char* tak_last_error(void) { return t_err; }
+
+const char* tak_last_kernel(void) { return t_kernel; }
 
 int tak_set_kernel_path(int path) {
   const int old = g_kernel_path;
@@ -147,6 +156,7 @@ int tak_flash_attention_prefill(const void* q, const int64_t* q_strides, const v
                                 int64_t num_seqs, void* out, const int64_t* out_strides, float* lse,
                                 int64_t total_tokens, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
                                 float scale, int causal, int dtype, void* stream) {
+  TAK_ENTRY();
   TAK_REQUIRE(dtype >= 0 && dtype <= 2, "prefill: unknown dtype");
   TAK_REQUIRE(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
               "prefill: num_q_heads must be a multiple of num_kv_heads");
@@ -190,23 +200,31 @@ size_t tak_paged_attention_decode_workspace_size(int64_t num_seqs, int64_t num_q
   return paged_decode_workspace_bytes(a);
 }
 
-int tak_paged_attention_decode(const void* q, const int64_t* q_strides, const void* k_cache,
-                               const int64_t* k_strides, const void* v_cache, const int64_t* v_strides,
-                               const int32_t* block_tables, const int64_t* bt_strides, const int32_t* context_lens,
-                               void* out, const int64_t* out_strides, float* lse, int64_t num_seqs,
-                               int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
-                               int64_t max_blocks, int64_t num_blocks, int64_t cache_rows, float scale, int dtype,
-                               void* workspace, size_t workspace_bytes, int split_pages, void* stream) {
+}  // extern "C"
+
+namespace tak {
+
+int make_paged_decode_args(PagedDecodeArgs* out_args, const void* q, const int64_t* q_strides, const void* k_cache,
+                           const int64_t* k_strides, const void* v_cache, const int64_t* v_strides,
+                           const int32_t* block_tables, const int64_t* bt_strides, const int32_t* context_lens,
+                           void* out, const int64_t* out_strides, float* lse, int64_t num_seqs,
+                           int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
+                           int64_t max_blocks, int64_t num_blocks, int64_t cache_rows, float scale, int dtype,
+                           int split_pages) {
   TAK_REQUIRE(dtype >= 0 && dtype <= 2, "paged decode: unknown dtype");
   TAK_REQUIRE(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
               "paged decode: num_q_heads must be a multiple of num_kv_heads");
   TAK_REQUIRE(head_dim > 0 && head_dim <= 640, "paged decode: head_dim must be in [1, 640]");
   TAK_REQUIRE(block_size > 0 && block_size <= cache_rows, "paged decode: block_size must be in [1, cache_rows]");
   TAK_REQUIRE(num_seqs >= 0 && max_blocks >= 0 && num_blocks >= 0, "paged decode: negative sizes");
-  if (num_seqs == 0) return 0;
+  PagedDecodeArgs a{};
+  a.num_seqs = static_cast<int>(num_seqs);
+  if (num_seqs == 0) {
+    *out_args = a;
+    return 0;
+  }
   TAK_REQUIRE(q && k_cache && v_cache && block_tables && context_lens && out, "paged decode: null pointer");
   TAK_REQUIRE(q_strides && k_strides && v_strides && bt_strides && out_strides, "paged decode: null strides");
-  PagedDecodeArgs a{};
   a.q = q; copy_strides(a.sq, q_strides, 3);
   a.k_cache = k_cache; copy_strides(a.sk, k_strides, 4);
   a.v_cache = v_cache; copy_strides(a.sv, v_strides, 4);
@@ -214,7 +232,6 @@ int tak_paged_attention_decode(const void* q, const int64_t* q_strides, const vo
   a.context_lens = context_lens;
   a.out = out; copy_strides(a.so, out_strides, 3);
   a.lse = lse;
-  a.num_seqs = static_cast<int>(num_seqs);
   a.num_q_heads = static_cast<int>(num_q_heads);
   a.num_kv_heads = static_cast<int>(num_kv_heads);
   a.head_dim = static_cast<int>(head_dim);
@@ -224,11 +241,32 @@ int tak_paged_attention_decode(const void* q, const int64_t* q_strides, const vo
   a.cache_rows = cache_rows;
   a.scale = scale;
   a.dtype = dtype;
-  a.workspace = workspace;
-  a.workspace_bytes = workspace_bytes;
   a.split_pages = split_pages;
   a.force_generic = g_kernel_path == 1;
-  const int r = paged_decode_launch(a, static_cast<cudaStream_t>(stream));
+  *out_args = a;
+  return 0;
+}
+
+}  // namespace tak
+
+extern "C" {
+
+int tak_paged_attention_decode(const void* q, const int64_t* q_strides, const void* k_cache,
+                               const int64_t* k_strides, const void* v_cache, const int64_t* v_strides,
+                               const int32_t* block_tables, const int64_t* bt_strides, const int32_t* context_lens,
+                               void* out, const int64_t* out_strides, float* lse, int64_t num_seqs,
+                               int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
+                               int64_t max_blocks, int64_t num_blocks, int64_t cache_rows, float scale, int dtype,
+                               void* workspace, size_t workspace_bytes, int split_pages, void* stream) {
+  TAK_ENTRY();
+  PagedDecodeArgs a{};
+  int r = make_paged_decode_args(&a, q, q_strides, k_cache, k_strides, v_cache, v_strides, block_tables, bt_strides,
+                                 context_lens, out, out_strides, lse, num_seqs, num_q_heads, num_kv_heads, head_dim,
+                                 block_size, max_blocks, num_blocks, cache_rows, scale, dtype, split_pages);
+  if (r || num_seqs == 0) return r;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  r = paged_decode_launch(a, static_cast<cudaStream_t>(stream));
   return r ? r : check_launch("paged decode");
 }
 
@@ -268,6 +306,7 @@ int tak_sparse_attn_prefill(const void* q, const int64_t* q_strides, const void*
                             const int64_t* out_strides, float* lse, int64_t total_tokens, int64_t num_q_heads,
                             int64_t num_kv_heads, int64_t head_dim, int64_t head_dim_v, int64_t kv_rows,
                             int64_t k_topk, float scale, int dtype, void* stream) {
+  TAK_ENTRY();
   if (total_tokens == 0) return 0;
   SparseArgs a{};
   int r = fill_sparse_common(a, q, q_strides, topk_idxs, topk_strides, attn_sink, out, out_strides, lse,
@@ -290,7 +329,8 @@ int tak_sparse_attn_decode(const void* q, const int64_t* q_strides, const void* 
                            void* out, const int64_t* out_strides, float* lse, int64_t num_seqs,
                            int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t head_dim_v,
                            int64_t num_compressed, int64_t k_topk, int64_t num_win, int64_t block_size,
-                           float scale, int dtype, void* stream) {
+                           int64_t max_blocks, int64_t num_blocks, float scale, int dtype, void* stream) {
+  TAK_ENTRY();
   if (num_seqs == 0) return 0;
   SparseArgs a{};
   int r = fill_sparse_common(a, q, q_strides, topk_idxs, topk_strides, attn_sink, out, out_strides, lse, num_seqs,
@@ -301,6 +341,8 @@ int tak_sparse_attn_decode(const void* q, const int64_t* q_strides, const void* 
   TAK_REQUIRE(num_compressed == 0 || (compressed_k && compressed_v && ck_strides && cv_strides),
               "sparse decode: null compressed k/v");
   TAK_REQUIRE(block_size > 0 && num_win >= 0, "sparse decode: bad block_size / num_win");
+  TAK_REQUIRE(max_blocks >= 0 && max_blocks <= 2147483647 && num_blocks >= 0,
+              "sparse decode: bad max_blocks / num_blocks");
   a.k = k_cache; copy_strides(a.sk, k_strides, 4);
   a.v = v_cache; copy_strides(a.sv, v_strides, 4);
   a.ck = compressed_k; copy_strides(a.sck, ck_strides, 3);
@@ -310,6 +352,8 @@ int tak_sparse_attn_decode(const void* q, const int64_t* q_strides, const void* 
   a.num_compressed = num_compressed;
   a.num_win = static_cast<int>(num_win);
   a.block_size = static_cast<int>(block_size);
+  a.max_blocks = static_cast<int>(max_blocks);
+  a.num_blocks = num_blocks;
   a.decode = 1;
   r = sparse_launch(a, static_cast<cudaStream_t>(stream));
   return r ? r : check_launch("sparse decode");
@@ -360,6 +404,7 @@ int tak_compress_kv(const void* k, const int64_t* k_strides, const void* v, cons
                     int64_t num_seqs, int64_t num_compressed, void* compressed_k, const int64_t* ck_strides,
                     void* compressed_v, const int64_t* cv_strides, int64_t num_kv_heads, int64_t head_dim,
                     int64_t head_dim_v, int64_t stride, int64_t window, int dtype, void* stream) {
+  TAK_ENTRY();
   if (num_compressed == 0) return 0;
   CompressArgs a{};
   int r = compress_common(a, k, k_strides, 3, v, v_strides, comp_offsets, num_seqs, num_compressed, compressed_k,
@@ -377,10 +422,11 @@ int tak_compress_kv(const void* k, const int64_t* k_strides, const void* v, cons
 int tak_compress_kv_paged(const void* k_cache, const int64_t* k_strides, const void* v_cache,
                           const int64_t* v_strides, const float* gate, const int64_t* gate_strides,
                           const int32_t* block_tables, const int64_t* bt_strides, const int32_t* context_lens,
-                          int64_t block_size, const int32_t* comp_offsets, int64_t num_seqs,
-                          int64_t num_compressed, void* compressed_k, const int64_t* ck_strides,
+                          int64_t block_size, int64_t max_blocks, int64_t num_blocks, const int32_t* comp_offsets,
+                          int64_t num_seqs, int64_t num_compressed, void* compressed_k, const int64_t* ck_strides,
                           void* compressed_v, const int64_t* cv_strides, int64_t num_kv_heads, int64_t head_dim,
                           int64_t head_dim_v, int64_t stride, int64_t window, int dtype, void* stream) {
+  TAK_ENTRY();
   if (num_compressed == 0) return 0;
   CompressArgs a{};
   int r = compress_common(a, k_cache, k_strides, 4, v_cache, v_strides, comp_offsets, num_seqs, num_compressed,
@@ -388,11 +434,15 @@ int tak_compress_kv_paged(const void* k_cache, const int64_t* k_strides, const v
                           stride, window, dtype);
   if (r) return r;
   TAK_REQUIRE(block_tables && bt_strides && context_lens && block_size > 0, "compress paged: bad page table");
+  TAK_REQUIRE(max_blocks >= 0 && max_blocks <= 2147483647 && num_blocks >= 0,
+              "compress paged: bad max_blocks / num_blocks");
   TAK_REQUIRE(!gate || gate_strides, "compress paged: gate needs strides");
   a.cu_seqlens = nullptr;
   a.block_tables = block_tables; copy_strides(a.sbt, bt_strides, 2);
   a.context_lens = context_lens;
   a.block_size = static_cast<int>(block_size);
+  a.max_blocks = static_cast<int>(max_blocks);
+  a.num_blocks = num_blocks;
   a.gate = gate;
   if (gate) copy_strides(a.sg, gate_strides, 2);
   r = compress_launch(a, static_cast<cudaStream_t>(stream));
@@ -406,6 +456,7 @@ int tak_compress_kv_csa_hca(const void* k, const int64_t* k_strides, const void*
                             const int32_t* hca_offsets, int64_t num_hca, void* hca_k, const int64_t* hca_k_strides,
                             void* hca_v, const int64_t* hca_v_strides, int64_t num_kv_heads, int64_t head_dim,
                             int64_t head_dim_v, int64_t m, int64_t m_prime, int dtype, void* stream) {
+  TAK_ENTRY();
   if (num_csa == 0 && num_hca == 0) return 0;
   TAK_REQUIRE(v && csa_v && hca_v, "compress csa+hca: null v");
   TAK_REQUIRE(m > 0 && m_prime > 0, "compress csa+hca: m and m_prime must be positive");

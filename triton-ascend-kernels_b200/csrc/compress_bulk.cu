@@ -130,39 +130,39 @@ __global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a
       // stage layout: the chunk's K rows, then its V rows
       uint8_t* dst = smem + st * stage_bytes;
       uint8_t* vdst = dst + ch * kbytes;
-      if (lane == 0) mbar_arrive_expect_tx(&full[st], n * row_bytes);
-      __syncwarp();
+      // this lane's rows [a0, a1) of the chunk and their sources; a paged
+      // piece past the block-table row or on a page outside the cache is
+      // zero-filled here instead of copied
+      const int r0 = pc.r;
+      int a0 = r0, a1 = r0;
+      int64_t ko = 0, vo = 0;
+      bool valid = true;
       if (span) {
         // rows contiguous within a page (or a sequence): one copy per page
         // piece and tensor; lane t takes the piece in the chunk's t-th page
-        const int r0 = pc.r;
-        int a0 = r0, a1 = r0 + n;
-        int64_t ko = 0, vo = 0;
-        bool mine = lane == 0;
         if (paged) {
           const int pg = r0 / a.block_size + lane;
           a0 = max(r0, pg * a.block_size);
-          a1 = min(r0 + n, (pg + 1) * a.block_size);
-          mine = a0 < a1;
-          if (mine) {
-            const int64_t page = a.block_tables[pc.s * a.sbt[0] + static_cast<int64_t>(pg) * a.sbt[1]];
+          a1 = max(a0, min(r0 + n, (pg + 1) * a.block_size));
+          if (a0 < a1) {
+            const int64_t page = paged_row_page(a, pc.s, a0);
+            valid = page >= 0;
             const int64_t off = a0 - static_cast<int64_t>(pg) * a.block_size;
             ko = page * a.sk[0] + h * a.sk[1] + off * a.sk[2];
             vo = page * a.sv[0] + h * a.sv[1] + off * a.sv[2];
           }
-        } else {
+        } else if (lane == 0) {
+          a1 = r0 + n;
           ko = (pc.tok0 + r0) * a.sk[0] + h * a.sk[1];
           vo = (pc.tok0 + r0) * a.sv[0] + h * a.sv[1];
         }
-        if (mine) {
-          bulk_copy_g2s(dst + (a0 - r0) * kbytes, kb + ko, (a1 - a0) * kbytes, &full[st]);
-          if (vbytes) bulk_copy_g2s(vdst + (a0 - r0) * vbytes, vb + vo, (a1 - a0) * vbytes, &full[st]);
-        }
       } else if (lane < n) {
-        const int r = pc.r + lane;
-        int64_t ko, vo;
+        const int r = r0 + lane;
+        a0 = r;
+        a1 = r + 1;
         if (paged) {
-          const int64_t page = a.block_tables[pc.s * a.sbt[0] + (r / a.block_size) * a.sbt[1]];
+          const int64_t page = paged_row_page(a, pc.s, r);
+          valid = page >= 0;
           const int64_t off = r % a.block_size;
           ko = page * a.sk[0] + h * a.sk[1] + off * a.sk[2];
           vo = page * a.sv[0] + h * a.sv[1] + off * a.sv[2];
@@ -170,8 +170,26 @@ __global__ void __launch_bounds__(288) compress_bulk_kernel(const CompressArgs a
           ko = (pc.tok0 + r) * a.sk[0] + h * a.sk[1];
           vo = (pc.tok0 + r) * a.sv[0] + h * a.sv[1];
         }
-        bulk_copy_g2s(dst + lane * kbytes, kb + ko, kbytes, &full[st]);
-        if (vbytes) bulk_copy_g2s(vdst + lane * vbytes, vb + vo, vbytes, &full[st]);
+      }
+      const int nrow = a1 - a0;
+      if (nrow > 0 && !valid) {
+        // zero rows, stored before the arrive below publishes the stage
+        uint4* zk = reinterpret_cast<uint4*>(dst + (a0 - r0) * kbytes);
+        for (uint32_t i = 0; i < nrow * kbytes / 16; ++i) zk[i] = make_uint4(0u, 0u, 0u, 0u);
+        uint4* zv = reinterpret_cast<uint4*>(vdst + (a0 - r0) * vbytes);
+        for (uint32_t i = 0; i < nrow * vbytes / 16; ++i) zv[i] = make_uint4(0u, 0u, 0u, 0u);
+        fence_proxy_async_smem();
+      }
+      const uint32_t copy_bytes = (nrow > 0 && valid) ? nrow * row_bytes : 0u;
+      uint32_t stage_tx = copy_bytes;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) stage_tx += __shfl_xor_sync(0xffffffffu, stage_tx, o);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_expect_tx(&full[st], stage_tx);
+      __syncwarp();
+      if (copy_bytes) {
+        bulk_copy_g2s(dst + (a0 - r0) * kbytes, kb + ko, nrow * kbytes, &full[st]);
+        if (vbytes) bulk_copy_g2s(vdst + (a0 - r0) * vbytes, vb + vo, nrow * vbytes, &full[st]);
       }
       more = bulk_seg_next<WIN_BLOCKS>(pc, a, gend, ch);
     }
@@ -573,6 +591,7 @@ static bool compress_dual_typed(const CompressArgs& csa, const CompressArgs& hca
   if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
   kern<<<dim3(static_cast<unsigned>(hca.num_compressed), a.num_kv_heads), threads, smem, st>>>(csa, hca, ch, nst,
                                                                                               span);
+  note_kernel("compress_dual");
   return true;
 }
 
@@ -624,6 +643,7 @@ static bool compress_bulk_typed(const CompressArgs& a, cudaStream_t st, int* err
   else kern = m4 ? compress_bulk_kernel<T, 2, 4> : compress_bulk_kernel<T, 2, 0>;
   if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
   kern<<<grid, threads, smem, st>>>(a, ch, nst, span);
+  note_kernel("compress_bulk");
   *err = 0;
   return true;
 }

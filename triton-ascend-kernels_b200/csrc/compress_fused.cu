@@ -593,6 +593,7 @@ static int compress_csa_hca_typed(const CompressArgs& csa, const CompressArgs& h
   auto kern = (m == 4 && mp == 128) ? compress_csa_hca_kernel<T, 4, 32> : compress_csa_hca_kernel<T, 0, 0>;
   if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem)) return r;
   kern<<<grid, kThreads, smem, st>>>(tm[0], tm[1], p);
+  note_kernel("compress_csa_hca");
   *handled = true;
   return 0;
 }

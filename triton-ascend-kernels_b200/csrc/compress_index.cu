@@ -24,6 +24,12 @@
 
 namespace tak {
 
+// Gate logit of paged row r of sequence s (0 for a row that paged_row_page rejects).
+__device__ __forceinline__ float paged_gate(const CompressArgs& a, int s, int r) {
+  const int64_t page = paged_row_page(a, s, r);
+  return page < 0 ? 0.f : a.gate[page * a.sg[0] + (r % a.block_size) * a.sg[1]];
+}
+
 template <typename T, int VEC>
 __global__ void compress_kernel(const CompressArgs a) {
   const int64_t slot = blockIdx.x;
@@ -49,18 +55,14 @@ __global__ void compress_kernel(const CompressArgs a) {
   if (a.gate) {
     gmax = -INFINITY;
     for (int r = r0; r < r1; ++r) {
-      const float g = paged ? a.gate[a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]] * a.sg[0] +
-                                     (r % a.block_size) * a.sg[1]]
-                            : a.gate[(a.cu_seqlens[s] + r) * a.sg[0]];
+      const float g = paged ? paged_gate(a, s, r) : a.gate[(a.cu_seqlens[s] + r) * a.sg[0]];
       gmax = fmaxf(gmax, g);
     }
     gsum = 0.f;
     // a window whose logits are all -inf (every row masked) pools to zeros
     if (gmax != -INFINITY) {
       for (int r = r0; r < r1; ++r) {
-        const float g = paged ? a.gate[a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]] * a.sg[0] +
-                                       (r % a.block_size) * a.sg[1]]
-                              : a.gate[(a.cu_seqlens[s] + r) * a.sg[0]];
+        const float g = paged ? paged_gate(a, s, r) : a.gate[(a.cu_seqlens[s] + r) * a.sg[0]];
         gsum += __expf(g - gmax);
       }
     }
@@ -73,9 +75,10 @@ __global__ void compress_kernel(const CompressArgs a) {
     const T* row;
     float w = 1.f;
     if (paged) {
-      const int64_t page = a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]];
+      const int64_t page = paged_row_page(a, s, r);
+      if (a.gate) w = all_masked ? 0.f : __expf(paged_gate(a, s, r) - gmax);
+      if (page < 0) continue;  // a zero row: adds nothing to the sum
       row = base + page * st[0] + h * st[1] + (r % a.block_size) * st[2];
-      if (a.gate) w = all_masked ? 0.f : __expf(a.gate[page * a.sg[0] + (r % a.block_size) * a.sg[1]] - gmax);
     } else {
       const int64_t tok = a.cu_seqlens[s] + r;
       row = base + tok * st[0] + h * st[1];
@@ -155,16 +158,18 @@ __global__ void __launch_bounds__(128) compress_stream_kernel(const CompressArgs
         gv[k] = -INFINITY;
         if (r < r_end) {
           int64_t roff, goff;
+          bool ok = true;
           if (paged) {
-            const int64_t page = a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]];
+            const int64_t page = paged_row_page(a, s, r);
+            ok = page >= 0;  // rows past the table or on pages outside the cache: zero row, logit 0
             roff = page * st[0] + h * st[1] + (r % a.block_size) * st[2];
             goff = page * a.sg[0] + (r % a.block_size) * a.sg[1];
           } else {
             roff = (tok0 + r) * st[0] + h * st[1];
             goff = (tok0 + r) * a.sg[0];
           }
-          if (active) u[k] = __ldg(reinterpret_cast<const uint4*>(base + roff + d0));
-          if (a.gate) gv[k] = __ldg(a.gate + goff);
+          if (active && ok) u[k] = __ldg(reinterpret_cast<const uint4*>(base + roff + d0));
+          if (a.gate) gv[k] = ok ? __ldg(a.gate + goff) : 0.f;
         }
       }
 #pragma unroll
@@ -302,16 +307,18 @@ __global__ void __launch_bounds__(512) compress_split_kernel(const CompressArgs 
       gv[k] = -INFINITY;
       if (r < gb) {
         int64_t roff, goff;
+        bool ok = true;
         if (paged) {
-          const int64_t page = a.block_tables[s * a.sbt[0] + (r / a.block_size) * a.sbt[1]];
+          const int64_t page = paged_row_page(a, s, r);
+          ok = page >= 0;  // rows past the table or on pages outside the cache: zero row, logit 0
           roff = page * st[0] + h * st[1] + (r % a.block_size) * st[2];
           goff = page * a.sg[0] + (r % a.block_size) * a.sg[1];
         } else {
           roff = (tok0 + r) * st[0] + h * st[1];
           goff = (tok0 + r) * a.sg[0];
         }
-        if (active) u[k] = __ldg(reinterpret_cast<const uint4*>(base + roff + d0));
-        if (a.gate) gv[k] = __ldg(a.gate + goff);
+        if (active && ok) u[k] = __ldg(reinterpret_cast<const uint4*>(base + roff + d0));
+        if (a.gate) gv[k] = ok ? __ldg(a.gate + goff) : 0.f;
       }
     }
 #pragma unroll
@@ -401,6 +408,7 @@ static int compress_typed(const CompressArgs& a, cudaStream_t st) {
     const int threads = (a.head_dim + a.head_dim_v) / 8;
     if (vec && threads <= 128 && a.window == a.stride && a.stride >= 64) {
       compress_split_kernel<T><<<grid, 512, 0, st>>>(a);
+      note_kernel("compress_split");
       return 0;
     }
     if (vec && threads <= 128 && (a.window == a.stride || a.window == 2 * a.stride)) {
@@ -411,12 +419,14 @@ static int compress_typed(const CompressArgs& a, cudaStream_t st) {
         compress_stream_kernel<T, 1><<<dim3(ctas, a.num_kv_heads), 128, 0, st>>>(a, spc);
       else
         compress_stream_kernel<T, 2><<<dim3(ctas, a.num_kv_heads), 128, 0, st>>>(a, spc);
+      note_kernel("compress_stream");
       return 0;
     }
     if (vec) {
       const int threads = (a.head_dim + a.head_dim_v) / 8;
       if (threads > 1024) return set_error(2, "compress: head dim too large");
       compress_kernel<T, 8><<<grid, threads, 0, st>>>(a);
+      note_kernel("compress_rows");
       return 0;
     }
   }
@@ -424,6 +434,7 @@ static int compress_typed(const CompressArgs& a, cudaStream_t st) {
     const int threads = a.head_dim + a.head_dim_v;
     if (threads > 1024) return set_error(2, "compress: head dim too large");
     compress_kernel<T, 1><<<grid, threads, 0, st>>>(a);
+    note_kernel("compress_rows");
   }
   return 0;
 }

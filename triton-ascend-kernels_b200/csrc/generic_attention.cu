@@ -63,11 +63,15 @@ struct DecodeTopkRows {
   const int32_t* idx; int64_t s_idx;
   int ctx, num_win, block_size;
   int64_t ncomp;
+  int64_t wreach;      // block-table width x block_size
+  int64_t num_blocks;  // pages of the cache
   __device__ bool get(int i, RowPair<T>& r) const {
     const int64_t j = idx[i * s_idx];
     if (i < num_win) {
-      if (j < 0 || j >= ctx) return false;
+      // inside the context, inside the block-table row, on a page of the cache
+      if (j < 0 || j >= ctx || j >= wreach) return false;
       const int64_t page = bt[(j / block_size) * sbt_b];
+      if (page < 0 || page >= num_blocks) return false;
       const int64_t off = j % block_size;
       r.k = kc + page * sk_b + off * sk_s;
       r.v = vc + page * sv_b + off * sv_s;
@@ -202,7 +206,8 @@ __global__ void __launch_bounds__(128) sparse_generic_kernel(const SparseArgs a,
                            reinterpret_cast<const T*>(a.cv) + kvh * a.scv[1], a.scv[0],
                            a.block_tables + t * a.sbt[0], a.sbt[1],
                            a.topk + t * a.stk[0], a.stk[1],
-                           a.context_lens[t], a.num_win, a.block_size, a.num_compressed};
+                           a.context_lens[t], a.num_win, a.block_size, a.num_compressed,
+                           static_cast<int64_t>(a.max_blocks) * a.block_size, a.num_blocks};
     generic_attend<T>(q, a.sq[2], a.sk[3], a.sv[3], a.head_dim, a.head_dim_v, a.k_topk, rows, scale_log2, has_sink,
                       sink_log2, out, a.so[2], lse, 0.f);
   }
@@ -212,6 +217,7 @@ int prefill_generic_launch(const PrefillArgs& a, cudaStream_t st) {
   if (a.total_tokens == 0 || a.num_q_heads == 0) return 0;
   const float sl2 = a.scale * kLog2e;
   dim3 grid(a.total_tokens, a.num_q_heads);
+  note_kernel("prefill_generic");
   if (a.dtype == kBF16)
     prefill_generic_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(a, sl2);
   else if (a.dtype == kF16)
@@ -225,6 +231,7 @@ int sparse_generic_launch(const SparseArgs& a, cudaStream_t st) {
   if (a.num_tokens == 0 || a.num_q_heads == 0) return 0;
   const float sl2 = a.scale * kLog2e;
   dim3 grid(a.num_tokens, a.num_q_heads);
+  note_kernel("sparse_generic");
   if (a.dtype == kBF16)
     sparse_generic_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(a, sl2);
   else if (a.dtype == kF16)

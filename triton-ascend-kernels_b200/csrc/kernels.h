@@ -12,6 +12,11 @@ namespace tak {
 
 // error reporting (capi.cu): stores a message for tak_last_error(), returns code
 int set_error(int code, const char* msg);
+// records, for tak_last_kernel(), the main kernel the calling thread's current
+// entry point launched (a string literal)
+void note_kernel(const char* name);
+// cudaGetLastError after a launch: 0, or status 3 with the CUDA error as message
+int check_launch(const char* what);
 int num_sms();
 // cudaFuncAttributeMaxDynamicSharedMemorySize of `func` on the current device,
 // raised to at least `bytes` (set once per device and kernel, cached)
@@ -38,7 +43,18 @@ struct PagedDecodeArgs {
   int force_generic;  // 1 = use the generic kernel (tests)
 };
 size_t paged_decode_workspace_bytes(const PagedDecodeArgs& a);
+// Workspace bytes paged_decode_launch will use for these arguments: 0 when
+// the generic kernel runs or every sequence fits one split.
+size_t paged_decode_required_workspace(const PagedDecodeArgs& a);
 int paged_decode_launch(const PagedDecodeArgs& a, cudaStream_t st);
+// Argument validation and filling shared by the decode entry points (capi.cu).
+int make_paged_decode_args(PagedDecodeArgs* out_args, const void* q, const int64_t* q_strides, const void* k_cache,
+                           const int64_t* k_strides, const void* v_cache, const int64_t* v_strides,
+                           const int32_t* block_tables, const int64_t* bt_strides, const int32_t* context_lens,
+                           void* out, const int64_t* out_strides, float* lse, int64_t num_seqs,
+                           int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t block_size,
+                           int64_t max_blocks, int64_t num_blocks, int64_t cache_rows, float scale, int dtype,
+                           int split_pages);
 
 struct PrefillArgs {
   const void* q; int64_t sq[3];
@@ -69,6 +85,8 @@ struct SparseArgs {
   const int32_t* context_lens;
   int64_t num_compressed;
   int num_win, block_size;
+  int max_blocks;      // block-table width: window rows past max_blocks * block_size are masked
+  int64_t num_blocks;  // pages of the cache: a window row on a page id outside [0, num_blocks) is masked
   // both
   const int32_t* topk; int64_t stk[2];
   const float* sink;
@@ -93,6 +111,8 @@ struct CompressArgs {
   const int32_t* block_tables; int64_t sbt[2];
   const int32_t* context_lens;
   int block_size;
+  int max_blocks;      // block-table width (paged)
+  int64_t num_blocks;  // pages of the cache (paged); rows past the table or on pages outside it read as zeros
   const int32_t* comp_offsets;
   int num_seqs;
   int64_t num_compressed;
@@ -103,6 +123,16 @@ struct CompressArgs {
   int dtype;
   int64_t total_rows;  // TND token count (only the fused CSA + HCA launch reads it)
 };
+// Page holding row r of paged sequence s, or -1 when the row lies past the
+// sequence's block-table row or the table names a page outside the cache
+// (such rows pool as zero rows with gate logit 0).
+__device__ __forceinline__ int64_t paged_row_page(const CompressArgs& a, int s, int r) {
+  const int pg = r / a.block_size;
+  if (pg >= a.max_blocks) return -1;
+  const int64_t page = a.block_tables[s * a.sbt[0] + static_cast<int64_t>(pg) * a.sbt[1]];
+  return (page >= 0 && page < a.num_blocks) ? page : -1;
+}
+
 int compress_launch(const CompressArgs& a, cudaStream_t st);
 // Plain-mean pooling streamed through shared memory by bulk copies (16-bit
 // rows, strides in multiples of 8 elements, window = stride or 2 * stride, no

@@ -297,16 +297,18 @@ __global__ void __launch_bounds__(160, D >= 256 ? 1 : 2)
   }
 }
 
-// Merge the split partials of one (sequence, KV head, head chunk): weights of
-// every split first (shared memory), then each thread merges 4 consecutive
-// output elements of one head with all splits' 16-byte loads independent
-// (one memory round trip, not a chain).  When launched with programmatic
-// stream serialization the grid may start while the partial-writing grid is
-// still running; griddepcontrol.wait holds it until that grid has completed.
+// Merge the split partials of one (sequence, KV head, head chunk).  One warp
+// per query head reduces the splits' maxima and weighted sums with warp
+// shuffles (lane j holds splits j and j + 32; at most 64 splits), leaving each
+// split's weight 2^(m_j - M) in shared memory; then each thread merges 4
+// consecutive output elements of one head with all splits' 16-byte loads
+// independent (one memory round trip, not a chain).  When launched with
+// programmatic stream serialization the grid may start while the
+// partial-writing grid is still running; griddepcontrol.wait holds it until
+// that grid has completed.
 template <typename T>
 __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeParams p) {
   __shared__ float wts[16 * 64];
-  __shared__ float lsum[16 * 64];
   __shared__ float inv_l[16];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int kvh = blockIdx.y / p.head_chunks, hc = blockIdx.y % p.head_chunks, seq = blockIdx.x;
@@ -316,28 +318,24 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeP
   if (ctx <= 0 || n <= 1) return;
   const int h0 = kvh * p.G + hc * 16;
   const int gcnt = min(16, p.G - hc * 16);
-  const int tid = threadIdx.x;
-  // every (head, split) max and sum in one parallel round of loads
-  for (int i = tid; i < gcnt * n; i += 128) {
-    const int r = i / n, j = i % n;
-    const float2 ml = *reinterpret_cast<const float2*>(
-        &p.ws_ml[((static_cast<int64_t>(seq) * p.H + h0 + r) * p.max_splits + j) * 2]);
-    wts[r * n + j] = ml.x;
-    lsum[r * n + j] = ml.y;
-  }
-  __syncthreads();
-  if (tid < gcnt) {
-    float M = -INFINITY;
-    for (int j = 0; j < n; ++j) M = fmaxf(M, wts[tid * n + j]);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int r = warp; r < gcnt; r += 4) {
+    const float2* ml =
+        reinterpret_cast<const float2*>(p.ws_ml + (static_cast<int64_t>(seq) * p.H + h0 + r) * p.max_splits * 2);
+    float2 a = make_float2(-INFINITY, 0.f), b = make_float2(-INFINITY, 0.f);
+    if (lane < n) a = ml[lane];
+    if (lane + 32 < n) b = ml[lane + 32];
+    const float M = warp_max(fmaxf(a.x, b.x));
     const float Mu = (M == -INFINITY) ? 0.f : M;
-    float L = 0.f;
-    for (int j = 0; j < n; ++j) {
-      const float w = fast_exp2(wts[tid * n + j] - Mu);
-      wts[tid * n + j] = w;
-      L += lsum[tid * n + j] * w;
+    const float wa = lane < n ? fast_exp2(a.x - Mu) : 0.f;
+    const float wb = lane + 32 < n ? fast_exp2(b.x - Mu) : 0.f;
+    const float L = warp_sum(a.y * wa + b.y * wb);
+    if (lane < n) wts[r * n + lane] = wa;
+    if (lane + 32 < n) wts[r * n + lane + 32] = wb;
+    if (lane == 0) {
+      inv_l[r] = L > 0.f ? 1.f / L : 0.f;
+      if (p.lse) p.lse[seq * p.H + h0 + r] = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
     }
-    inv_l[tid] = L > 0.f ? 1.f / L : 0.f;
-    if (p.lse) p.lse[seq * p.H + h0 + tid] = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
   }
   __syncthreads();
   const int nvec = p.D / 4;
@@ -395,6 +393,7 @@ struct DecodeGenericParams {
   int64_t so_s, so_h, so_d;
   float* lse;
   int H, G, D, block_size, max_ctx;
+  int64_t num_blocks;
   float scale_log2;
 };
 
@@ -418,6 +417,9 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(const DecodeG
   float m = -INFINITY, l = 0.f;
   for (int tok = warp; tok < ctx; tok += 4) {
     const int64_t page = p.block_tables[seq * p.sbt_s + (tok / p.block_size) * p.sbt_b];
+    // a page id outside the cache reads as a zero row (score 0, value 0), as
+    // the fast path's TMA loads zero-fill it
+    const bool in_cache = page >= 0 && page < p.num_blocks;
     const int off = tok % p.block_size;
     const T* kr = kc + page * p.sk_b + kvh * p.sk_h + off * p.sk_s;
     const T* vr = vc + page * p.sv_b + kvh * p.sv_h + off * p.sv_s;
@@ -425,7 +427,7 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(const DecodeG
 #pragma unroll
     for (int i = 0; i < kGenMaxDPerLane; ++i) {
       const int d = lane + 32 * i;
-      if (d < p.D) s += qr[i] * Elem<T>::to_f(kr[d * p.sk_d]);
+      if (d < p.D && in_cache) s += qr[i] * Elem<T>::to_f(kr[d * p.sk_d]);
     }
     s = warp_sum(s) * p.scale_log2;
     const float mn = fmaxf(m, s);
@@ -434,7 +436,7 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(const DecodeG
 #pragma unroll
     for (int i = 0; i < kGenMaxDPerLane; ++i) {
       const int d = lane + 32 * i;
-      acc[i] = acc[i] * a + (d < p.D ? e * Elem<T>::to_f(vr[d * p.sv_d]) : 0.f);
+      acc[i] = acc[i] * a + (d < p.D && in_cache ? e * Elem<T>::to_f(vr[d * p.sv_d]) : 0.f);
     }
     m = mn;
   }
@@ -513,6 +515,13 @@ size_t paged_decode_workspace_bytes(const PagedDecodeArgs& a) {
                              256);
 }
 
+size_t paged_decode_required_workspace(const PagedDecodeArgs& a) {
+  if (a.num_seqs == 0 || a.num_q_heads == 0 || a.num_kv_heads == 0) return 0;
+  int ch = 0;
+  if (a.force_generic || !decode_fast_path_ok(a, &ch)) return 0;
+  return paged_decode_workspace_bytes(a);
+}
+
 static int encode_cache_map(CUtensorMap* map, const void* base, const int64_t* st, int64_t num_blocks,
                             int64_t hkv, int64_t rows, int64_t d, int box_rows) {
   const uint64_t dims[4] = {static_cast<uint64_t>(d), static_cast<uint64_t>(rows), static_cast<uint64_t>(hkv),
@@ -555,6 +564,7 @@ static int launch_fast(const PagedDecodeArgs& a, int pps, int max_splits, int he
   if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), SMEM)) return r;
   dim3 grid(max_splits, a.num_kv_heads * head_chunks, a.num_seqs);
   kern<<<grid, 160, SMEM, st>>>(mk, mv, p);
+  note_kernel("paged_decode_tc");
   if (max_splits > 1) {
     // programmatic dependent launch: the combine grid may be scheduled during
     // the main grid's last wave (it waits for the main grid in-kernel)
@@ -590,8 +600,10 @@ static int launch_generic(const PagedDecodeArgs& a, cudaStream_t st) {
   p.lse = a.lse;
   p.H = a.num_q_heads; p.G = a.num_q_heads / a.num_kv_heads; p.D = a.head_dim; p.block_size = a.block_size;
   p.max_ctx = a.max_blocks * a.block_size;
+  p.num_blocks = a.num_blocks;
   p.scale_log2 = a.scale * kLog2e;
   dim3 grid(a.num_q_heads, a.num_seqs);
+  note_kernel("paged_decode_generic");
   paged_decode_generic_kernel<T><<<grid, 128, 0, st>>>(p);
   return 0;
 }

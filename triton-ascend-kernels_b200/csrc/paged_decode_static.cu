@@ -19,9 +19,13 @@
 //     host threads) race and corrupt each other's partials -- serialise them;
 //   * nothing in the array needs to start at zero (every partial a call reads
 //     was written earlier in the same call);
-//   * the array's device address is looked up once per GPU, on the first call
-//     made with that GPU current; make that first call before any stream
-//     capture begins.
+//   * the array's device address is looked up on the first call made with a
+//     GPU current and again whenever that GPU's context has changed since
+//     (after cudaDeviceReset, for one); make the first call on each GPU, and
+//     the first after a reset, before any stream capture begins;
+//   * the arguments are validated as for tak_paged_attention_decode, and the
+//     size limit applies only when the split-KV kernels run (fp32 caches,
+//     unaligned strides and single-split sizes need no scratch).
 #include <cstdio>
 #include <mutex>
 
@@ -40,26 +44,61 @@ static __device__ __align__(256) unsigned char g_decode_static_scratch[kStaticSc
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchAddr {
+  void* ptr;
+  unsigned long long ctx_id;  // context the address belongs to (0: unknown)
+};
+ScratchAddr g_scratch[kMaxDevices] = {};
 
-// Device address of the scratch array on the current GPU (resolved once per GPU).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current CUDA context (0 when the driver
+// cannot tell); a new primary context after a device reset gets a new id.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&ctx) == CUDA_SUCCESS && ctx && get_id(ctx, &id) == CUDA_SUCCESS)
+    return id;
+  return 0;
+}
+
+// Device address of the scratch array on the current GPU: resolved on the
+// first call with that GPU current, and again when its context has changed.
 int static_scratch_address(void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return set_error(3, "paged decode (static scratch): no usable current CUDA device");
+  const unsigned long long ctx_id = current_context_id();
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  ScratchAddr& e = g_scratch[dev];
+  if (e.ptr == nullptr || e.ctx_id != ctx_id) {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_static_scratch);
-    if (e != cudaSuccess || p == nullptr) {
+    const cudaError_t r = cudaGetSymbolAddress(&p, g_decode_static_scratch);
+    if (r != cudaSuccess || p == nullptr) {
       char buf[200];
       std::snprintf(buf, sizeof(buf), "paged decode (static scratch): cudaGetSymbolAddress failed: %s",
-                    cudaGetErrorString(e));
+                    cudaGetErrorString(r));
       return set_error(3, buf);
     }
-    g_scratch_addr[dev] = p;
+    e.ptr = p;
+    e.ctx_id = current_context_id();  // the lookup made the device's context current
   }
-  *out = g_scratch_addr[dev];
+  *out = e.ptr;
   return 0;
 }
 }  // namespace
@@ -73,8 +112,13 @@ extern "C" int tak_paged_attention_decode_static_scratch(
     int64_t head_dim, int64_t block_size, int64_t max_blocks, int64_t num_blocks, int64_t cache_rows, float scale,
     int dtype, int split_pages, void* stream) {
   using namespace tak;
-  const size_t need = tak_paged_attention_decode_workspace_size(num_seqs, num_q_heads, num_kv_heads, head_dim,
-                                                                block_size, max_blocks, split_pages);
+  note_kernel("");
+  PagedDecodeArgs a{};
+  int r = make_paged_decode_args(&a, q, q_strides, k_cache, k_strides, v_cache, v_strides, block_tables, bt_strides,
+                                 context_lens, out, out_strides, lse, num_seqs, num_q_heads, num_kv_heads, head_dim,
+                                 block_size, max_blocks, num_blocks, cache_rows, scale, dtype, split_pages);
+  if (r || num_seqs == 0) return r;
+  const size_t need = paged_decode_required_workspace(a);
   if (need > kStaticScratchBytes) {
     char buf[300];
     std::snprintf(buf, sizeof(buf),
@@ -83,13 +127,10 @@ extern "C" int tak_paged_attention_decode_static_scratch(
                   need, kStaticScratchBytes);
     return set_error(2, buf);
   }
-  void* scratch = nullptr;
   if (need > 0) {
-    const int r = static_scratch_address(&scratch);
-    if (r) return r;
+    if ((r = static_scratch_address(&a.workspace))) return r;
+    a.workspace_bytes = kStaticScratchBytes;
   }
-  return tak_paged_attention_decode(q, q_strides, k_cache, k_strides, v_cache, v_strides, block_tables, bt_strides,
-                                    context_lens, out, out_strides, lse, num_seqs, num_q_heads, num_kv_heads,
-                                    head_dim, block_size, max_blocks, num_blocks, cache_rows, scale, dtype, scratch,
-                                    need > 0 ? kStaticScratchBytes : 0, split_pages, stream);
+  r = paged_decode_launch(a, static_cast<cudaStream_t>(stream));
+  return r ? r : check_launch("paged decode (static scratch)");
 }

@@ -459,6 +459,7 @@ int prefill_tc_launch(const PrefillArgs& a, cudaStream_t st, bool* handled) {
     if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(prefill_tc_kernel<__half>), pf::SMEM)) return r;
     prefill_tc_kernel<__half><<<grid, 320, pf::SMEM, st>>>(mq, mk, mv, p);
   }
+  note_kernel("prefill_tc");
   *handled = true;
   return 0;
 }

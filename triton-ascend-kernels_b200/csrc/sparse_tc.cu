@@ -71,14 +71,23 @@ struct SparseTcParams {
   const int32_t* ctx_lens;
   int64_t ncomp;
   int num_win, block_size;
+  int64_t wreach;      // block-table width x block_size: window positions at or past it are masked
+  int64_t num_blocks;  // pages of the cache: a window position on a page id outside [0, num_blocks) is masked
 };
 
 // Validity of slot c holding index j (decode: by slot position, SA:151-171 for
-// the window slots [0, num_win) and SA:197-210 for the compressed ones).
+// the window slots [0, num_win) and SA:197-210 for the compressed ones).  A
+// window slot must also lie inside its block-table row and name a page of the
+// cache (the reference reads past both unchecked); bt_row is the request's
+// block-table row.
 template <bool DECODE>
-__device__ __forceinline__ bool sp_slot_valid(const SparseTcParams& p, int c, int64_t j, int ctx) {
+__device__ __forceinline__ bool sp_slot_valid(const SparseTcParams& p, int c, int64_t j, int ctx,
+                                              const int32_t* bt_row) {
   if (!DECODE) return j >= 0 && j < p.kv_rows;
-  return c < p.num_win ? (j >= 0 && j < ctx) : (j >= ctx && j - ctx < p.ncomp);
+  if (c >= p.num_win) return j >= ctx && j - ctx < p.ncomp;
+  if (j < 0 || j >= ctx || j >= p.wreach) return false;
+  const int64_t page = bt_row[(j / p.block_size) * p.sbt1];
+  return page >= 0 && page < p.num_blocks;
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int c0, int c1) {
@@ -155,6 +164,7 @@ __global__ void __launch_bounds__(288, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int32_t* idx_row = p.topk + static_cast<int64_t>(t) * p.stk0;
   const int ctx = DECODE ? p.ctx_lens[t] : 0;
+  const int32_t* bt_row = DECODE ? p.bt + static_cast<int64_t>(t) * p.sbt0 : nullptr;
 
   if (tid == 0) {
     mbar_init(q_full, 1);
@@ -192,7 +202,6 @@ __global__ void __launch_bounds__(288, 1)
     }
     const T* kb = reinterpret_cast<const T*>(p.k);
     const T* vb = reinterpret_cast<const T*>(p.v);
-    const int32_t* bt_row = DECODE ? p.bt + static_cast<int64_t>(t) * p.sbt0 : nullptr;
     // K (and V unless shared) row addresses of this thread's 4 slots of tile j; null = masked
     auto load_rows = [&](int j, const T** kr, const T** vr) {
 #pragma unroll
@@ -201,7 +210,7 @@ __global__ void __launch_bounds__(288, 1)
         const int64_t r = (j < n_tiles && c < p.k_topk) ? static_cast<int64_t>(idx_row[c * p.stk1]) : -1;
         kr[g] = nullptr;
         vr[g] = nullptr;
-        if (!(j < n_tiles && c < p.k_topk) || !sp_slot_valid<DECODE>(p, c, r, ctx)) continue;
+        if (!(j < n_tiles && c < p.k_topk) || !sp_slot_valid<DECODE>(p, c, r, ctx, bt_row)) continue;
         if (!DECODE) {
           kr[g] = kb + r * p.k_s0 + kvh * p.k_sh;
           if (!SHARED) vr[g] = vb + r * p.v_s0 + kvh * p.v_sh;
@@ -335,8 +344,10 @@ __global__ void __launch_bounds__(288, 1)
       const int c0 = j * BN + lane, c1 = c0 + 32;
       const int64_t r0 = c0 < p.k_topk ? static_cast<int64_t>(idx_row[c0 * p.stk1]) : -1;
       const int64_t r1 = c1 < p.k_topk ? static_cast<int64_t>(idx_row[c1 * p.stk1]) : -1;
-      const uint32_t lo = __ballot_sync(0xffffffffu, c0 < p.k_topk && sp_slot_valid<DECODE>(p, c0, r0, ctx));
-      const uint32_t hi_m = __ballot_sync(0xffffffffu, c1 < p.k_topk && sp_slot_valid<DECODE>(p, c1, r1, ctx));
+      const uint32_t lo =
+          __ballot_sync(0xffffffffu, c0 < p.k_topk && sp_slot_valid<DECODE>(p, c0, r0, ctx, bt_row));
+      const uint32_t hi_m =
+          __ballot_sync(0xffffffffu, c1 < p.k_topk && sp_slot_valid<DECODE>(p, c1, r1, ctx, bt_row));
       return hi ? hi_m : lo;
     };
     uint32_t vnext = n_tiles > 0 ? tile_mask(0) : 0u;
@@ -528,11 +539,14 @@ static int launch_sparse_tc_mode(const SparseArgs& a, cudaStream_t st) {
     p.ncomp = a.num_compressed;
     p.num_win = a.num_win;
     p.block_size = a.block_size;
+    p.wreach = static_cast<int64_t>(a.max_blocks) * a.block_size;
+    p.num_blocks = a.num_blocks;
   }
   auto kern = sparse_tc_kernel<T, DQK, DV, SHARED, DECODE>;
   if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::SMEM)) return r;
   dim3 grid(a.num_tokens, a.num_kv_heads * p.head_chunks);
   kern<<<grid, 288, L::SMEM, st>>>(mq, p);
+  note_kernel("sparse_tc");
   return 0;
 }
 
