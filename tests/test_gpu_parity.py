@@ -248,6 +248,27 @@ def test_prefill_edge_lengths(D, causal, kernel_path):
     assert (npy(out)[-3:] == 0).all()
 
 
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_prefill_head_dims_take_tensor_cores(D, causal, dtype):
+    """Every power-of-two head dim the tensor-core prefill takes (64, 128,
+    256; the reference's HEAD_DIM is a free constexpr, FP:24,49) runs on the
+    tcgen05 kernel -- asserted through tak_last_kernel() -- and matches the
+    oracle: ragged lengths past several 128- and 256-row blocks, GQA 8/2."""
+    lens = [1, 129, 300, 0, 1000, 2100]
+    Tn = sum(lens)
+    g = torch.Generator().manual_seed(7 + D)
+    q = torch.randn(Tn, 8, D, generator=g).to(DEV, dtype)
+    k = torch.randn(Tn, 2, D, generator=g).to(DEV, dtype)
+    v = torch.randn(Tn, 2, D, generator=g).to(DEV, dtype)
+    out, lse = FP.flash_attention_prefill(q, k, v, _cu_t(lens), causal, return_lse=True)
+    assert T.last_kernel() == "prefill_tc"
+    ref, ref_lse = O.prefill(npy(q), npy(k), npy(v), [0] + np.cumsum(lens).tolist(), causal, acc=np.float32)
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+
+
 def _paged_case(B, H, Hkv, D, P, max_ctx, pool, dtype, seed, ctx=None):
     g = torch.Generator().manual_seed(seed)
     if ctx is None:

@@ -6,7 +6,9 @@
 // (FP:97), plus the natural-log LSE.
 //
 // One CTA = up to 256 query rows of one sequence x one query head, as two
-// 128-row tiles A and B that share every K/V block.  Row blocks are 256-row
+// 128-row tiles A and B that share every K/V block (head dims 64 and 128; a
+// 256-dim head's O fills 256 TMEM columns, so there a CTA owns one 128-row
+// tile and single-stage K/V rings: 64 KB each for Q, K and V).  Row blocks are 256-row
 // blocks aligned to global token positions (clipped to the sequence owning the
 // block's first row) plus one "head piece" per sequence for its rows before
 // the first aligned boundary, so the schedule needs no host-side table (the
@@ -29,7 +31,8 @@
 //               reads O, normalises, stores the row and its LSE.  While one
 //               warpgroup runs its softmax the tensor core works on the other
 //               tile.
-// TMEM: O_A [0,128), O_B [128,256), S/P_A [256,384), S/P_B [384,512).
+// TMEM: O_A [0,128), O_B [128,256), S/P_A [256,384), S/P_B [384,512); with
+// one tile (D = 256), O_A [0,256) and S/P_A [256,384).
 #include <type_traits>
 
 #include "common.cuh"
@@ -47,13 +50,24 @@ struct PrefillTcParams {
 };
 
 namespace pf {
-constexpr int BM = 128, BN = 128, D = 128, ROWS = 256;
+constexpr int BM = 128, BN = 128;
 constexpr int TILE = 128 * 128;                   // one 64-column block of 128 rows (bytes)
-constexpr int QOFF = 0, KOFF = 4 * TILE, VOFF = 8 * TILE;
-constexpr int BAROFF = 12 * TILE;                 // 192 KB of tiles, then barriers
 constexpr int NBAR = 15;
-constexpr int SMEM = BAROFF + NBAR * 8 + 16 + 1024;
 constexpr float kRescaleThreshold = 8.f;          // log2 units
+// Shared-memory layout and tiling of head dim D: NT query tiles of 128 rows
+// per CTA, NST-stage K and V rings, NB 64-column boxes per row.
+template <int D>
+struct Cfg {
+  static constexpr int NB = D / 64;
+  static constexpr int NT = D >= 256 ? 1 : 2;
+  static constexpr int NST = D >= 256 ? 1 : 2;
+  static constexpr int ROWS = NT * BM;
+  static constexpr int QOFF = 0;
+  static constexpr int KOFF = NT * NB * TILE;
+  static constexpr int VOFF = KOFF + NST * NB * TILE;
+  static constexpr int BAROFF = VOFF + NST * NB * TILE;
+  static constexpr int SMEM = BAROFF + NBAR * 8 + 16 + 1024;
+};
 }  // namespace pf
 
 __device__ __forceinline__ int pf_find_seq(const int32_t* cu, int n, int t) {
@@ -70,14 +84,17 @@ __device__ __forceinline__ int pf_find_seq(const int32_t* cu, int n, int t) {
   return ans;
 }
 
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(320, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const PrefillTcParams p) {
   using namespace pf;
+  using C = Cfg<D>;
+  constexpr int NB = C::NB, NST = C::NST, ROWS = C::ROWS;
+  constexpr int QOFF = C::QOFF, KOFF = C::KOFF, VOFF = C::VOFF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAROFF);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAROFF);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
@@ -89,8 +106,10 @@ __global__ void __launch_bounds__(320, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
-  const int h = blockIdx.x;
-  const int slot = blockIdx.y;
+  // blockIdx.x = slot * H + h: the heads of one row block are adjacent (they
+  // share K/V through L2) and the grid has no 65535 limit on row blocks
+  const int h = static_cast<int>(blockIdx.x % static_cast<unsigned>(p.H));
+  const int slot = static_cast<int>(blockIdx.x / static_cast<unsigned>(p.H));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = p.num_seqs;
   const int cu_end = p.cu_seqlens[S];
@@ -161,28 +180,27 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       const int nq = rows_t[1] > 0 ? 2 : 1;
-      mbar_arrive_expect_tx(q_full, nq * 2 * TILE);
-      for (int t = 0; t < nq; ++t) {
-        tma_load_3d(smem + QOFF + t * 2 * TILE, &tmQ, q_full, 0, h, row0 + t * BM);
-        tma_load_3d(smem + QOFF + t * 2 * TILE + TILE, &tmQ, q_full, 64, h, row0 + t * BM);
-      }
+      mbar_arrive_expect_tx(q_full, nq * NB * TILE);
+      for (int t = 0; t < nq; ++t)
+        for (int b = 0; b < NB; ++b)
+          tma_load_3d(smem + QOFF + (t * NB + b) * TILE, &tmQ, q_full, b * 64, h, row0 + t * BM);
       for (int j = 0; j < n_kv && !*abort_flag; ++j) {
-        const int st = j & 1;
+        const int st = j % NST;
         const int key0 = seq_start + j * BN;
-        if (j >= 2 && !mbar_wait(&k_empty[st], ((j >> 1) - 1) & 1)) {
+        if (j >= NST && !mbar_wait(&k_empty[st], ((j / NST) - 1) & 1)) {
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[st], 2 * TILE);
-        tma_load_3d(smem + KOFF + st * 2 * TILE, &tmK, &k_full[st], 0, kvh, key0);
-        tma_load_3d(smem + KOFF + st * 2 * TILE + TILE, &tmK, &k_full[st], 64, kvh, key0);
-        if (j >= 2 && !mbar_wait(&v_empty[st], ((j >> 1) - 1) & 1)) {
+        mbar_arrive_expect_tx(&k_full[st], NB * TILE);
+        for (int b = 0; b < NB; ++b)
+          tma_load_3d(smem + KOFF + (st * NB + b) * TILE, &tmK, &k_full[st], b * 64, kvh, key0);
+        if (j >= NST && !mbar_wait(&v_empty[st], ((j / NST) - 1) & 1)) {
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&v_full[st], 2 * TILE);
-        tma_load_3d(smem + VOFF + st * 2 * TILE, &tmV, &v_full[st], 0, kvh, key0);
-        tma_load_3d(smem + VOFF + st * 2 * TILE + TILE, &tmV, &v_full[st], 64, kvh, key0);
+        mbar_arrive_expect_tx(&v_full[st], NB * TILE);
+        for (int b = 0; b < NB; ++b)
+          tma_load_3d(smem + VOFF + (st * NB + b) * TILE, &tmV, &v_full[st], b * 64, kvh, key0);
       }
     }
   } else if (warp == 9) {
@@ -198,9 +216,9 @@ __global__ void __launch_bounds__(320, 1)
       const uint64_t q_desc0 = tc_sdesc_sw128(sbase + QOFF, 16, 1024);
       const uint64_t k_desc0 = tc_sdesc_sw128(sbase + KOFF, 16, 1024);
       const uint64_t v_desc0 = tc_sdesc_sw128(sbase + VOFF, TILE, 1024);
-      constexpr uint64_t kTileStep = (2 * TILE) >> 4;  // next Q tile / next K or V stage
+      constexpr uint64_t kTileStep = (NB * TILE) >> 4;  // next Q tile / next K or V stage
       auto qk = [&](int t, int j) {
-        const uint64_t qd = q_desc0 + (t ? kTileStep : 0), kd = k_desc0 + ((j & 1) ? kTileStep : 0);
+        const uint64_t qd = q_desc0 + (t ? kTileStep : 0), kd = k_desc0 + ((j % NST) ? kTileStep : 0);
         const uint32_t d_tmem = taddr + 256 + t * 128;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -210,7 +228,7 @@ __global__ void __launch_bounds__(320, 1)
         tc_commit(&s_full[t]);
       };
       auto pv = [&](int t, int j) {
-        const uint64_t vd = v_desc0 + ((j & 1) ? kTileStep : 0);
+        const uint64_t vd = v_desc0 + ((j % NST) ? kTileStep : 0);
         const uint32_t p_tmem = taddr + 256 + t * 128;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
@@ -233,8 +251,8 @@ __global__ void __launch_bounds__(320, 1)
         // Per tile: P.V of block j, then (once that P.V has read P) S of block
         // j + 1, so a tile's next softmax can start while the other tile's
         // softmax is still running.
-        const int st = j & 1;
-        if (!(ok = mbar_wait(&v_full[st], (j >> 1) & 1))) break;
+        const int st = j % NST;
+        if (!(ok = mbar_wait(&v_full[st], (j / NST) & 1))) break;
         const bool next = j + 1 < n_kv;
         bool k_next = false;  // K block j + 1 waited for
 #pragma unroll
@@ -245,7 +263,7 @@ __global__ void __launch_bounds__(320, 1)
             pv(t, j);
             if (t == 1 || j >= n_t[1]) tc_commit(&v_empty[st]);
             if (j + 1 < n_t[t]) {
-              if (!k_next && !(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) break;
+              if (!k_next && !(ok = mbar_wait(&k_full[(j + 1) % NST], ((j + 1) / NST) & 1))) break;
               k_next = true;
               // this tile's S/P columns are rewritten only after its PV of block j has read P
               if (!(ok = mbar_wait(&o_done[t], j & 1))) break;
@@ -259,8 +277,8 @@ __global__ void __launch_bounds__(320, 1)
           // every tile with block j + 1 has issued its S MMA; the commit frees the K stage
           // (a tile without block j + 1 issues none, and then k_full of block j + 1 may
           // not have been waited for: wait here so the stage's phases stay in step)
-          if (!k_next && !(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) break;
-          tc_commit(&k_empty[(j + 1) & 1]);
+          if (!k_next && !(ok = mbar_wait(&k_full[(j + 1) % NST], ((j + 1) / NST) & 1))) break;
+          tc_commit(&k_empty[(j + 1) % NST]);
         }
       }
       if (!ok && n_kv > 0) *abort_flag = 1;
@@ -317,7 +335,7 @@ __global__ void __launch_bounds__(320, 1)
         const float f = rescale_o ? fast_exp2(m_used - m_new) : 1.f;
         uint32_t orow[32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < D / 32; ++c) {
           tmem_ld32(o_tmem + c * 32, orow);
           tmem_ld_wait();
 #pragma unroll
@@ -379,24 +397,32 @@ __global__ void __launch_bounds__(320, 1)
     if (!ok) *abort_flag = 1;
     if (nt > 0) {
       tc_fence_after();
-      float o[128];
+      const float f = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_run);
+      const float inv = (l > 0.f && ok) ? f / (l * f + 1e-6f) : 0.f;
+      T* orow = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(row0 + t * BM + r) * p.so_t +
+                static_cast<int64_t>(h) * p.so_h;
+      // up to 128 columns of O per TMEM round trip (all loads, one wait, stores)
+      constexpr int CW = D < 128 ? D : 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(o_tmem + c * 32, reinterpret_cast<uint32_t*>(o) + c * 32);
-      tmem_ld_wait();
-      if (row_ok) {
-        const float f = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_run);
-        const float inv = (l > 0.f && ok) ? f / (l * f + 1e-6f) : 0.f;
-        T* orow = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(row0 + t * BM + r) * p.so_t +
-                  static_cast<int64_t>(h) * p.so_h;
+      for (int c0 = 0; c0 < D; c0 += CW) {
+        float o[CW];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          uint4 u;
-          u.x = Elem<T>::pack2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
-          u.y = Elem<T>::pack2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-          u.z = Elem<T>::pack2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-          u.w = Elem<T>::pack2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-          *reinterpret_cast<uint4*>(orow + 8 * c) = u;
+        for (int c = 0; c < CW / 32; ++c)
+          tmem_ld32(o_tmem + c0 + c * 32, reinterpret_cast<uint32_t*>(o) + c * 32);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int c = 0; c < CW / 8; ++c) {
+            uint4 u;
+            u.x = Elem<T>::pack2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
+            u.y = Elem<T>::pack2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+            u.z = Elem<T>::pack2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+            u.w = Elem<T>::pack2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c0 + 8 * c) = u;
+          }
         }
+      }
+      if (row_ok) {
         if (p.lse)
           p.lse[static_cast<int64_t>(row0 + t * BM + r) * p.H + h] =
               (l > 0.f && ok) ? (m_used + __log2f(l)) * kLn2 : -INFINITY;
@@ -411,8 +437,8 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
-static int encode_tnd_map(CUtensorMap* m, const void* base, const int64_t* st, int64_t T, int64_t heads) {
-  const uint64_t dims[3] = {128, static_cast<uint64_t>(heads), static_cast<uint64_t>(T)};
+static int encode_tnd_map(CUtensorMap* m, const void* base, const int64_t* st, int64_t T, int64_t heads, int d) {
+  const uint64_t dims[3] = {static_cast<uint64_t>(d), static_cast<uint64_t>(heads), static_cast<uint64_t>(T)};
   const uint64_t strides[2] = {static_cast<uint64_t>(st[1] * 2), static_cast<uint64_t>(st[0] * 2)};
   const uint32_t box[3] = {64, 1, 128};
   const uint32_t es[3] = {1, 1, 1};
@@ -425,17 +451,14 @@ static bool tma_ok(const void* ptr, const int64_t* st) {
   return st[0] > 0 && st[1] > 0 && (st[0] * 2) % 16 == 0 && (st[1] * 2) % 16 == 0;
 }
 
-int prefill_tc_launch(const PrefillArgs& a, cudaStream_t st, bool* handled) {
-  *handled = false;
-  if (a.dtype == kF32 || a.head_dim != 128 || a.head_dim_v != 128) return 0;
-  if (!tma_ok(a.q, a.sq) || !tma_ok(a.k, a.sk) || !tma_ok(a.v, a.sv)) return 0;
-  if (a.so[2] != 1 || (a.so[0] % 8) || (a.so[1] % 8) || (reinterpret_cast<uintptr_t>(a.out) & 15)) return 0;
-  const int n_aligned = (a.total_tokens + pf::ROWS - 1) / pf::ROWS;
-  if (static_cast<int64_t>(n_aligned) + a.num_seqs + 1 > 65535) return 0;
+template <typename T, int D>
+static int launch_prefill_tc(const PrefillArgs& a, cudaStream_t st) {
+  using C = pf::Cfg<D>;
+  const int64_t n_aligned = (static_cast<int64_t>(a.total_tokens) + C::ROWS - 1) / C::ROWS;
   CUtensorMap mq, mk, mv;
-  if (int r = encode_tnd_map(&mq, a.q, a.sq, a.total_tokens, a.num_q_heads)) return r;
-  if (int r = encode_tnd_map(&mk, a.k, a.sk, a.total_tokens, a.num_kv_heads)) return r;
-  if (int r = encode_tnd_map(&mv, a.v, a.sv, a.total_tokens, a.num_kv_heads)) return r;
+  if (int r = encode_tnd_map(&mq, a.q, a.sq, a.total_tokens, a.num_q_heads, D)) return r;
+  if (int r = encode_tnd_map(&mk, a.k, a.sk, a.total_tokens, a.num_kv_heads, D)) return r;
+  if (int r = encode_tnd_map(&mv, a.v, a.sv, a.total_tokens, a.num_kv_heads, D)) return r;
   PrefillTcParams p{};
   p.cu_seqlens = a.cu_seqlens;
   p.num_seqs = a.num_seqs;
@@ -443,25 +466,42 @@ int prefill_tc_launch(const PrefillArgs& a, cudaStream_t st, bool* handled) {
   p.H = a.num_q_heads;
   p.Hkv = a.num_kv_heads;
   p.G = a.num_q_heads / a.num_kv_heads;
-  p.n_aligned = n_aligned;
+  p.n_aligned = static_cast<int>(n_aligned);
   p.causal = a.causal;
   p.out = a.out;
   p.so_t = a.so[0];
   p.so_h = a.so[1];
   p.lse = a.lse;
   p.scale_log2 = a.scale * kLog2e;
-  dim3 grid(a.num_q_heads, n_aligned + a.num_seqs + 1);
-  if (a.dtype == kBF16) {
-    if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(prefill_tc_kernel<__nv_bfloat16>), pf::SMEM))
-      return r;
-    prefill_tc_kernel<__nv_bfloat16><<<grid, 320, pf::SMEM, st>>>(mq, mk, mv, p);
-  } else {
-    if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(prefill_tc_kernel<__half>), pf::SMEM)) return r;
-    prefill_tc_kernel<__half><<<grid, 320, pf::SMEM, st>>>(mq, mk, mv, p);
-  }
+  // one CTA per (row block, query head); the last row-block slot per head zeroes
+  // the rows past the last sequence
+  const dim3 grid(static_cast<unsigned>((n_aligned + a.num_seqs + 1) * a.num_q_heads));
+  auto kern = prefill_tc_kernel<T, D>;
+  if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::SMEM)) return r;
+  kern<<<grid, 320, C::SMEM, st>>>(mq, mk, mv, p);
   note_kernel("prefill_tc");
-  *handled = true;
   return 0;
+}
+
+int prefill_tc_launch(const PrefillArgs& a, cudaStream_t st, bool* handled) {
+  *handled = false;
+  if (a.dtype == kF32 || a.head_dim != a.head_dim_v) return 0;
+  if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256) return 0;
+  if (!tma_ok(a.q, a.sq) || !tma_ok(a.k, a.sk) || !tma_ok(a.v, a.sv)) return 0;
+  if (a.so[2] != 1 || (a.so[0] % 8) || (a.so[1] % 8) || (reinterpret_cast<uintptr_t>(a.out) & 15)) return 0;
+  // the grid's one dimension holds (row blocks + sequences + 1) x heads CTAs
+  const int rows = a.head_dim >= 256 ? pf::BM : 2 * pf::BM;
+  const int64_t ctas = ((static_cast<int64_t>(a.total_tokens) + rows - 1) / rows + a.num_seqs + 1) * a.num_q_heads;
+  if (ctas > 2147483647) return 0;
+  int r;
+  const bool bf = a.dtype == kBF16;
+  switch (a.head_dim) {
+    case 64: r = bf ? launch_prefill_tc<__nv_bfloat16, 64>(a, st) : launch_prefill_tc<__half, 64>(a, st); break;
+    case 128: r = bf ? launch_prefill_tc<__nv_bfloat16, 128>(a, st) : launch_prefill_tc<__half, 128>(a, st); break;
+    default: r = bf ? launch_prefill_tc<__nv_bfloat16, 256>(a, st) : launch_prefill_tc<__half, 256>(a, st); break;
+  }
+  *handled = true;
+  return r;
 }
 
 }  // namespace tak
