@@ -145,18 +145,22 @@ DEC = dict(batch=64, q_heads=32, kv_heads=8, head_dim=128, page=128, pool=5000, 
 
 
 def decode_inputs(seed, device, world=1, rank=0):
-    """One global batch of 64 x world requests drawn from one seed (context
-    lengths, q), assigned to ranks by the longest-processing-time rule on
-    context length (sharding.shard_requests: the bytes each request streams).
-    Returns this rank's (q, k_cache, v_cache, block_tables, context_lens) and
-    every rank's global request ids.  Each rank holds its own 5000-page pool;
-    its requests' pages are drawn in order from one random permutation of it.
-    At world = 1 this is the single-GPU batch: requests 0..63 in order."""
+    """One global batch of 64 x world requests from one seed, assigned to
+    ranks by the longest-processing-time rule on context length
+    (sharding.shard_requests: the bytes each request streams).  Weak scaling:
+    the batch at N GPUs holds the 64 context lengths of the one-GPU batch N
+    times over (fresh queries for every copy), so each GPU's share streams the
+    same bytes as the one-GPU step.  Returns this rank's (q, k_cache, v_cache,
+    block_tables, context_lens) and every rank's global request ids.  Each
+    rank holds its own 5000-page pool; its requests' pages are drawn in order
+    from one random permutation of it.  At world = 1 this is the single-GPU
+    batch: requests 0..63 in order."""
     import sharding
     c = DEC
     g = torch.Generator().manual_seed(seed)
     n = c["batch"] * world
-    ctx_all = torch.randint(1, c["max_ctx"] + 1, (n,), generator=g, dtype=torch.int64).to(torch.int32)
+    ctx_all = torch.randint(1, c["max_ctx"] + 1, (c["batch"],), generator=g, dtype=torch.int64).to(torch.int32)
+    ctx_all = ctx_all.repeat(world)
     maxb = c["max_ctx"] // c["page"]
     perm = torch.randperm(c["pool"], generator=g).to(torch.int32)
     q_all = torch.randn(n, c["q_heads"], c["head_dim"], generator=g).to(torch.bfloat16)
@@ -244,10 +248,11 @@ class PipelinedE2E:
     `outputs` lists their (shape, dtype).  The copies back of consecutive
     steps are ordered on their stream, so one pinned host set receives them."""
 
-    def __init__(self, host_inputs, compute, outputs, device, copy_back=True):
+    def __init__(self, host_inputs, compute, outputs, device, copy_back=True, post=None):
         self.hin = [t if t.is_pinned() else t.pin_memory() for t in host_inputs]
         self.sets = [[torch.empty(t.shape, dtype=t.dtype, device=device) for t in self.hin] for _ in range(2)]
         self.compute = compute
+        self.post = post  # runs on the copy-back stream after compute (the NCCL output gather)
         self.copy_back = copy_back
         self.hout = [torch.empty(sh, dtype=dt).pin_memory() for sh, dt in outputs] if copy_back else None
         self.h2d = torch.cuda.Stream(device)
@@ -276,11 +281,16 @@ class PipelinedE2E:
         o = self.compute(*self.sets[b])
         outs = o if isinstance(o, (tuple, list)) else (o,)
         self.ev_done[b].record(self.comp)
-        if self.copy_back:
+        if self.copy_back or self.post is not None:
             with torch.cuda.stream(self.d2h):
                 self.d2h.wait_event(self.ev_done[b])
-                for h, d in zip(self.hout, outs):
-                    h.copy_(d, non_blocking=True)
+                res = outs
+                if self.post is not None:
+                    r = self.post(*outs)
+                    res = r if isinstance(r, (tuple, list)) else (r,)
+                if self.copy_back:
+                    for h, d in zip(self.hout, res):
+                        h.copy_(d, non_blocking=True)
             for d in outs:
                 d.record_stream(self.d2h)
         self.i += 1
@@ -296,7 +306,7 @@ class PipelinedE2E:
         e0.record(self.h2d)
         for _ in range(steps):
             self.step()
-        e1.record(self.d2h if self.copy_back else self.comp)
+        e1.record(self.d2h if (self.copy_back or self.post is not None) else self.comp)
         torch.cuda.synchronize(self.device)
         return e0.elapsed_time(e1) / steps
 
@@ -368,12 +378,12 @@ def run_decode_ours(args, rank, world, device):
     # context lengths copied in from pinned memory every step, the output
     # (gathered from every rank at N > 1) copied back to rank 0's host
     def e2e_compute(qe, bte, ctxe):
-        o = PD.paged_attention_decode(qe, kc, vc, bte, ctxe, DEC["page"], DEC["page"])
-        return gather(o) if gather is not None else o
+        return PD.paged_attention_decode(qe, kc, vc, bte, ctxe, DEC["page"], DEC["page"])
 
+    # the gather runs on the copy-back stream, so step i's gather overlaps step i + 1's kernels
     n_all = sum(len(i) for i in ids)
     e2e = PipelinedE2E([q, bt, ctx], e2e_compute, [((n_all,) + tuple(q.shape[1:]), q.dtype)], device,
-                       copy_back=rank == 0)
+                       copy_back=rank == 0, post=gather)
     e2e_ms = e2e.timed(args.steps, args.warmup, world)
     h2d, d2h = e2e.h2d_bytes(), e2e.d2h_bytes()
 
@@ -432,8 +442,9 @@ def run_decode_ours(args, rank, world, device):
                 "note": "public paged_attention_decode() with q / block tables / context lengths copied from pinned "
                         "host memory and the output copied back every step, copies on two copy streams overlapping "
                         "the neighbouring steps' kernels (two buffer sets); the KV cache is resident"
-                        + ("; includes the NCCL all-gather of every rank's output and rank 0's copy of the whole "
-                           "result" if world > 1 else "")},
+                        + ("; includes the NCCL all-gather of every rank's output (on the copy-back stream, "
+                           "overlapping the next step's kernels) and rank 0's copy of the whole result"
+                           if world > 1 else "")},
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clk.summary(),
     }

@@ -368,6 +368,27 @@ def test_sparse_prefill_mla_shape(with_sink, kernel_path):
     close_lse(lse, ref_lse)
 
 
+@pytest.mark.parametrize("variant", ["576v512_shared", "576v576_shared", "576v576_sep", "576v512_sep",
+                                     "512v512_shared", "512v512_sep", "256v256_sep"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_sparse_prefill_tensor_core_variants(variant, dtype):
+    """Every K/V head-dim pairing the tensor-core sparse kernel takes --
+    V a prefix view of K (the MLA latent: 576/512, 512/512, and V = K itself
+    at 576, the call the reference's own shape rule k.shape == v.shape makes,
+    SA:279) and V a tensor of its own (576/576, 576/512, 512/512, 256/256) --
+    runs on the tcgen05 kernel (tak_last_kernel()) and matches the oracle.
+    Ragged -1 padding and a fully masked row; 64 heads on one KV head."""
+    dq, dv = (int(x) for x in variant.split("_")[0].split("v"))
+    shared = variant.endswith("shared")
+    H, Hkv = (64, 1) if dq >= 512 else (16, 2)
+    q, k, v, idx, sink = _sparse_case(20, H, Hkv, dq, dv, 900, 200, dtype, 27 + dq + dv, shared_latent=shared)
+    out, lse = SA.sparse_attn_prefill(q, k, v, idx, None, sink, return_lse=True)
+    assert T.last_kernel() == "sparse_tc"
+    ref, ref_lse = O.sparse_prefill(npy(q), npy(k), npy(v), idx.cpu(), None, sink.cpu())
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+
+
 def test_sparse_prefill_wide_index_rows():
     """The sparse bench's index width: 2048 sorted unique indices per token drawn causally
     from a 32768-row latent KV (MQA, 64 heads, 576/512), -1 padding for early
@@ -440,7 +461,7 @@ def _sparse_decode_case(ctx, H, Hkv, D, Dv, P, n_win, n_comp_slots, ncomp, dtype
     return q, kc, vc, ck, cv, bt.to(DEV), idx.to(DEV), cl.to(DEV), sink
 
 
-@pytest.mark.parametrize("shape", ["latent576", "latent512", "gqa128", "gqa64"])
+@pytest.mark.parametrize("shape", ["latent576", "latent512", "gqa128", "gqa64", "sep512", "latent576v576"])
 @pytest.mark.parametrize("with_sink", [False, True])
 def test_sparse_decode_paged_and_compressed(shape, with_sink, kernel_path):
     """Sparse decode over a paged window plus compressed rows: 64 heads sharing
@@ -448,7 +469,13 @@ def test_sparse_decode_paged_and_compressed(shape, with_sink, kernel_path):
     64-dim heads; ragged index rows (slot counts not a multiple of 64), empty
     and short contexts, and every masking case of the slot-position rule."""
     ctx = [0, 1, 5, 127, 128, 3 * 64 + 7, 9 * 64, 1000, 33, 2]
-    if shape.startswith("latent"):
+    if shape == "latent576v576":      # V = K itself (the reference's k.shape == v.shape call)
+        case = _sparse_decode_case(ctx, 64, 1, 576, 576, 64, 128, 200, 700, torch.bfloat16, 54, shared_latent=True)
+        n_win = 128
+    elif shape == "sep512":           # compressed K and V of their own (pooled separately)
+        case = _sparse_decode_case(ctx, 64, 1, 512, 512, 64, 128, 200, 700, torch.bfloat16, 55)
+        n_win = 128
+    elif shape.startswith("latent"):
         D = int(shape[6:])
         case = _sparse_decode_case(ctx, 64, 1, D, 512, 64, 128, 200, 700, torch.bfloat16, 51, shared_latent=True)
         n_win = 128
@@ -462,6 +489,8 @@ def test_sparse_decode_paged_and_compressed(shape, with_sink, kernel_path):
     P = kc.shape[2]
     s = sink if with_sink else None
     out, lse = SA.sparse_attn_decode(q, kc, vc, ck, cv, bt, idx, cl, n_win, P, s, return_lse=True)
+    if kernel_path == 0:
+        assert T.last_kernel() == "sparse_tc"
     ref, ref_lse = O.sparse_decode(npy(q), npy(kc), npy(vc), npy(ck), npy(cv), bt.cpu(), idx.cpu(), cl.cpu(),
                                    n_win, P, None if s is None else s.cpu())
     close(out, ref, TOL16)

@@ -20,25 +20,36 @@
 // head (MQA: all 64 heads of the token).  The 64 head rows are the MMA's
 // M = 64 dimension, so every gathered K/V row is read once for all heads.
 //
+// Tensor memory (M = 64 uses half of each 32-lane quadrant):
+//   lanes 0-15 of each quadrant: S (two 64-column buffers, columns 0-127) and
+//            Q as the QK MMA's A operand (columns 128 .. 128 + Dqk/2; the A
+//            operand and the accumulator of one MMA sit on the same lanes),
+//            plus O's columns past 512 for a 576-dim V;
+//   lanes 16-31: O (up to 512 fp32 columns).
+// Keeping Q out of shared memory leaves room for three gather stages of the
+// 576-dim latent rows (3 x 72 KB), so the gathers of two tiles are in flight
+// while the tensor core works on a third.
+//
 // Warp roles (288 threads):
-//   warps 4-7 gather producers: Q rows once (one TMA), then for each tile of
-//            64 indices, cp.async 16-byte copies of the gathered rows (8 lanes
-//            per 128-byte line, so every warp instruction moves 4 full lines)
-//            written straight into the 128-byte-swizzled layout the MMA reads,
-//            2-stage ring; masked rows are zero-filled; the next tile's
-//            indices are loaded while the current tile is in flight.
+//   warps 4-7 gather producers: Q rows once (one TMA, staged in the last K
+//            stage), then for each tile of 64 indices, cp.async 16-byte copies
+//            of the gathered rows (8 lanes per 128-byte line, so every warp
+//            instruction moves 4 full lines) written straight into the
+//            128-byte-swizzled layout the MMA reads; K and V have rings of
+//            their own unless V is a prefix view of K (then the K rows serve
+//            both); masked rows are zero-filled; the next tile's indices are
+//            loaded while the current tile is in flight.
 //   warp 8   TMEM allocator + single-thread tcgen05.mma issuer:
-//            S_j = Q K_j^T (M=64, N=64, K=16 x Dqk/16) into TMEM lanes 16-31
-//            of each quadrant (two buffers), O += P_j V_j (M=64, N<=256 per
-//            instruction, V from the same gathered rows when it is a view of
-//            K) into TMEM lanes 0-15.  Issue order is greedy: whichever of
-//            "QK of the next loaded tile" and "PV of the next softmaxed tile"
-//            is ready goes first.
-//   warps 0-3 softmax: TMEM loads of shape 16x32bx2 let all 32 threads of a
-//            warp work on its 16 head rows (two threads per row, 32 columns
-//            each); lazy rescaling of O (only when the max grows by > 2^8);
-//            P written to shared memory (K-major, swizzled) for the PV MMA;
-//            epilogue folds the sink, normalises and stores the rows.
+//            S_j = Q K_j^T (M=64, N=64, K=16 x Dqk/16, A from TMEM), O += P_j
+//            V_j (M=64, N<=256 per instruction, P from shared memory).  Issue
+//            order is greedy: whichever of "QK of the next loaded tile" and
+//            "PV of the next softmaxed tile" is ready goes first.
+//   warps 0-3 move Q from shared memory into TMEM once, then run the softmax:
+//            TMEM loads of shape 16x32bx2 let all 32 threads of a warp work
+//            on its 16 head rows (two threads per row, 32 columns each); lazy
+//            rescaling of O (only when the max grows by > 2^8); P written to
+//            shared memory (K-major, swizzled) for the PV MMA; epilogue folds
+//            the sink, normalises and stores the rows.
 #include <type_traits>
 
 #include "common.cuh"
@@ -121,19 +132,51 @@ __device__ __forceinline__ void tmem_st16x2(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 
+// 16 lanes x 16 columns per half-warp (the x16 form of tmem_st16x2): threads
+// 0-15 write columns [c, c+16) of lanes base+t, threads 16-31 columns
+// [c+16, c+32) of lanes base+t-16.
+__device__ __forceinline__ void tmem_st16x2_x16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], 16, {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// Shared-memory plan of one head-dim variant.  K stages hold DQK columns of
+// 64 gathered rows; V stages (only when V is not a prefix view of K) DV
+// columns.  Q (64 x DQK) is staged in the last K stage before it moves to
+// TMEM.  Stage counts are the most that fit next to P (at most 4).
 template <int DQK, int DV, bool SHARED>
 struct SpLayout {
   static constexpr int BLK = 64 * 128;  // 64 rows x 128 B: one 64-column block of a 64-row tile
   static constexpr int NQB = DQK / 64, NVB = DV / 64;
-  static constexpr int QOFF = 0;
-  static constexpr int STAGE = (NQB + (SHARED ? 0 : NVB)) * BLK;
-  static constexpr int KVOFF = NQB * BLK;
-  static constexpr int POFF = KVOFF + 2 * STAGE;
-  static constexpr int MASKOFF = POFF + BLK;
-  static constexpr int BAROFF = MASKOFF + 16;
-  static constexpr int NBAR = 10;
+  static constexpr int KST = NQB * BLK;
+  static constexpr int VST = SHARED ? 0 : NVB * BLK;
+  static constexpr int BUDGET = 232448 - 1024 - BLK - 512;  // opt-in maximum - alignment - P - barriers
+  static constexpr int NPAIR = BUDGET / (KST + VST) < 4 ? BUDGET / (KST + VST) : 4;
+  static constexpr int NSK = SHARED ? (BUDGET / KST < 4 ? BUDGET / KST : 4)
+                                    : (NPAIR >= 2 ? NPAIR : (2 * KST + VST <= BUDGET ? 2 : 1));
+  static constexpr int NSV = SHARED ? 0 : (NPAIR >= 2 ? NPAIR : 1);
+  static constexpr int KOFF = 0;
+  static constexpr int VOFF = KOFF + NSK * KST;
+  static constexpr int POFF = VOFF + NSV * VST;
+  static constexpr int BAROFF = POFF + BLK;
+  static constexpr int NBAR = 24;
   static constexpr int SMEM = BAROFF + NBAR * 8 + 16 + 1024;
-  static constexpr int TMEM_COLS = DV <= 128 ? 128 : (DV <= 256 ? 256 : 512);
+  // TMEM columns: S [0, 128) and Q [128, 128 + DQK/2) on lanes 0-15, then O's
+  // columns past 512 (576-dim V); O [0, min(DV, 512)) on lanes 16-31
+  static constexpr int QCOL = 128;
+  static constexpr int OMAIN = DV < 512 ? DV : 512;
+  static constexpr int OTAIL = DV - OMAIN;
+  static constexpr int TCOL = QCOL + DQK / 2;
+  static_assert(TCOL + OTAIL <= 512, "TMEM columns");
+  static constexpr int TMEM_NEED = (TCOL + OTAIL) > OMAIN ? (TCOL + OTAIL) : OMAIN;
+  static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;  // a power of two
+  static_assert(SMEM <= 232448, "shared memory");
+  static_assert(NSK >= 1 && (SHARED || NSV >= 1), "stages");
+  static_assert(OTAIL == 0 || OTAIL == 64, "a V wider than 512 columns has one 64-column tail");
 };
 
 template <typename T, int DQK, int DV, bool SHARED, bool DECODE>
@@ -142,18 +185,24 @@ __global__ void __launch_bounds__(288, 1)
   using L = SpLayout<DQK, DV, SHARED>;
   constexpr int BN = 64;
   constexpr int NPROD = 128;  // producer threads
+  constexpr int NSK = L::NSK, NSV = L::NSV;
+  constexpr int NSVd = SHARED ? 1 : NSV;  // V ring size as a divisor (unused when V is K's rows)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAROFF);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* p_full = bars + 7;
-  uint64_t* p_free = bars + 8;
-  uint64_t* o_done = bars + 9;
+  uint64_t* q_full = bars + 0;   // Q landed in its staging stage
+  uint64_t* q_tmem = bars + 1;   // Q copied into TMEM (staging stage free)
+  uint64_t* k_full = bars + 2;   // [4]
+  uint64_t* k_empty = bars + 6;  // [4]
+  uint64_t* v_full = bars + 10;  // [4]
+  uint64_t* v_empty = bars + 14; // [4]
+  uint64_t* s_full = bars + 18;  // [2]
+  uint64_t* p_full = bars + 20;
+  uint64_t* p_free = bars + 21;
+  uint64_t* o_done = bars + 22;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  uint8_t* const qstage = smem + L::KOFF + (NSK - 1) * L::KST;
 
   const int t = blockIdx.x;
   const int kvh = blockIdx.y / p.head_chunks;
@@ -168,11 +217,16 @@ __global__ void __launch_bounds__(288, 1)
 
   if (tid == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], NPROD);
-      mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
+    mbar_init(q_tmem, 128);
+    for (int i = 0; i < NSK; ++i) {
+      mbar_init(&k_full[i], NPROD);
+      mbar_init(&k_empty[i], 1);
     }
+    for (int i = 0; i < NSV; ++i) {
+      mbar_init(&v_full[i], NPROD);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) mbar_init(&s_full[i], 1);
     mbar_init(p_full, 128);
     mbar_init(p_free, 1);
     mbar_init(o_done, 1);
@@ -197,8 +251,7 @@ __global__ void __launch_bounds__(288, 1)
       tma_prefetch_desc(&tmQ);
       mbar_arrive_expect_tx(q_full, L::NQB * L::BLK);
 #pragma unroll 1
-      for (int cb = 0; cb < L::NQB; ++cb)
-        tma_load_2d(smem + L::QOFF + cb * L::BLK, &tmQ, q_full, cb * 64, t * p.H + h0);
+      for (int cb = 0; cb < L::NQB; ++cb) tma_load_2d(qstage + cb * L::BLK, &tmQ, q_full, cb * 64, t * p.H + h0);
     }
     const T* kb = reinterpret_cast<const T*>(p.k);
     const T* vb = reinterpret_cast<const T*>(p.v);
@@ -231,89 +284,118 @@ __global__ void __launch_bounds__(288, 1)
     const T* vcur[4];
     const T* vnxt[4];
     load_rows(0, cur, vcur);
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
-      load_rows(j + 1, nxt, vnxt);  // in flight while this tile's stage frees up
-      if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1)) {
-        *abort_flag = 1;
-        break;
-      }
-      uint8_t* kst = smem + L::KVOFF + st * L::STAGE;
+    bool ok = true;
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      load_rows(j + 1, nxt, vnxt);  // in flight while this tile's stages free up
+      // ---- K rows of tile j ----
+      const int sk = j % NSK;
+      if (j >= NSK) ok = mbar_wait(&k_empty[sk], ((j / NSK) - 1) & 1);
+      else if (sk == NSK - 1) ok = mbar_wait(q_tmem, 0);  // the Q staging area is free
+      if (!ok) break;
+      uint8_t* kst = smem + L::KOFF + sk * L::KST;
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         const int row = g * 16 + rsub;
-        const bool ok = cur[g] != nullptr;
+        const bool valid = cur[g] != nullptr;
         // masked rows: a zero-byte copy (zero fill) from an in-bounds address
-        const T* src = (ok ? cur[g] : kb) + chunk * 8;
+        const T* src = (valid ? cur[g] : kb) + chunk * 8;
         const uint32_t dst_off = row * 128 + ((chunk ^ (row & 7)) << 4);
 #pragma unroll
-        for (int cb = 0; cb < L::NQB; ++cb) cp_async_16(kst + cb * L::BLK + dst_off, src + cb * 64, ok);
-        if (!SHARED) {
-          const T* vsrc = (ok ? vcur[g] : vb) + chunk * 8;
-#pragma unroll
-          for (int cb = 0; cb < L::NVB; ++cb)
-            cp_async_16(kst + (L::NQB + cb) * L::BLK + dst_off, vsrc + cb * 64, ok);
-        }
+        for (int cb = 0; cb < L::NQB; ++cb) cp_async_16(kst + cb * L::BLK + dst_off, src + cb * 64, valid);
       }
-      cp_async_mbar_arrive(&kv_full[st]);
+      cp_async_mbar_arrive(&k_full[sk]);
+      if constexpr (!SHARED) {
+        // ---- V rows of tile j ----
+        const int sv = j % NSV;
+        if (j >= NSV && !(ok = mbar_wait(&v_empty[sv], ((j / NSV) - 1) & 1))) break;
+        uint8_t* vst = smem + L::VOFF + sv * L::VST;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int row = g * 16 + rsub;
+          const bool valid = vcur[g] != nullptr;
+          const T* src = (valid ? vcur[g] : vb) + chunk * 8;
+          const uint32_t dst_off = row * 128 + ((chunk ^ (row & 7)) << 4);
+#pragma unroll
+          for (int cb = 0; cb < L::NVB; ++cb) cp_async_16(vst + cb * L::BLK + dst_off, src + cb * 64, valid);
+        }
+        cp_async_mbar_arrive(&v_full[sv]);
+      }
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         cur[g] = nxt[g];
         vcur[g] = vnxt[g];
       }
     }
+    if (!ok) *abort_flag = 1;
     cp_async_wait_all();
   } else if (warp == 8) {
     // ---------------- MMA issuer (greedy order) ----------------
     if (lane == 0 && n_tiles > 0) {
       constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-      constexpr int NPV = DV < 256 ? DV : 256;
+      constexpr int NPV = L::OMAIN < 256 ? L::OMAIN : 256;
       const uint32_t idesc_qk = tc_idesc_f16(AB, 64, BN, 0);
       const uint32_t idesc_pv = tc_idesc_f16(AB, 64, NPV, 1);
+      const uint32_t idesc_tail = tc_idesc_f16(AB, 64, 64, 1);
       // descriptors built once, advanced per k-step by constant offsets (see prefill_tc.cu)
-      const uint64_t q_desc = tc_sdesc_sw128(sbase + L::QOFF, 16, 1024);
-      const uint64_t k_desc0 = tc_sdesc_sw128(sbase + L::KVOFF, 16, 1024);
-      const uint64_t v_desc0 = tc_sdesc_sw128(sbase + L::KVOFF + (SHARED ? 0 : L::NQB * L::BLK), L::BLK, 1024);
-      constexpr uint64_t kStageStep = static_cast<uint64_t>(L::STAGE >> 4);
+      const uint64_t k_desc0 = tc_sdesc_sw128(sbase + L::KOFF, 16, 1024);
+      const uint64_t v_desc0 =
+          SHARED ? tc_sdesc_sw128(sbase + L::KOFF, L::BLK, 1024) : tc_sdesc_sw128(sbase + L::VOFF, L::BLK, 1024);
+      constexpr uint64_t kKStep = static_cast<uint64_t>(L::KST >> 4);
+      constexpr uint64_t kVStep = static_cast<uint64_t>((SHARED ? L::KST : L::VST) >> 4);
       const uint64_t p_desc = tc_sdesc_sw128(sbase + L::POFF, 16, 1024);
-      bool ok = mbar_wait(q_full, 0);
+      const uint32_t q_tmem_addr = taddr + L::QCOL;          // lanes 0-15
+      const uint32_t o_main = taddr + (16u << 16);           // lanes 16-31
+      const uint32_t o_tail = taddr + L::TCOL;               // lanes 0-15
+      bool ok = mbar_wait(q_tmem, 0);
       int nq = 0, np = 0;  // next QK / PV to issue
       const uint64_t t0 = globaltimer();
       uint32_t spins = 0;
       while (ok && np < n_tiles) {
         bool did = false;
-        // QK of tile nq: its stage must be loaded and its S buffer consumed (nq <= np + 1)
-        if (nq < n_tiles && nq <= np + 1 && mbar_try_wait(smem_u32(&kv_full[nq & 1]), (nq >> 1) & 1)) {
+        // QK of tile nq: its K stage must be loaded and its S buffer consumed (nq <= np + 1)
+        if (nq < n_tiles && nq <= np + 1 && mbar_try_wait(smem_u32(&k_full[nq % NSK]), (nq / NSK) & 1)) {
           fence_proxy_async_smem();
           tc_fence_after();
-          const int st = nq & 1;
-          const uint32_t d_tmem = taddr + (16u << 16) + st * 64;
-          const uint64_t kd = k_desc0 + (st ? kStageStep : 0);
+          const int sk = nq % NSK;
+          const uint32_t d_tmem = taddr + (nq & 1) * 64;
+          const uint64_t kd = k_desc0 + sk * kKStep;
 #pragma unroll
           for (int kk = 0; kk < DQK / 16; ++kk) {
             const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * L::BLK + (kk & 3) * 32) >> 4);
-            tc_mma_ss(d_tmem, q_desc + koff, kd + koff, idesc_qk, kk > 0 ? 1u : 0u);
+            tc_mma_ts(d_tmem, q_tmem_addr + kk * 8, kd + koff, idesc_qk, kk > 0 ? 1u : 0u);
           }
-          tc_commit(&s_full[st]);
+          tc_commit(&s_full[nq & 1]);
+          if (!SHARED) tc_commit(&k_empty[sk]);  // K rows are done once S is computed
           ++nq;
           did = true;
         }
-        // PV of tile np once its P is in shared memory
-        if (np < nq && mbar_try_wait(smem_u32(p_full), np & 1)) {
+        // PV of tile np once its P is in shared memory (and, unshared, its V rows loaded)
+        if (np < nq && mbar_try_wait(smem_u32(p_full), np & 1) &&
+            (SHARED || mbar_try_wait(smem_u32(&v_full[np % NSVd]), (np / NSVd) & 1))) {
+          if (!SHARED) fence_proxy_async_smem();
           tc_fence_after();
-          const int st = np & 1;
-          const uint64_t vd = v_desc0 + (st ? kStageStep : 0);
+          const int sv = SHARED ? np % NSK : np % NSVd;
+          const uint64_t vd = v_desc0 + sv * kVStep;
 #pragma unroll
-          for (int half = 0; half < (DV + 255) / 256; ++half) {
+          for (int half = 0; half < (L::OMAIN + 255) / 256; ++half) {
 #pragma unroll
             for (int kk = 0; kk < BN / 16; ++kk) {
               const uint64_t a = p_desc + static_cast<uint64_t>((kk * 32) >> 4);
               const uint64_t b = vd + static_cast<uint64_t>((half * 4 * L::BLK + kk * 2048) >> 4);
-              tc_mma_ss(taddr + half * 256, a, b, idesc_pv, (np > 0 || kk > 0) ? 1u : 0u);
+              tc_mma_ss(o_main + half * 256, a, b, idesc_pv, (np > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          if constexpr (L::OTAIL > 0) {
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              const uint64_t a = p_desc + static_cast<uint64_t>((kk * 32) >> 4);
+              const uint64_t b = vd + static_cast<uint64_t>((8 * L::BLK + kk * 2048) >> 4);
+              tc_mma_ss(o_tail, a, b, idesc_tail, (np > 0 || kk > 0) ? 1u : 0u);
             }
           }
           tc_commit(o_done);
-          tc_commit(&kv_empty[st]);
+          if (SHARED) tc_commit(&k_empty[sv]);
+          else tc_commit(&v_empty[sv]);
           tc_commit(p_free);
           ++np;
           did = true;
@@ -328,17 +410,54 @@ __global__ void __launch_bounds__(288, 1)
       if (!ok) *abort_flag = 1;
     }
   } else {
-    // ---------------- softmax + epilogue: warps 0-3, 16 head rows per warp ----------------
+    // ---------------- Q into TMEM, softmax + epilogue: warps 0-3, 16 head rows per warp ----------------
     const int t16 = lane & 15, hi = lane >> 4;
     const int row = 16 * warp + t16;
     const bool row_ok = row < nrows;
     const int head = h0 + row;
     const bool has_sink = p.sink != nullptr;
     const float sink_log2 = (has_sink && row_ok) ? p.sink[head] * kLog2e : -INFINITY;
-    const uint32_t s_lane = static_cast<uint32_t>(32 * warp + 16) << 16;
-    const uint32_t o_lane = static_cast<uint32_t>(32 * warp) << 16;
+    const uint32_t s_lane = static_cast<uint32_t>(32 * warp) << 16;       // S, Q, O tail: lanes 0-15
+    const uint32_t o_lane = static_cast<uint32_t>(32 * warp + 16) << 16;  // O: lanes 16-31
+    bool ok = mbar_wait(q_full, 0);
+    if (ok) {
+      // Q row `row`, 128-byte swizzled boxes of 64 columns -> TMEM columns
+      // QCOL + k/2 (two 16-bit elements per column): per instruction, threads
+      // 0-15 take box 2i and threads 16-31 box 2i + 1 of their rows
+      const uint8_t* qrow = qstage + row * 128;
+#pragma unroll 1
+      for (int i = 0; i < L::NQB / 2; ++i) {
+        uint32_t r[32];
+        const uint8_t* box = qrow + (2 * i + hi) * L::BLK;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 u = *reinterpret_cast<const uint4*>(box + ((c ^ (row & 7)) << 4));
+          r[4 * c] = u.x;
+          r[4 * c + 1] = u.y;
+          r[4 * c + 2] = u.z;
+          r[4 * c + 3] = u.w;
+        }
+        tmem_st16x2(taddr + s_lane + L::QCOL + 64 * i, r);
+      }
+      if constexpr (L::NQB % 2) {
+        // the odd last box: threads 0-15 its first 32 elements, threads 16-31 the rest
+        uint32_t r[16];
+        const uint8_t* box = qrow + (L::NQB - 1) * L::BLK;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 u = *reinterpret_cast<const uint4*>(box + (((4 * hi + c) ^ (row & 7)) << 4));
+          r[4 * c] = u.x;
+          r[4 * c + 1] = u.y;
+          r[4 * c + 2] = u.z;
+          r[4 * c + 3] = u.w;
+        }
+        tmem_st16x2_x16(taddr + s_lane + L::QCOL + 32 * (L::NQB - 1), r);
+      }
+      tmem_st_wait();
+    }
+    tc_fence_before();
+    mbar_arrive(q_tmem);
     float m_run = -INFINITY, m_used = -INFINITY, l = 0.f;
-    bool ok = true;
     auto tile_mask = [&](int j) -> uint32_t {
       // validity of this thread's 32 columns of tile j (lane l: columns l and l+32)
       const int c0 = j * BN + lane, c1 = c0 + 32;
@@ -350,8 +469,12 @@ __global__ void __launch_bounds__(288, 1)
           __ballot_sync(0xffffffffu, c1 < p.k_topk && sp_slot_valid<DECODE>(p, c1, r1, ctx, bt_row));
       return hi ? hi_m : lo;
     };
-    uint32_t vnext = n_tiles > 0 ? tile_mask(0) : 0u;
-    for (int j = 0; j < n_tiles; ++j) {
+    // O columns [c*64, c*64 + 64) of this warp's rows: lanes 16-31 below 512, the tail on lanes 0-15
+    auto o_addr = [&](int c) -> uint32_t {
+      return c * 64 < L::OMAIN ? taddr + o_lane + c * 64 : taddr + s_lane + L::TCOL + (c * 64 - L::OMAIN);
+    };
+    uint32_t vnext = (ok && n_tiles > 0) ? tile_mask(0) : 0u;
+    for (int j = 0; ok && j < n_tiles; ++j) {
       const int b = j & 1;
       const uint32_t vbits = vnext;
       if (j + 1 < n_tiles) vnext = tile_mask(j + 1);
@@ -389,11 +512,11 @@ __global__ void __launch_bounds__(288, 1)
         uint32_t orow[32];
 #pragma unroll 1
         for (int c = 0; c < DV / 64; ++c) {
-          tmem_ld16x2(taddr + o_lane + c * 64, orow);
+          tmem_ld16x2(o_addr(c), orow);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * f);
-          tmem_st16x2(taddr + o_lane + c * 64, orow);
+          tmem_st16x2(o_addr(c), orow);
         }
         tmem_st_wait();
         l *= f;
@@ -454,7 +577,7 @@ __global__ void __launch_bounds__(288, 1)
     for (int c = 0; c < DV / 64; ++c) {
       uint32_t o[32];
       if (n_tiles > 0) {
-        tmem_ld16x2(taddr + o_lane + c * 64, o);
+        tmem_ld16x2(o_addr(c), o);
         tmem_ld_wait();
       } else {
 #pragma unroll
@@ -576,6 +699,22 @@ static bool same_view(const void* a, const int64_t* sa, const void* b, const int
   return true;
 }
 
+// Head-dim variants on the tensor cores; -1 = no variant (generic kernel).
+// shared: V is a prefix view of K (its rows come from the same gathers).
+template <typename T>
+static int route_sparse_tc(const SparseArgs& a, cudaStream_t st, bool shared, int dq, int dv) {
+  if (dq == 576 && dv == 512) return shared ? launch_sparse_tc<T, 576, 512, true>(a, st)
+                                            : launch_sparse_tc<T, 576, 512, false>(a, st);
+  if (dq == 576 && dv == 576) return shared ? launch_sparse_tc<T, 576, 576, true>(a, st)
+                                            : launch_sparse_tc<T, 576, 576, false>(a, st);
+  if (dq == 512 && dv == 512) return shared ? launch_sparse_tc<T, 512, 512, true>(a, st)
+                                            : launch_sparse_tc<T, 512, 512, false>(a, st);
+  if (dq == dv && dq == 256) return launch_sparse_tc<T, 256, 256, false>(a, st);
+  if (dq == dv && dq == 128) return launch_sparse_tc<T, 128, 128, false>(a, st);
+  if (dq == dv && dq == 64) return launch_sparse_tc<T, 64, 64, false>(a, st);
+  return -1;
+}
+
 int sparse_tc_launch(const SparseArgs& a, cudaStream_t st, bool* handled) {
   *handled = false;
   if (a.dtype == kF32) return 0;
@@ -602,19 +741,8 @@ int sparse_tc_launch(const SparseArgs& a, cudaStream_t st, bool* handled) {
   if (a.so[2] != 1 || (a.so[0] % 8) || (a.so[1] % 8) || (reinterpret_cast<uintptr_t>(a.out) & 15)) return 0;
   const int dq = a.head_dim, dv = a.head_dim_v;
   int r = -1;
-  if (a.dtype == kBF16) {
-    if (shared && dq == 576 && dv == 512) r = launch_sparse_tc<__nv_bfloat16, 576, 512, true>(a, st);
-    else if (shared && dq == 512 && dv == 512) r = launch_sparse_tc<__nv_bfloat16, 512, 512, true>(a, st);
-    else if (dq == 128 && dv == 128) r = launch_sparse_tc<__nv_bfloat16, 128, 128, false>(a, st);
-    else if (dq == 64 && dv == 64) r = launch_sparse_tc<__nv_bfloat16, 64, 64, false>(a, st);
-    else if (dq == 256 && dv == 256) r = launch_sparse_tc<__nv_bfloat16, 256, 256, false>(a, st);
-  } else {
-    if (shared && dq == 576 && dv == 512) r = launch_sparse_tc<__half, 576, 512, true>(a, st);
-    else if (shared && dq == 512 && dv == 512) r = launch_sparse_tc<__half, 512, 512, true>(a, st);
-    else if (dq == 128 && dv == 128) r = launch_sparse_tc<__half, 128, 128, false>(a, st);
-    else if (dq == 64 && dv == 64) r = launch_sparse_tc<__half, 64, 64, false>(a, st);
-    else if (dq == 256 && dv == 256) r = launch_sparse_tc<__half, 256, 256, false>(a, st);
-  }
+  if (a.dtype == kBF16) r = route_sparse_tc<__nv_bfloat16>(a, st, shared, dq, dv);
+  else r = route_sparse_tc<__half>(a, st, shared, dq, dv);
   if (r < 0) return 0;
   *handled = true;
   return r;
