@@ -798,8 +798,8 @@ class CsaWL(Workload):
         self.launches = 5
         self.config = {"tokens": T, "indices_per_query": self.n_win + self.top_k, "valid_indices": n_idx,
                        "l2_policy": "q (4.3 GB) and outputs stream; the 1.3 MB latent per sequence is L2-resident",
-                       "timed_path": "csa_prefill_forward(): compression, window rows, Lightning indexer, "
-                                     "concatenation and sparse attention, every step"}
+                       "timed_path": "csa_prefill_forward(): compression, window rows, Lightning indexer and "
+                                     "sparse attention over the latent and compressed rows in place, every step"}
 
     def step(self):
         return self.CSA.csa_prefill_forward(self.q, self.kv, self.kv, self.cu_h, self.n_win, self.top_k, self.m,
@@ -815,12 +815,11 @@ class CsaWL(Workload):
         ev[1].record()
         idx = CSA.build_csa_topk_idxs(self.q, ck, self.cu_h, offs, self.n_win, self.top_k, self.m)
         ev[2].record()
-        kf = torch.cat([self.kv, ck], 0)
-        CSA.sparse_attn_prefill(self.q, kf, kf, idx, self.cu_h.to(device), attn_sink=self.sink)
+        CSA.sparse_attn_prefill_two_sources(self.q, self.kv, self.kv, ck, ck, idx, attn_sink=self.sink)
         ev[3].record()
         torch.cuda.synchronize(device)
         return {"compress_ms": round(ev[0].elapsed_time(ev[1]), 3), "index_ms": round(ev[1].elapsed_time(ev[2]), 3),
-                "concat_attention_ms": round(ev[2].elapsed_time(ev[3]), 3)}
+                "attention_ms": round(ev[2].elapsed_time(ev[3]), 3)}
 
     def e2e_setup(self):
         self.hq, self.hkv, self.hg = (t.cpu().pin_memory() for t in (self.q, self.kv, self.gate))

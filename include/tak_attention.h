@@ -147,6 +147,26 @@ int tak_sparse_attn_prefill(const void* q, const int64_t* q_strides, const void*
                             int64_t k_topk, float scale, int dtype, void* stream);
 
 /*
+ * Sparse prefill over two row sources without concatenating them: index j <
+ * kv_rows addresses row j of k/v [kv_rows, H_kv, D(v)], index j >= kv_rows
+ * row j - kv_rows of k2/v2 [kv2_rows, H_kv, D(v)] (same head dims and
+ * head-dim strides); every other argument as tak_sparse_attn_prefill.
+ * Replaces the torch.cat([k, compressed_k]) / torch.cat([v, compressed_v])
+ * and the sparse_attn_prefill call of csa_prefill_forward
+ * (attention/csa.py:191-194) and hca_prefill_forward (attention/hca.py:173-176),
+ * whose index rows address the concatenation (entries total_tokens +
+ * comp_offsets[s] + i).  v/v2 being prefix views of k/k2 (one latent tensor
+ * as K and V) lets each gathered row serve both.
+ */
+int tak_sparse_attn_prefill_2src(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                 const void* v, const int64_t* v_strides, int64_t kv_rows, const void* k2,
+                                 const int64_t* k2_strides, const void* v2, const int64_t* v2_strides,
+                                 int64_t kv2_rows, const int32_t* topk_idxs, const int64_t* topk_strides,
+                                 const float* attn_sink, void* out, const int64_t* out_strides, float* lse,
+                                 int64_t total_tokens, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                 int64_t head_dim_v, int64_t k_topk, float scale, int dtype, void* stream);
+
+/*
  * Top-k sparse decode over a paged window plus compressed rows.  Replaces
  * sparse_attn_decode(q, k_cache, v_cache, compressed_k, compressed_v,
  * block_tables, topk_idxs, context_lens, num_win, block_size, attn_sink) of

@@ -389,6 +389,53 @@ def test_sparse_prefill_tensor_core_variants(variant, dtype):
     close_lse(lse, ref_lse)
 
 
+@pytest.mark.parametrize("variant", ["latent576", "sep512", "gqa128"])
+def test_sparse_prefill_two_sources(variant, kernel_path):
+    """Attention over [K | compressed K] read in place from the two tensors
+    (the CSA / HCA forwards' layout, CSA:191-192) equals attention over their
+    concatenation: indices on both sides of the boundary, -1 and indices past
+    both sources."""
+    if variant == "latent576":
+        H, Hkv, D, Dv, shared = 64, 1, 576, 512, True
+    elif variant == "sep512":
+        H, Hkv, D, Dv, shared = 64, 1, 512, 512, False
+    else:
+        H, Hkv, D, Dv, shared = 16, 2, 128, 128, False
+    rows1, rows2 = 700, 300
+    q, k, v, idx, sink = _sparse_case(18, H, Hkv, D, Dv, rows1 + rows2, 160, torch.bfloat16, 61, shared_latent=shared)
+    idx[4, 7] = rows1 + rows2 + 5     # past both sources: masked
+    k1, k2 = k[:rows1], k[rows1:].clone()
+    if shared:
+        v1, v2 = k1[..., :Dv], k2[..., :Dv]
+    else:
+        v1, v2 = v[:rows1], v[rows1:].clone()
+    out, lse = SA.sparse_attn_prefill_two_sources(q, k1, v1, k2, v2, idx, sink, return_lse=True)
+    if kernel_path == 0:
+        assert T.last_kernel() == "sparse_tc"
+    vfull = torch.cat([v1, v2], 0)
+    ref, ref_lse = O.sparse_prefill(npy(q), npy(torch.cat([k1, k2], 0)), npy(vfull), idx.cpu(), None, sink.cpu())
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+
+
+def test_csa_forward_separate_v_on_tensor_cores():
+    """csa_prefill_forward with K and V of their own (512-dim, 64 heads): the
+    attention over [K | compressed K] and [V | compressed V] runs on the
+    tensor-core kernel and matches the oracle's forward."""
+    lens = [300, 700]
+    Tn = sum(lens)
+    g = torch.Generator().manual_seed(62)
+    q = torch.randn(Tn, 64, 512, generator=g).to(DEV, torch.bfloat16)
+    k = torch.randn(Tn, 1, 512, generator=g).to(DEV, torch.bfloat16)
+    v = torch.randn(Tn, 1, 512, generator=g).to(DEV, torch.bfloat16)
+    sink = torch.randn(64, generator=g).to(DEV)
+    cuq = _cu_t(lens)
+    out = CSA.csa_prefill_forward(q, k, v, cuq, 64, 32, 4, sink)
+    assert T.last_kernel() == "sparse_tc"
+    ref, _, _ = O.csa_prefill_forward(npy(q), npy(k), npy(v), cuq.cpu(), 64, 32, 4, sink.cpu(), "bfloat16")
+    close(out, ref, TOL16)
+
+
 def test_sparse_prefill_wide_index_rows():
     """The sparse bench's index width: 2048 sorted unique indices per token drawn causally
     from a 32768-row latent KV (MQA, 64 heads, 576/512), -1 padding for early

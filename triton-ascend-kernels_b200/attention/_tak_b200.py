@@ -37,6 +37,8 @@ _SIGS = {
                                                    _I64, _I64, _I64, _I64, _I64, _F32, _I32, _I32, _P], _I32),
     "tak_sparse_attn_prefill": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                  _I64, _I64, _F32, _I32, _P], _I32),
+    "tak_sparse_attn_prefill_2src": ([_P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _P,
+                                      _I64, _I64, _I64, _I64, _I64, _I64, _F32, _I32, _P], _I32),
     "tak_sparse_attn_decode": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64,
                                 _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F32, _I32, _P], _I32),
     "tak_build_token_to_seq": ([_P, _I64, _I64, _P, _P], _I32),

@@ -13,7 +13,7 @@ here ties go to the lower slot and masked picks come in ascending slot order.
 """
 
 import _tak_b200 as _t
-from sparse_attn_fwd import sparse_attn_prefill, sparse_attn_decode
+from sparse_attn_fwd import sparse_attn_prefill, sparse_attn_prefill_two_sources, sparse_attn_decode
 
 torch = _t.torch
 
@@ -79,11 +79,13 @@ def csa_prefill_forward(q, k, v, cu_seqlens, n_win, top_k, m, attn_sink=None, *,
     topk_idxs with the Lightning indexer, sparse attention over [K | compressed K]."""
     compressed_k, compressed_v, comp_offsets = compress_kv_overlap(k, v, cu_seqlens, m, gate=gate)
     topk_idxs = build_csa_topk_idxs(q, compressed_k, cu_seqlens, comp_offsets, n_win, top_k, m)
-    k_full = torch.cat([k, compressed_k], dim=0)
-    # one latent tensor as both K and V (MLA): its compressed K and V are equal,
-    # so the attention reads one [K | compressed] tensor as both
-    v_full = k_full if v is k else torch.cat([v, compressed_v], dim=0)
-    return sparse_attn_prefill(q, k_full, v_full, topk_idxs, cu_seqlens, attn_sink=attn_sink, return_lse=return_lse)
+    # the index rows address [K | compressed K] (CSA:191-192); the attention reads
+    # both sources in place instead of concatenating them.  One latent tensor
+    # as K and V (MLA): its compressed K and V are equal, so each gathered row
+    # serves both.
+    v2 = compressed_k if v is k else compressed_v
+    return sparse_attn_prefill_two_sources(q, k, v, compressed_k, v2, topk_idxs, attn_sink=attn_sink,
+                                           return_lse=return_lse)
 
 
 def csa_decode_forward(q, k_cache, v_cache, block_tables, context_lens,

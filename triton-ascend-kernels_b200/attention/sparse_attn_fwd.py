@@ -72,6 +72,32 @@ def sparse_attn_prefill(q, k, v, topk_idxs, cu_seqlens, attn_sink=None, *, retur
     return (out, lse) if return_lse else out
 
 
+def sparse_attn_prefill_two_sources(q, k, v, k2, v2, topk_idxs, attn_sink=None, *, return_lse=False):
+    """sparse_attn_prefill over the rows of k/v followed by the rows of k2/v2,
+    without building their concatenation (an addition used by the CSA / HCA
+    forwards, whose index rows address [K | compressed K], CSA:191-194).
+    Index j < k.shape[0] is row j of k/v, index j >= k.shape[0] row
+    j - k.shape[0] of k2/v2; -1 and indices past both are masked."""
+    _t.require_cuda(q, k, v, k2, v2)
+    total_tokens, num_q_heads, head_dim = q.shape
+    num_kv_heads = k.shape[1]
+    assert num_q_heads % num_kv_heads == 0
+    assert k.shape[1:] == k2.shape[1:] and v.shape[1:] == v2.shape[1:] and k.shape[:2] == v.shape[:2]
+    assert k2.shape[0] == v2.shape[0] and topk_idxs.shape[0] == total_tokens
+    idx = _t.as_i32(topk_idxs, q.device)
+    sink = _sink_arg(attn_sink, num_q_heads, q.device)
+    head_dim_v = v.shape[2]
+    out = q.new_empty((total_tokens, num_q_heads, head_dim_v))
+    lse = q.new_empty((total_tokens, num_q_heads), dtype=torch.float32) if return_lse else None
+    if total_tokens:
+        _t.check(_t.lib().tak_sparse_attn_prefill_2src(
+            _t.ptr(q), _t.strides(q), _t.ptr(k), _t.strides(k), _t.ptr(v), _t.strides(v), k.shape[0], _t.ptr(k2),
+            _t.strides(k2), _t.ptr(v2), _t.strides(v2), k2.shape[0], _t.ptr(idx), _t.strides(idx), _t.ptr(sink),
+            _t.ptr(out), _t.strides(out), _t.ptr(lse), total_tokens, num_q_heads, num_kv_heads, head_dim, head_dim_v,
+            idx.shape[1], 1.0 / math.sqrt(head_dim), _t.dtype_code(q), _t.stream_of(q)))
+    return (out, lse) if return_lse else out
+
+
 def sparse_attn_decode(q, k_cache, v_cache, compressed_k, compressed_v,
                        block_tables, topk_idxs, context_lens,
                        num_win, block_size=16, attn_sink=None, *, return_lse=False):

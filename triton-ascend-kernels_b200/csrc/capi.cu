@@ -316,9 +316,42 @@ int tak_sparse_attn_prefill(const void* q, const int64_t* q_strides, const void*
   a.k = k; copy_strides(a.sk, k_strides, 3);
   a.v = v; copy_strides(a.sv, v_strides, 3);
   a.kv_rows = kv_rows;
+  a.rows1 = kv_rows;
   a.decode = 0;
   r = sparse_launch(a, static_cast<cudaStream_t>(stream));
   return r ? r : check_launch("sparse prefill");
+}
+
+int tak_sparse_attn_prefill_2src(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                 const void* v, const int64_t* v_strides, int64_t kv_rows, const void* k2,
+                                 const int64_t* k2_strides, const void* v2, const int64_t* v2_strides,
+                                 int64_t kv2_rows, const int32_t* topk_idxs, const int64_t* topk_strides,
+                                 const float* attn_sink, void* out, const int64_t* out_strides, float* lse,
+                                 int64_t total_tokens, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                 int64_t head_dim_v, int64_t k_topk, float scale, int dtype, void* stream) {
+  TAK_ENTRY();
+  if (total_tokens == 0) return 0;
+  SparseArgs a{};
+  int r = fill_sparse_common(a, q, q_strides, topk_idxs, topk_strides, attn_sink, out, out_strides, lse,
+                             total_tokens, num_q_heads, num_kv_heads, head_dim, head_dim_v, k_topk, scale, dtype);
+  if (r) return r;
+  TAK_REQUIRE(kv_rows >= 0 && kv2_rows >= 0, "sparse prefill (two sources): negative row counts");
+  TAK_REQUIRE(k && v && k_strides && v_strides, "sparse prefill (two sources): null k/v");
+  TAK_REQUIRE(kv2_rows == 0 || (k2 && v2 && k2_strides && v2_strides),
+              "sparse prefill (two sources): null second k/v");
+  a.k = k; copy_strides(a.sk, k_strides, 3);
+  a.v = v; copy_strides(a.sv, v_strides, 3);
+  if (kv2_rows > 0) {
+    a.ck = k2; copy_strides(a.sck, k2_strides, 3);
+    a.cv = v2; copy_strides(a.scv, v2_strides, 3);
+    if (a.sck[2] != a.sk[2] || a.scv[2] != a.sv[2])
+      return set_error(2, "sparse prefill (two sources): the two sources need the same head-dim stride");
+  }
+  a.kv_rows = kv_rows + kv2_rows;
+  a.rows1 = kv_rows;
+  a.decode = 0;
+  r = sparse_launch(a, static_cast<cudaStream_t>(stream));
+  return r ? r : check_launch("sparse prefill (two sources)");
 }
 
 int tak_sparse_attn_decode(const void* q, const int64_t* q_strides, const void* k_cache, const int64_t* k_strides,

@@ -34,18 +34,27 @@ struct DenseRows {
 };
 
 // Row source for sparse prefill: rows topk[i] of flat K/V, -1 (or out of
-// range) masked (SA:55-57).
+// range) masked (SA:55-57); rows from rows1 on come from a second source
+// (compressed rows appended after the K/V rows).
 template <typename T>
 struct TopkRows {
   const T* k; int64_t sk_t;
   const T* v; int64_t sv_t;
   const int32_t* idx; int64_t s_idx;
   int64_t rows;
+  int64_t rows1;
+  const T* k2; int64_t sk2_t;
+  const T* v2; int64_t sv2_t;
   __device__ bool get(int i, RowPair<T>& r) const {
     const int64_t j = idx[i * s_idx];
     if (j < 0 || j >= rows) return false;
-    r.k = k + j * sk_t;
-    r.v = v + j * sv_t;
+    if (j < rows1) {
+      r.k = k + j * sk_t;
+      r.v = v + j * sv_t;
+    } else {
+      r.k = k2 + (j - rows1) * sk2_t;
+      r.v = v2 + (j - rows1) * sv2_t;
+    }
     return true;
   }
 };
@@ -194,9 +203,12 @@ __global__ void __launch_bounds__(128) sparse_generic_kernel(const SparseArgs a,
   const bool has_sink = a.sink != nullptr;
   const float sink_log2 = has_sink ? a.sink[h] * kLog2e : 0.f;
   if (!a.decode) {
+    const bool two = a.rows1 < a.kv_rows;
     TopkRows<T> rows{reinterpret_cast<const T*>(a.k) + kvh * a.sk[1], a.sk[0],
                      reinterpret_cast<const T*>(a.v) + kvh * a.sv[1], a.sv[0],
-                     a.topk + t * a.stk[0], a.stk[1], a.kv_rows};
+                     a.topk + t * a.stk[0], a.stk[1], a.kv_rows, a.rows1,
+                     two ? reinterpret_cast<const T*>(a.ck) + kvh * a.sck[1] : nullptr, a.sck[0],
+                     two ? reinterpret_cast<const T*>(a.cv) + kvh * a.scv[1] : nullptr, a.scv[0]};
     generic_attend<T>(q, a.sq[2], a.sk[2], a.sv[2], a.head_dim, a.head_dim_v, a.k_topk, rows, scale_log2, has_sink,
                       sink_log2, out, a.so[2], lse, 0.f);
   } else {

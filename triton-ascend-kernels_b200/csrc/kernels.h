@@ -78,7 +78,7 @@ struct SparseArgs {
   // prefill: k/v rows [rows, H_kv, D]; decode: the paged caches
   const void* k; int64_t sk[4];
   const void* v; int64_t sv[4];
-  // decode only
+  // decode: the compressed rows; prefill: the second row source (see rows1)
   const void* ck; int64_t sck[3];
   const void* cv; int64_t scv[3];
   const int32_t* block_tables; int64_t sbt[2];
@@ -94,6 +94,10 @@ struct SparseArgs {
   float* lse;
   int num_tokens, num_q_heads, num_kv_heads, head_dim, head_dim_v, k_topk;
   int64_t kv_rows;
+  // prefill with two row sources: rows [0, rows1) of k/v, then rows
+  // [rows1, kv_rows) as rows 0.. of ck/cv (the compressed rows); rows1 ==
+  // kv_rows when there is one source
+  int64_t rows1;
   float scale;
   int dtype;
   int decode;

@@ -68,9 +68,11 @@ struct SparseTcParams {
   float* lse;
   int H, Hkv, G, head_chunks;
   float scale_log2;
-  // Row sources, in elements.  Prefill: row r of head h is k + r*k_s0 + h*k_sh.
-  // Decode: k/v are the paged caches (page stride k_s0, head k_sh, row in page
-  // k_sr) and ck/cv the compressed rows (row stride ck_s0, head ck_sh).
+  // Row sources, in elements.  Prefill: row r < rows1 of head h is k + r*k_s0 +
+  // h*k_sh, row r >= rows1 is ck + (r - rows1)*ck_s0 + h*ck_sh.  Decode: k/v are
+  // the paged caches (page stride k_s0, head k_sh, row in page k_sr) and ck/cv
+  // the compressed rows (row stride ck_s0, head ck_sh).
+  int64_t rows1;
   const void* k;
   const void* v;
   const void* ck;
@@ -265,8 +267,14 @@ __global__ void __launch_bounds__(288, 1)
         vr[g] = nullptr;
         if (!(j < n_tiles && c < p.k_topk) || !sp_slot_valid<DECODE>(p, c, r, ctx, bt_row)) continue;
         if (!DECODE) {
-          kr[g] = kb + r * p.k_s0 + kvh * p.k_sh;
-          if (!SHARED) vr[g] = vb + r * p.v_s0 + kvh * p.v_sh;
+          if (r < p.rows1) {
+            kr[g] = kb + r * p.k_s0 + kvh * p.k_sh;
+            if (!SHARED) vr[g] = vb + r * p.v_s0 + kvh * p.v_sh;
+          } else {  // the second source (compressed rows appended after the K/V rows)
+            const int64_t cr = r - p.rows1;
+            kr[g] = reinterpret_cast<const T*>(p.ck) + cr * p.ck_s0 + kvh * p.ck_sh;
+            if (!SHARED) vr[g] = reinterpret_cast<const T*>(p.cv) + cr * p.cv_s0 + kvh * p.cv_sh;
+          }
         } else if (c < p.num_win) {  // window slot: logical position -> page, row in page (SA:160-166)
           const int64_t page = bt_row[(r / p.block_size) * p.sbt1];
           const int64_t off = r % p.block_size;
@@ -646,6 +654,15 @@ static int launch_sparse_tc_mode(const SparseArgs& a, cudaStream_t st) {
   p.k_sh = a.sk[1];
   p.v_s0 = a.sv[0];
   p.v_sh = a.sv[1];
+  p.rows1 = a.decode ? 0 : a.rows1;
+  if (!a.decode && a.rows1 < a.kv_rows) {
+    p.ck = a.ck;
+    p.cv = a.cv;
+    p.ck_s0 = a.sck[0];
+    p.ck_sh = a.sck[1];
+    p.cv_s0 = a.scv[0];
+    p.cv_sh = a.scv[1];
+  }
   if (a.decode) {
     p.k_sr = a.sk[2];
     p.v_sr = a.sv[2];
@@ -729,6 +746,10 @@ int sparse_tc_launch(const SparseArgs& a, cudaStream_t st, bool* handled) {
   if (!a.decode) {
     if (!rows_ok(a.k, a.sk, 3, a.num_kv_heads) || !rows_ok(a.v, a.sv, 3, a.num_kv_heads)) return 0;
     shared = same_view(a.v, a.sv, a.k, a.sk, 3);
+    if (a.rows1 < a.kv_rows) {  // a second row source
+      if (!rows_ok(a.ck, a.sck, 3, a.num_kv_heads) || !rows_ok(a.cv, a.scv, 3, a.num_kv_heads)) return 0;
+      shared = shared && same_view(a.cv, a.scv, a.ck, a.sck, 3);
+    }
   } else {
     // with no compressed rows every compressed slot is masked and ck/cv are never read
     const bool comp = a.num_compressed > 0;
