@@ -1008,7 +1008,7 @@ class MixedWL(Workload):
     at N GPUs is N/8 of the 8-GPU step (N x 32 prefill sequences, N x 512
     decode requests), drawn from one seed and assigned to ranks by a greedy
     longest-processing-time rule on estimated roofline time."""
-    name, unit, bound, peak_key, kernel = "mixed", "% of roofline", "mixed", None, "mixed_step_kernel"
+    name, unit, bound, peak_key, kernel = "mixed", "% of roofline", "mixed", None, "mixed_step"
     desc = ("mixed serving step, one GPU's share of 8: varlen causal prefill of 32 sequences with lengths "
             "log-uniform in [512, 32768] (64 q heads / 8 KV heads, d 128, bf16) plus paged decode of 512 requests "
             "with contexts U[1, 131072] (32 q heads / 8 KV heads, d 128, page 128, bf16), requests and sequences "
@@ -1022,10 +1022,9 @@ class MixedWL(Workload):
 
     def setup(self, rank, device):
         import flash_attention_prefill as FP
-        import mixed_step as MS
         import paged_attention_decode as PD
         import sharding
-        self.FP, self.PD, self.MS = FP, PD, MS
+        self.FP, self.PD = FP, PD
         pk, _ = peaks()
         tens, hbm = pk["bf16_tflops"] * 1e12, pk["hbm_gbs"] * 1e9
         world = self.world
@@ -1063,7 +1062,7 @@ class MixedWL(Workload):
         self.pre_flops = 4.0 * 128 * 64 * sum(L * (L + 1) / 2 for L in self.lens)
         self.dec_bytes = int(self.ctx.to(torch.int64).sum()) * 8 * 128 * 2 * 2 + 2 * B * 32 * 128 * 2
         self.work = self.pre_flops / tens + self.dec_bytes / hbm
-        self.launches = 1
+        self.launches = 3
         self.config = {"prefill_sequences": len(self.lens), "prefill_tokens": T, "decode_requests": B,
                        "decode_context_tokens": int(self.ctx.to(torch.int64).sum()),
                        "prefill_tflop": round(self.pre_flops / 1e12, 3), "decode_gb": round(self.dec_bytes / 1e9, 3),
@@ -1072,32 +1071,23 @@ class MixedWL(Workload):
                        "assignment": f"LPT over {n_pre} sequences + {n_dec} requests on {world} GPU(s)"}
 
     def step(self):
-        # one persistent launch: prefill row blocks and decode splits from one work queue
-        out, _ = self.MS.prefill_and_decode(self.q, self.k, self.v, self.cu, self.qd, self.kc, self.vc, self.btd,
-                                            self.ctxd, 128, True)
+        out = self.FP.flash_attention_prefill(self.q, self.k, self.v, self.cu, True)
+        self.PD.paged_attention_decode(self.qd, self.kc, self.vc, self.btd, self.ctxd, 128, 128)
         return out
 
     def phases(self, device):
-        """Device time of the two kernels launched back to back (each alone)
-        and of the one-launch step, eager, the mean of 3 calls each."""
-        def timed(fn):
-            fn()
-            torch.cuda.synchronize(device)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(3):
-                fn()
-            e1.record()
-            torch.cuda.synchronize(device)
-            return e0.elapsed_time(e1) / 3
-        pms = timed(lambda: self.FP.flash_attention_prefill(self.q, self.k, self.v, self.cu, True))
-        dms = timed(lambda: self.PD.paged_attention_decode(self.qd, self.kc, self.vc, self.btd, self.ctxd, 128, 128))
-        oms = timed(self.step)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        torch.cuda.synchronize(device)
+        ev[0].record()
+        self.FP.flash_attention_prefill(self.q, self.k, self.v, self.cu, True)
+        ev[1].record()
+        self.PD.paged_attention_decode(self.qd, self.kc, self.vc, self.btd, self.ctxd, 128, 128)
+        ev[2].record()
+        torch.cuda.synchronize(device)
+        pms, dms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+        pk, _ = peaks()
         return {"prefill_ms": round(pms, 3), "prefill_tflops": round(self.pre_flops / (pms * 1e-3) / 1e12, 1),
-                "decode_ms": round(dms, 3), "decode_gbs": round(self.dec_bytes / (dms * 1e-3) / 1e9, 1),
-                "back_to_back_ms": round(pms + dms, 3), "one_launch_ms": round(oms, 3),
-                "roofline_frac_back_to_back": round(self.work * 1e3 / (pms + dms), 4),
-                "roofline_frac_one_launch": round(self.work * 1e3 / oms, 4)}
+                "decode_ms": round(dms, 3), "decode_gbs": round(self.dec_bytes / (dms * 1e-3) / 1e9, 1)}
 
     def e2e_setup(self):
         self.h = [t.cpu().pin_memory() for t in (self.q, self.k, self.v, self.qd, self.bt, self.ctx)]
@@ -1111,7 +1101,8 @@ class MixedWL(Workload):
         for d, h in zip(self.d, self.h):
             d.copy_(h, non_blocking=True)
         q, k, v, qd, bt, ctx = self.d
-        o1, o2 = self.MS.prefill_and_decode(q, k, v, self.cu, qd, self.kc, self.vc, bt, ctx, 128, True)
+        o1 = self.FP.flash_attention_prefill(q, k, v, self.cu, True)
+        o2 = self.PD.paged_attention_decode(qd, self.kc, self.vc, bt, ctx, 128, 128)
         self.hout[0].copy_(o1, non_blocking=True)
         self.hout[1].copy_(o2, non_blocking=True)
 

@@ -103,38 +103,6 @@ int tak_paged_attention_decode(const void* q, const int64_t* q_strides, const vo
                                void* workspace, size_t workspace_bytes, int split_pages, void* stream);
 
 /*
- * A serving step's varlen prefill and paged decode in ONE persistent launch
- * (an addition: the reference runs flash_attention_prefill,
- * attention/flash_attention_prefill.py:108-171, and paged_attention_decode,
- * attention/paged_attention_decode.py:104-151, as separate launches).  The
- * arguments are those of tak_flash_attention_prefill followed by those of
- * tak_paged_attention_decode (decode ones prefixed or suffixed _dec), one
- * dtype for both.  A grid of one CTA per SM pulls prefill row-block units and
- * split-KV decode units from one work queue, with decode units spread through
- * it so that the HBM-bound decode overlaps the tensor-bound prefill; the
- * split that finishes last merges its request's splits.  Results equal the
- * two entry points'.  Taken when the prefill has head dim 128 on the
- * tensor-core path and the decode head dim 128 with page size a multiple of
- * 64 on the split-KV path; other shapes run the two kernels back to back.
- * workspace: at least tak_mixed_prefill_decode_workspace_size() bytes (decode
- * partials and work-queue counters; the call clears the counters on its
- * stream).  Calls that share a workspace must not overlap on the GPU.
- */
-size_t tak_mixed_prefill_decode_workspace_size(int64_t num_seqs, int64_t num_q_heads, int64_t num_kv_heads,
-                                               int64_t head_dim, int64_t block_size, int64_t max_blocks);
-int tak_mixed_prefill_decode(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
-                             const void* v, const int64_t* v_strides, const int32_t* cu_seqlens, int64_t num_seqs,
-                             void* out, const int64_t* out_strides, float* lse, int64_t total_tokens,
-                             int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, float scale, int causal,
-                             const void* q_dec, const int64_t* qd_strides, const void* k_cache,
-                             const int64_t* kc_strides, const void* v_cache, const int64_t* vc_strides,
-                             const int32_t* block_tables, const int64_t* bt_strides, const int32_t* context_lens,
-                             void* out_dec, const int64_t* od_strides, float* lse_dec, int64_t num_requests,
-                             int64_t dec_q_heads, int64_t dec_kv_heads, int64_t dec_head_dim, int64_t block_size,
-                             int64_t max_blocks, int64_t num_blocks, int64_t cache_rows, float dec_scale, int dtype,
-                             void* workspace, size_t workspace_bytes, void* stream);
-
-/*
  * Paged decode that allocates nothing.  No counterpart in the reference: it
  * exists for callers that cannot provide the workspace above -- code where a
  * cudaMalloc is not allowed or would stall the device, hosts whose device

@@ -227,14 +227,6 @@ def _call_invalid(name, **vals):
     ("tak_csa_indexer_topk", dict(dtype=1, m=4, top_k=32, n_win=8, ld=16, num_q_heads=8, num_kv_heads=1,
                                   head_dim=512), "null pointer"),
     ("tak_build_token_to_seq", dict(num_seqs=-1, total_tokens=4), "token_to_seq"),
-    ("tak_mixed_prefill_decode", dict(dtype=9, num_q_heads=64, num_kv_heads=8, head_dim=128), "unknown dtype"),
-    ("tak_mixed_prefill_decode", dict(dtype=1, num_q_heads=64, num_kv_heads=8, head_dim=128, dec_q_heads=32,
-                                      dec_kv_heads=5, dec_head_dim=128, block_size=16, cache_rows=16),
-     "num_q_heads must be a multiple"),
-    ("tak_sparse_attn_prefill_2src", dict(dtype=1, total_tokens=4, num_q_heads=64, num_kv_heads=1, head_dim=576,
-                                          head_dim_v=512, k_topk=8, q=8, q_strides=_S4, topk_idxs=8,
-                                          topk_strides=_S4, out=8, out_strides=_S4, kv_rows=-1),
-     "negative row counts"),
 ])
 def test_c_abi_rejects_invalid_arguments(name, vals, msg):
     """Every entry point validates its arguments before touching the device:

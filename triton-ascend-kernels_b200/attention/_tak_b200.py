@@ -33,10 +33,6 @@ _SIGS = {
     "tak_paged_attention_decode_workspace_size": ([_I64, _I64, _I64, _I64, _I64, _I64, _I32], _SZ),
     "tak_paged_attention_decode": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                     _I64, _I64, _I64, _F32, _I32, _P, _SZ, _I32, _P], _I32),
-    "tak_mixed_prefill_decode_workspace_size": ([_I64, _I64, _I64, _I64, _I64, _I64], _SZ),
-    "tak_mixed_prefill_decode": ([_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _I32,
-                                  _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
-                                  _I64, _I64, _I64, _F32, _I32, _P, _SZ, _P], _I32),
     "tak_paged_attention_decode_static_scratch": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64,
                                                    _I64, _I64, _I64, _I64, _I64, _F32, _I32, _I32, _P], _I32),
     "tak_sparse_attn_prefill": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,

@@ -151,28 +151,21 @@ int tak_read_device_error(void* stream) {
   return v;
 }
 
-}  // extern "C"
-
-namespace tak {
-
-static int make_prefill_args(PrefillArgs* out_args, const void* q, const int64_t* q_strides, const void* k,
-                             const int64_t* k_strides, const void* v, const int64_t* v_strides,
-                             const int32_t* cu_seqlens, int64_t num_seqs, void* out, const int64_t* out_strides,
-                             float* lse, int64_t total_tokens, int64_t num_q_heads, int64_t num_kv_heads,
-                             int64_t head_dim, float scale, int causal, int dtype) {
+int tak_flash_attention_prefill(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                const void* v, const int64_t* v_strides, const int32_t* cu_seqlens,
+                                int64_t num_seqs, void* out, const int64_t* out_strides, float* lse,
+                                int64_t total_tokens, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                                float scale, int causal, int dtype, void* stream) {
+  TAK_ENTRY();
   TAK_REQUIRE(dtype >= 0 && dtype <= 2, "prefill: unknown dtype");
   TAK_REQUIRE(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0,
               "prefill: num_q_heads must be a multiple of num_kv_heads");
   TAK_REQUIRE(head_dim > 0 && head_dim <= 640, "prefill: head_dim must be in [1, 640]");
   TAK_REQUIRE(num_seqs >= 0 && total_tokens >= 0, "prefill: negative sizes");
-  PrefillArgs a{};
-  a.total_tokens = static_cast<int>(total_tokens);
-  if (total_tokens == 0) {
-    *out_args = a;
-    return 0;
-  }
+  if (total_tokens == 0) return 0;
   TAK_REQUIRE(q && k && v && out && cu_seqlens && q_strides && k_strides && v_strides && out_strides,
               "prefill: null pointer");
+  PrefillArgs a{};
   a.q = q; copy_strides(a.sq, q_strides, 3);
   a.k = k; copy_strides(a.sk, k_strides, 3);
   a.v = v; copy_strides(a.sv, v_strides, 3);
@@ -180,6 +173,7 @@ static int make_prefill_args(PrefillArgs* out_args, const void* q, const int64_t
   a.out = out; copy_strides(a.so, out_strides, 3);
   a.lse = lse;
   a.num_seqs = static_cast<int>(num_seqs);
+  a.total_tokens = static_cast<int>(total_tokens);
   a.num_q_heads = static_cast<int>(num_q_heads);
   a.num_kv_heads = static_cast<int>(num_kv_heads);
   a.head_dim = a.head_dim_v = static_cast<int>(head_dim);
@@ -187,78 +181,8 @@ static int make_prefill_args(PrefillArgs* out_args, const void* q, const int64_t
   a.causal = causal;
   a.dtype = dtype;
   a.force_generic = g_kernel_path == 1;
-  *out_args = a;
-  return 0;
-}
-
-}  // namespace tak
-
-extern "C" {
-
-int tak_flash_attention_prefill(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
-                                const void* v, const int64_t* v_strides, const int32_t* cu_seqlens,
-                                int64_t num_seqs, void* out, const int64_t* out_strides, float* lse,
-                                int64_t total_tokens, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
-                                float scale, int causal, int dtype, void* stream) {
-  TAK_ENTRY();
-  PrefillArgs a{};
-  const int r0 = make_prefill_args(&a, q, q_strides, k, k_strides, v, v_strides, cu_seqlens, num_seqs, out,
-                                   out_strides, lse, total_tokens, num_q_heads, num_kv_heads, head_dim, scale, causal,
-                                   dtype);
-  if (r0 || total_tokens == 0) return r0;
   const int r = prefill_launch(a, static_cast<cudaStream_t>(stream));
   return r ? r : check_launch("prefill");
-}
-
-size_t tak_mixed_prefill_decode_workspace_size(int64_t num_seqs, int64_t num_q_heads, int64_t num_kv_heads,
-                                               int64_t head_dim, int64_t block_size, int64_t max_blocks) {
-  if (num_kv_heads <= 0 || num_q_heads <= 0 || block_size <= 0) return 0;
-  PagedDecodeArgs a{};
-  a.num_seqs = static_cast<int>(num_seqs);
-  a.num_q_heads = static_cast<int>(num_q_heads);
-  a.num_kv_heads = static_cast<int>(num_kv_heads);
-  a.head_dim = static_cast<int>(head_dim);
-  a.block_size = static_cast<int>(block_size);
-  a.max_blocks = static_cast<int>(max_blocks);
-  return mixed_workspace_bytes(a);
-}
-
-int tak_mixed_prefill_decode(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
-                             const void* v, const int64_t* v_strides, const int32_t* cu_seqlens, int64_t num_seqs,
-                             void* out, const int64_t* out_strides, float* lse, int64_t total_tokens,
-                             int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, float scale, int causal,
-                             const void* q_dec, const int64_t* qd_strides, const void* k_cache,
-                             const int64_t* kc_strides, const void* v_cache, const int64_t* vc_strides,
-                             const int32_t* block_tables, const int64_t* bt_strides, const int32_t* context_lens,
-                             void* out_dec, const int64_t* od_strides, float* lse_dec, int64_t num_requests,
-                             int64_t dec_q_heads, int64_t dec_kv_heads, int64_t dec_head_dim, int64_t block_size,
-                             int64_t max_blocks, int64_t num_blocks, int64_t cache_rows, float dec_scale, int dtype,
-                             void* workspace, size_t workspace_bytes, void* stream) {
-  TAK_ENTRY();
-  PrefillArgs pa{};
-  int r = make_prefill_args(&pa, q, q_strides, k, k_strides, v, v_strides, cu_seqlens, num_seqs, out, out_strides,
-                            lse, total_tokens, num_q_heads, num_kv_heads, head_dim, scale, causal, dtype);
-  if (r) return r;
-  PagedDecodeArgs da{};
-  r = make_paged_decode_args(&da, q_dec, qd_strides, k_cache, kc_strides, v_cache, vc_strides, block_tables,
-                             bt_strides, context_lens, out_dec, od_strides, lse_dec, num_requests, dec_q_heads,
-                             dec_kv_heads, dec_head_dim, block_size, max_blocks, num_blocks, cache_rows, dec_scale,
-                             dtype, 0);
-  if (r) return r;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (total_tokens == 0 && num_requests == 0) return 0;
-  if (num_requests == 0) {  // prefill alone
-    r = prefill_launch(pa, st);
-    return r ? r : check_launch("mixed step (prefill)");
-  }
-  da.workspace = workspace;
-  da.workspace_bytes = workspace_bytes;
-  if (total_tokens == 0) {  // decode alone
-    r = paged_decode_launch(da, st);
-    return r ? r : check_launch("mixed step (decode)");
-  }
-  r = mixed_step_launch(pa, da, st);
-  return r ? r : check_launch("mixed step");
 }
 
 size_t tak_paged_attention_decode_workspace_size(int64_t num_seqs, int64_t num_q_heads, int64_t num_kv_heads,

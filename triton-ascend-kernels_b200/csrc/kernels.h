@@ -56,12 +56,6 @@ int make_paged_decode_args(PagedDecodeArgs* out_args, const void* q, const int64
                            int64_t max_blocks, int64_t num_blocks, int64_t cache_rows, float scale, int dtype,
                            int split_pages);
 
-struct PrefillArgs;
-// Prefill and paged decode in one persistent launch (mixed_step.cu); da's
-// workspace holds the decode partials and the work-queue counters.
-size_t mixed_workspace_bytes(const PagedDecodeArgs& d);
-int mixed_step_launch(const PrefillArgs& pa, const PagedDecodeArgs& da, cudaStream_t st);
-
 struct PrefillArgs {
   const void* q; int64_t sq[3];
   const void* k; int64_t sk[3];
