@@ -187,14 +187,14 @@ __global__ void __launch_bounds__(320, 1)
       for (int j = 0; j < n_kv && !*abort_flag; ++j) {
         const int st = j % NST;
         const int key0 = seq_start + j * BN;
-        if (j >= NST && !mbar_wait(&k_empty[st], ((j / NST) - 1) & 1)) {
+        if (j >= NST && !mbar_wait_sleep(&k_empty[st], ((j / NST) - 1) & 1)) {
           *abort_flag = 1;
           break;
         }
         mbar_arrive_expect_tx(&k_full[st], NB * TILE);
         for (int b = 0; b < NB; ++b)
           tma_load_3d(smem + KOFF + (st * NB + b) * TILE, &tmK, &k_full[st], b * 64, kvh, key0);
-        if (j >= NST && !mbar_wait(&v_empty[st], ((j / NST) - 1) & 1)) {
+        if (j >= NST && !mbar_wait_sleep(&v_empty[st], ((j / NST) - 1) & 1)) {
           *abort_flag = 1;
           break;
         }
@@ -205,7 +205,14 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // The whole warp runs the issuer (one elected lane issues each MMA and
+    // commit); its waits suspend in hardware and are made warp-uniform, so the
+    // warp stays converged and takes no issue slots from the softmax warps
+    // sharing its SM sub-partition.
+    {
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait_sleep(bar, parity));
+      };
       constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t idesc_qk = tc_idesc_f16(AB, BM, BN, 0);
       const uint32_t idesc_pv = tc_idesc_f16(AB, BM, D, 1);
@@ -223,28 +230,28 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * TILE + (kk & 3) * 32) >> 4);
-          tc_mma_ss(d_tmem, qd + koff, kd + koff, idesc_qk, kk > 0 ? 1u : 0u);
+          tc_mma_ss_w(d_tmem, qd + koff, kd + koff, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[t]);
+        tc_commit_w(&s_full[t]);
       };
       auto pv = [&](int t, int j) {
         const uint64_t vd = v_desc0 + ((j % NST) ? kTileStep : 0);
         const uint32_t p_tmem = taddr + 256 + t * 128;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          tc_mma_ts(taddr + t * 128, p_tmem + kk * 8, vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
+          tc_mma_ts_w(taddr + t * 128, p_tmem + kk * 8, vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
                     (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&o_done[t]);
+        tc_commit_w(&o_done[t]);
       };
-      bool ok = n_kv > 0 && mbar_wait(q_full, 0) && mbar_wait(&k_full[0], 0);
+      bool ok = n_kv > 0 && wait(q_full, 0) && wait(&k_full[0], 0);
       if (ok) {
         tc_fence_after();
         if (n_t[0] > 0) qk(0, 0);
         if (n_t[1] > 0) qk(1, 0);
-        tc_commit(&k_empty[0]);
+        tc_commit_w(&k_empty[0]);
       }
       for (int j = 0; ok && j < n_kv; ++j) {
-        if (*abort_flag) {
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) {
           ok = false;
           break;
         }
@@ -252,21 +259,21 @@ __global__ void __launch_bounds__(320, 1)
         // j + 1, so a tile's next softmax can start while the other tile's
         // softmax is still running.
         const int st = j % NST;
-        if (!(ok = mbar_wait(&v_full[st], (j / NST) & 1))) break;
+        if (!(ok = wait(&v_full[st], (j / NST) & 1))) break;
         const bool next = j + 1 < n_kv;
         bool k_next = false;  // K block j + 1 waited for
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (j < n_t[t]) {
-            if (!(ok = mbar_wait(&p_full[t], j & 1))) break;
+            if (!(ok = wait(&p_full[t], j & 1))) break;
             tc_fence_after();
             pv(t, j);
-            if (t == 1 || j >= n_t[1]) tc_commit(&v_empty[st]);
+            if (t == 1 || j >= n_t[1]) tc_commit_w(&v_empty[st]);
             if (j + 1 < n_t[t]) {
-              if (!k_next && !(ok = mbar_wait(&k_full[(j + 1) % NST], ((j + 1) / NST) & 1))) break;
+              if (!k_next && !(ok = wait(&k_full[(j + 1) % NST], ((j + 1) / NST) & 1))) break;
               k_next = true;
               // this tile's S/P columns are rewritten only after its PV of block j has read P
-              if (!(ok = mbar_wait(&o_done[t], j & 1))) break;
+              if (!(ok = wait(&o_done[t], j & 1))) break;
               tc_fence_after();
               qk(t, j + 1);
             }
@@ -277,8 +284,8 @@ __global__ void __launch_bounds__(320, 1)
           // every tile with block j + 1 has issued its S MMA; the commit frees the K stage
           // (a tile without block j + 1 issues none, and then k_full of block j + 1 may
           // not have been waited for: wait here so the stage's phases stay in step)
-          if (!k_next && !(ok = mbar_wait(&k_full[(j + 1) % NST], ((j + 1) / NST) & 1))) break;
-          tc_commit(&k_empty[(j + 1) % NST]);
+          if (!k_next && !(ok = wait(&k_full[(j + 1) % NST], ((j + 1) / NST) & 1))) break;
+          tc_commit_w(&k_empty[(j + 1) % NST]);
         }
       }
       if (!ok && n_kv > 0) *abort_flag = 1;
@@ -298,7 +305,7 @@ __global__ void __launch_bounds__(320, 1)
     float m_run = -INFINITY, m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
-      if (!(ok = mbar_wait(&s_full[t], j & 1))) break;
+      if (!(ok = mbar_wait_sleep(&s_full[t], j & 1))) break;
       tc_fence_after();
       const bool interior = (j + 1) * BN <= lim_all;
       const int nvalid = lim - j * BN;

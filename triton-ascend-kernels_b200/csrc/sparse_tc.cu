@@ -257,12 +257,24 @@ __global__ void __launch_bounds__(288, 1)
     }
     const T* kb = reinterpret_cast<const T*>(p.k);
     const T* vb = reinterpret_cast<const T*>(p.v);
-    // K (and V unless shared) row addresses of this thread's 4 slots of tile j; null = masked
-    auto load_rows = [&](int j, const T** kr, const T** vr) {
+    // Two-stage index pipeline: the raw indices of this thread's 4 slots of a
+    // tile are loaded two tiles ahead (no branch on them, so the loads stay in
+    // flight), and turned into row addresses one tile ahead; a branch on an
+    // index that has just been loaded would stall the producer for a full
+    // memory latency every tile.
+    auto load_idx = [&](int j, int32_t* rr) {
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         const int c = j * BN + g * 16 + rsub;
-        const int64_t r = (j < n_tiles && c < p.k_topk) ? static_cast<int64_t>(idx_row[c * p.stk1]) : -1;
+        rr[g] = (j < n_tiles && c < p.k_topk) ? idx_row[c * p.stk1] : -1;
+      }
+    };
+    // K (and V unless shared) row addresses of the 4 slots of tile j; null = masked
+    auto make_rows = [&](int j, const int32_t* rr, const T** kr, const T** vr) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int c = j * BN + g * 16 + rsub;
+        const int64_t r = rr[g];
         kr[g] = nullptr;
         vr[g] = nullptr;
         if (!(j < n_tiles && c < p.k_topk) || !sp_slot_valid<DECODE>(p, c, r, ctx, bt_row)) continue;
@@ -291,14 +303,18 @@ __global__ void __launch_bounds__(288, 1)
     const T* nxt[4];
     const T* vcur[4];
     const T* vnxt[4];
-    load_rows(0, cur, vcur);
+    int32_t ia[4], ib[4];  // raw indices of tiles j + 1 and j + 2
+    load_idx(0, ia);
+    make_rows(0, ia, cur, vcur);
+    load_idx(1, ia);
     bool ok = true;
     for (int j = 0; j < n_tiles && ok; ++j) {
-      load_rows(j + 1, nxt, vnxt);  // in flight while this tile's stages free up
+      load_idx(j + 2, ib);
+      make_rows(j + 1, ia, nxt, vnxt);
       // ---- K rows of tile j ----
       const int sk = j % NSK;
-      if (j >= NSK) ok = mbar_wait(&k_empty[sk], ((j / NSK) - 1) & 1);
-      else if (sk == NSK - 1) ok = mbar_wait(q_tmem, 0);  // the Q staging area is free
+      if (j >= NSK) ok = mbar_wait_sleep(&k_empty[sk], ((j / NSK) - 1) & 1);
+      else if (sk == NSK - 1) ok = mbar_wait_sleep(q_tmem, 0);  // the Q staging area is free
       if (!ok) break;
       uint8_t* kst = smem + L::KOFF + sk * L::KST;
 #pragma unroll
@@ -315,7 +331,7 @@ __global__ void __launch_bounds__(288, 1)
       if constexpr (!SHARED) {
         // ---- V rows of tile j ----
         const int sv = j % NSV;
-        if (j >= NSV && !(ok = mbar_wait(&v_empty[sv], ((j / NSV) - 1) & 1))) break;
+        if (j >= NSV && !(ok = mbar_wait_sleep(&v_empty[sv], ((j / NSV) - 1) & 1))) break;
         uint8_t* vst = smem + L::VOFF + sv * L::VST;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
@@ -332,13 +348,21 @@ __global__ void __launch_bounds__(288, 1)
       for (int g = 0; g < 4; ++g) {
         cur[g] = nxt[g];
         vcur[g] = vnxt[g];
+        ia[g] = ib[g];
       }
     }
     if (!ok) *abort_flag = 1;
     cp_async_wait_all();
   } else if (warp == 8) {
     // ---------------- MMA issuer (greedy order) ----------------
-    if (lane == 0 && n_tiles > 0) {
+    // The whole warp runs the issuer: one elected lane issues each MMA and
+    // commit, every barrier probe is made warp-uniform (all lanes must see the
+    // phase complete), and an idle pass sleeps briefly so the spinning warp
+    // leaves its SM sub-partition's issue slots to the softmax and gather warps.
+    if (n_tiles > 0) {
+      auto ready = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_try_wait(smem_u32(bar), parity));
+      };
       constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       constexpr int NPV = L::OMAIN < 256 ? L::OMAIN : 256;
       const uint32_t idesc_qk = tc_idesc_f16(AB, 64, BN, 0);
@@ -354,14 +378,14 @@ __global__ void __launch_bounds__(288, 1)
       const uint32_t q_tmem_addr = taddr + L::QCOL;          // lanes 0-15
       const uint32_t o_main = taddr + (16u << 16);           // lanes 16-31
       const uint32_t o_tail = taddr + L::TCOL;               // lanes 0-15
-      bool ok = mbar_wait(q_tmem, 0);
+      bool ok = __all_sync(0xffffffffu, mbar_wait_sleep(q_tmem, 0));
       int nq = 0, np = 0;  // next QK / PV to issue
       const uint64_t t0 = globaltimer();
       uint32_t spins = 0;
       while (ok && np < n_tiles) {
         bool did = false;
         // QK of tile nq: its K stage must be loaded and its S buffer consumed (nq <= np + 1)
-        if (nq < n_tiles && nq <= np + 1 && mbar_try_wait(smem_u32(&k_full[nq % NSK]), (nq / NSK) & 1)) {
+        if (nq < n_tiles && nq <= np + 1 && ready(&k_full[nq % NSK], (nq / NSK) & 1)) {
           fence_proxy_async_smem();
           tc_fence_after();
           const int sk = nq % NSK;
@@ -370,16 +394,15 @@ __global__ void __launch_bounds__(288, 1)
 #pragma unroll
           for (int kk = 0; kk < DQK / 16; ++kk) {
             const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * L::BLK + (kk & 3) * 32) >> 4);
-            tc_mma_ts(d_tmem, q_tmem_addr + kk * 8, kd + koff, idesc_qk, kk > 0 ? 1u : 0u);
+            tc_mma_ts_w(d_tmem, q_tmem_addr + kk * 8, kd + koff, idesc_qk, kk > 0 ? 1u : 0u);
           }
-          tc_commit(&s_full[nq & 1]);
-          if (!SHARED) tc_commit(&k_empty[sk]);  // K rows are done once S is computed
+          tc_commit_w(&s_full[nq & 1]);
+          if (!SHARED) tc_commit_w(&k_empty[sk]);  // K rows are done once S is computed
           ++nq;
           did = true;
         }
         // PV of tile np once its P is in shared memory (and, unshared, its V rows loaded)
-        if (np < nq && mbar_try_wait(smem_u32(p_full), np & 1) &&
-            (SHARED || mbar_try_wait(smem_u32(&v_full[np % NSVd]), (np / NSVd) & 1))) {
+        if (np < nq && ready(p_full, np & 1) && (SHARED || ready(&v_full[np % NSVd], (np / NSVd) & 1))) {
           if (!SHARED) fence_proxy_async_smem();
           tc_fence_after();
           const int sv = SHARED ? np % NSK : np % NSVd;
@@ -390,7 +413,7 @@ __global__ void __launch_bounds__(288, 1)
             for (int kk = 0; kk < BN / 16; ++kk) {
               const uint64_t a = p_desc + static_cast<uint64_t>((kk * 32) >> 4);
               const uint64_t b = vd + static_cast<uint64_t>((half * 4 * L::BLK + kk * 2048) >> 4);
-              tc_mma_ss(o_main + half * 256, a, b, idesc_pv, (np > 0 || kk > 0) ? 1u : 0u);
+              tc_mma_ss_w(o_main + half * 256, a, b, idesc_pv, (np > 0 || kk > 0) ? 1u : 0u);
             }
           }
           if constexpr (L::OTAIL > 0) {
@@ -398,19 +421,21 @@ __global__ void __launch_bounds__(288, 1)
             for (int kk = 0; kk < BN / 16; ++kk) {
               const uint64_t a = p_desc + static_cast<uint64_t>((kk * 32) >> 4);
               const uint64_t b = vd + static_cast<uint64_t>((8 * L::BLK + kk * 2048) >> 4);
-              tc_mma_ss(o_tail, a, b, idesc_tail, (np > 0 || kk > 0) ? 1u : 0u);
+              tc_mma_ss_w(o_tail, a, b, idesc_tail, (np > 0 || kk > 0) ? 1u : 0u);
             }
           }
-          tc_commit(o_done);
-          if (SHARED) tc_commit(&k_empty[sv]);
-          else tc_commit(&v_empty[sv]);
-          tc_commit(p_free);
+          tc_commit_w(o_done);
+          if (SHARED) tc_commit_w(&k_empty[sv]);
+          else tc_commit_w(&v_empty[sv]);
+          tc_commit_w(p_free);
           ++np;
           did = true;
         }
-        if (!did && (++spins & 255u) == 0u) {
-          if (globaltimer() - t0 > TAK_WAIT_LIMIT_NS * 4 || *abort_flag) {
-            record_error(1);
+        if (!did) {
+          __nanosleep(32);
+          if ((++spins & 255u) == 0u &&
+              __any_sync(0xffffffffu, globaltimer() - t0 > TAK_WAIT_LIMIT_NS * 4 || *abort_flag != 0)) {
+            if (lane == 0) record_error(1);
             ok = false;
           }
         }
@@ -486,7 +511,7 @@ __global__ void __launch_bounds__(288, 1)
       const int b = j & 1;
       const uint32_t vbits = vnext;
       if (j + 1 < n_tiles) vnext = tile_mask(j + 1);
-      if (!(ok = mbar_wait(&s_full[b], (j >> 1) & 1))) break;
+      if (!(ok = mbar_wait_sleep(&s_full[b], (j >> 1) & 1))) break;
       tc_fence_after();
       uint32_t sr[32];
       tmem_ld16x2(taddr + s_lane + b * 64, sr);
@@ -562,7 +587,7 @@ __global__ void __launch_bounds__(288, 1)
         }
       }
       l += ls;
-      if (j >= 1 && !(ok = mbar_wait(p_free, (j - 1) & 1))) break;
+      if (j >= 1 && !(ok = mbar_wait_sleep(p_free, (j - 1) & 1))) break;
       uint8_t* prow = smem + L::POFF + row * 128;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
