@@ -16,21 +16,26 @@
 // their diagonal block (the reference sweeps every block, FP:60).  Aligned
 // blocks are issued last-first (longest work first).
 //
-// Warp roles (320 threads):
-//   warp 8      TMA producer: both Q tiles once, then K and V blocks of 128
+// Warp roles (576 threads):
+//   warp 16     TMA producer: both Q tiles once, then K and V blocks of 128
 //               rows into 2-stage rings (128-byte swizzle, 64-column boxes).
-//   warp 9      TMEM allocator + single-thread tcgen05.mma issuer.  Per K/V
-//               block j and tile t: PV_t(j) (TS-MMA: P read from TMEM, V from
-//               smem, MN-major), then S_t(j+1) = Q_t K^T (SS-MMA, M=N=128)
-//               once PV_t(j) has completed (S_t and P_t share TMEM columns).
-//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B (thread = row =
-//               TMEM lane): load S, mask only on boundary blocks, online max
-//               with lazy rescaling (O and l rescaled only when the max grows
-//               by more than 2^8), P = 2^(s - m) on the MUFU unit, packed to
-//               16 bits back into the tile's S columns; epilogue
-//               reads O, normalises, stores the row and its LSE.  While one
-//               warpgroup runs its softmax the tensor core works on the other
-//               tile.
+//   warp 17     TMEM allocator + tcgen05.mma issuer (the whole warp runs it,
+//               one elected lane issues).  Per K/V block j and tile t:
+//               PV_t(j) (TS-MMA: P read from TMEM, V from smem, MN-major),
+//               then S_t(j+1) = Q_t K^T (SS-MMA, M=N=128) once PV_t(j) has
+//               completed (S_t and P_t share TMEM columns).
+//   warps 0-7   softmax of tile A, warps 8-15 softmax of tile B, two threads
+//               per row (thread = TMEM lane; warp w and its partner w ^ 4 take
+//               score columns [0,64) and [64,128)): load S, mask only on
+//               boundary blocks, exchange the halves' row maxima through
+//               shared memory (an mbarrier per warp pair), online max with lazy
+//               rescaling (O and l rescaled only when the max grows by more
+//               than 2^8), P = 2^(s - m) on the MUFU unit, packed to 16 bits
+//               into the half's own first 32 S columns; epilogue adds the
+//               halves' row sums, normalises and stores each half of the row
+//               and its LSE.  Two warps per row on each SM sub-partition keep
+//               the exponent pipe busier than one; while one tile's softmax
+//               runs the tensor core works on the other tile.
 // TMEM: O_A [0,128), O_B [128,256), S/P_A [256,384), S/P_B [384,512); with
 // one tile (D = 256), O_A [0,256) and S/P_A [256,384).
 #include <type_traits>
@@ -52,7 +57,7 @@ struct PrefillTcParams {
 namespace pf {
 constexpr int BM = 128, BN = 128;
 constexpr int TILE = 128 * 128;                   // one 64-column block of 128 rows (bytes)
-constexpr int NBAR = 15;
+constexpr int NBAR = 23;
 constexpr float kRescaleThreshold = 8.f;          // log2 units
 // Shared-memory layout and tiling of head dim D: NT query tiles of 128 rows
 // per CTA, NST-stage K and V rings, NB 64-column boxes per row.
@@ -66,8 +71,13 @@ struct Cfg {
   static constexpr int KOFF = NT * NB * TILE;
   static constexpr int VOFF = KOFF + NST * NB * TILE;
   static constexpr int BAROFF = VOFF + NST * NB * TILE;
-  static constexpr int SMEM = BAROFF + NBAR * 8 + 16 + 1024;
+  // softmax partner exchange: row maxima [block parity][tile][half][row] and
+  // row sums [tile][half][row]
+  static constexpr int XOFF = BAROFF + NBAR * 8 + 16 + 8;
+  static constexpr int SMEM = XOFF + (2 * 2 * 2 * 128 + 2 * 2 * 128) * 4 + 1024;
+  static_assert(SMEM <= 232448, "shared memory");
 };
+constexpr int NWARP = 18;  // 16 softmax warps, producer, MMA issuer
 }  // namespace pf
 
 __device__ __forceinline__ int pf_find_seq(const int32_t* cu, int n, int t) {
@@ -85,7 +95,7 @@ __device__ __forceinline__ int pf_find_seq(const int32_t* cu, int n, int t) {
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(pf::NWARP * 32, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const PrefillTcParams p) {
   using namespace pf;
@@ -103,6 +113,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* s_full = bars + 9;   // [2] per tile
   uint64_t* p_full = bars + 11;  // [2] per tile
   uint64_t* o_done = bars + 13;  // [2] per tile
+  uint64_t* pair_mb = bars + 15; // [2][4] per tile and lane quadrant: the two softmax warps' exchange
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -129,7 +140,7 @@ __global__ void __launch_bounds__(320, 1)
     row1 = min((st / ROWS + 1) * ROWS, en);
   } else {
     // rows past the last sequence: zeros (FP:189)
-    for (int t = cu_end + warp; t < p.total_tokens; t += 10) {
+    for (int t = cu_end + warp; t < p.total_tokens; t += NWARP) {
       T* o = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(t) * p.so_t + static_cast<int64_t>(h) * p.so_h;
       for (int d = lane; d < D; d += 32) o[d] = Elem<T>::from_f(0.f);
       if (lane == 0 && p.lse) p.lse[static_cast<int64_t>(t) * p.H + h] = -INFINITY;
@@ -151,19 +162,20 @@ __global__ void __launch_bounds__(320, 1)
 
   if (tid == 0) {
     mbar_init(q_full, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&pair_mb[i], 64);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 256);
       mbar_init(&o_done[i], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == 17) {
     tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
   }
@@ -173,7 +185,7 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t taddr = *tmem_holder;
   const uint32_t sbase = smem_u32(smem);
 
-  if (warp == 8) {
+  if (warp == 16) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -203,7 +215,7 @@ __global__ void __launch_bounds__(320, 1)
           tma_load_3d(smem + VOFF + (st * NB + b) * TILE, &tmV, &v_full[st], b * 64, kvh, key0);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 17) {
     // ---------------- MMA issuer ----------------
     // The whole warp runs the issuer (one elected lane issues each MMA and
     // commit); its waits suspend in hardware and are made warp-uniform, so the
@@ -239,7 +251,8 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t p_tmem = taddr + 256 + t * 128;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          tc_mma_ts_w(taddr + t * 128, p_tmem + kk * 8, vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
+          tc_mma_ts_w(taddr + t * 128, p_tmem + (kk >> 2) * 64 + (kk & 3) * 8,
+                      vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
                     (j > 0 || kk > 0) ? 1u : 0u);
         tc_commit_w(&o_done[t]);
       };
@@ -290,32 +303,41 @@ __global__ void __launch_bounds__(320, 1)
       }
       if (!ok && n_kv > 0) *abort_flag = 1;
     }
-  } else if (warp < 8) {
-    // ---------------- softmax + epilogue: warps 0-3 tile A, warps 4-7 tile B ----------------
-    const int t = warp >> 2;
-    const int r = tid & 127;
+  } else if (warp < 16) {
+    // ---------------- softmax + epilogue: warps 0-7 tile A, warps 8-15 tile B ----------------
+    // Two threads per row: warp w covers TMEM lane quadrant w % 4 and score
+    // columns [64 hf, 64 hf + 64) of its tile, hf = (w / 4) % 2; its partner
+    // warp w ^ 4 covers the other half of the same rows.
+    const int t = warp >> 3;
+    const int hf = (warp >> 2) & 1;
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;
     const int nt = n_t[t];
     const bool row_ok = r < rows_t[t];
     const int lim = !row_ok ? 0 : (p.causal ? min(seq_len, p0_t[t] + r + 1) : seq_len);
     // blocks below this bound need no mask for any row of the tile
     const int lim_all = p.causal ? min(seq_len, p0_t[t] + 1) : seq_len;
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
     const uint32_t s_tmem = taddr + lane_off + 256 + t * 128;
-    const uint32_t o_tmem = taddr + lane_off + t * 128;
+    const uint32_t o_tmem = taddr + lane_off + t * 128 + hf * (D / 2);  // this thread's half of O's columns
+    float* const xmax = reinterpret_cast<float*>(smem + C::XOFF);       // [2][2][2][128]
+    float* const xl = xmax + 2 * 2 * 2 * 128;                           // [2][2][128]
+    uint64_t* const xbar = &pair_mb[t * 4 + qd];  // phase j: block j's maxima; phase nt: the row sums
     float m_run = -INFINITY, m_used = -INFINITY, l = 0.f;
     bool ok = true;
+    const float sl2 = p.scale_log2;
+    const uint64_t sl2x2 = (static_cast<uint64_t>(__float_as_uint(sl2)) << 32) | __float_as_uint(sl2);
     for (int j = 0; j < nt; ++j) {
       if (!(ok = mbar_wait_sleep(&s_full[t], j & 1))) break;
       tc_fence_after();
       const bool interior = (j + 1) * BN <= lim_all;
-      const int nvalid = lim - j * BN;
-      // pass 1: row max over the 128 scores (two 64-column loads)
+      const int nvalid = lim - j * BN - hf * 64;  // valid columns of this half
+      // pass 1: this half's row max over its 64 scores
       float mx = -INFINITY;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
+      {
         uint32_t sr[64];
-        tmem_ld32(s_tmem + hh * 64, sr);
-        tmem_ld32(s_tmem + hh * 64 + 32, sr + 32);
+        tmem_ld32(s_tmem + hf * 64, sr);
+        tmem_ld32(s_tmem + hf * 64 + 32, sr + 32);
         tmem_ld_wait();
         if (interior) {
           // four independent chains of three-input maxima (two scores each)
@@ -330,10 +352,17 @@ __global__ void __launch_bounds__(320, 1)
           mx = fmax3(mx, m1, fmaxf(m2, m3));
         } else {
 #pragma unroll
-          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, hh * 64 + c < nvalid ? __uint_as_float(sr[c]) : -INFINITY);
+          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, c < nvalid ? __uint_as_float(sr[c]) : -INFINITY);
         }
       }
-      const float m_new = fmaxf(m_run, mx * p.scale_log2);
+      // the row max over both halves (exchange buffers alternate by block, so
+      // a write of block j + 2 follows the partner's read of block j)
+      float* xm = xmax + ((j & 1) * 4 + t * 2) * 128;
+      xm[hf * 128 + r] = mx;
+      mbar_arrive(xbar);
+      if (!(ok = mbar_wait(xbar, j & 1))) break;
+      mx = fmaxf(mx, xm[(hf ^ 1) * 128 + r]);
+      const float m_new = fmaxf(m_run, mx * sl2);
       const bool need = m_new != -INFINITY && m_new > m_used + kRescaleThreshold;
       const bool rescale_o = need && m_used != -INFINITY;
       if (__any_sync(0xffffffffu, rescale_o)) {
@@ -342,7 +371,7 @@ __global__ void __launch_bounds__(320, 1)
         const float f = rescale_o ? fast_exp2(m_used - m_new) : 1.f;
         uint32_t orow[32];
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
           tmem_ld32(o_tmem + c * 32, orow);
           tmem_ld_wait();
 #pragma unroll
@@ -355,17 +384,16 @@ __global__ void __launch_bounds__(320, 1)
       if (need) m_used = m_new;
       m_run = m_new;
       const float mu = m_used == -INFINITY ? 0.f : m_used;
-      const float sl2 = p.scale_log2;
-      // pass 2: P = 2^(s*scale - m), 32 scores at a time; the 16 packed columns
-      // of chunk c land on S columns [16c, 16c+16), already consumed
+      // pass 2: P = 2^(s*scale - m) of this half's 64 keys, 32 at a time,
+      // packed into this half's own first 32 S columns (key pair c of the half
+      // in column 64 hf + c; chunk c4 lands on columns already read)
       float ls0 = 0.f, ls1 = 0.f;
       uint64_t lsx2 = 0;  // packed row-sum pair of the interior path (two +0.0f)
-      const uint64_t sl2x2 = (static_cast<uint64_t>(__float_as_uint(sl2)) << 32) | __float_as_uint(sl2);
       const uint64_t nmux2 = (static_cast<uint64_t>(__float_as_uint(-mu)) << 32) | __float_as_uint(-mu);
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c4 = 0; c4 < 2; ++c4) {
         uint32_t sr[32], pk[16];
-        tmem_ld32(s_tmem + c4 * 32, sr);
+        tmem_ld32(s_tmem + hf * 64 + c4 * 32, sr);
         tmem_ld_wait();
         if (interior) {
           // two scores per packed fp32 FMA and per packed row-sum add (same
@@ -391,7 +419,7 @@ __global__ void __launch_bounds__(320, 1)
             pk[c] = Elem<T>::pack2(a, bb);
           }
         }
-        tmem_st16(s_tmem + 16 * c4, pk);
+        tmem_st16(s_tmem + hf * 64 + 16 * c4, pk);
       }
       ls0 += __uint_as_float(static_cast<uint32_t>(lsx2));
       ls1 += __uint_as_float(static_cast<uint32_t>(lsx2 >> 32));
@@ -403,15 +431,21 @@ __global__ void __launch_bounds__(320, 1)
     if (ok && nt > 0) ok = mbar_wait(&o_done[t], (nt - 1) & 1);
     if (!ok) *abort_flag = 1;
     if (nt > 0) {
+      // the row sum over both halves
+      xl[(t * 2 + hf) * 128 + r] = l;
+      mbar_arrive(xbar);
+      if (ok) ok = mbar_wait(xbar, nt & 1);
+      const float l_tot = l + xl[(t * 2 + (hf ^ 1)) * 128 + r];
       tc_fence_after();
       const float f = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_run);
-      const float inv = (l > 0.f && ok) ? f / (l * f + 1e-6f) : 0.f;
+      const float inv = (l_tot > 0.f && ok) ? f / (l_tot * f + 1e-6f) : 0.f;
       T* orow = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(row0 + t * BM + r) * p.so_t +
-                static_cast<int64_t>(h) * p.so_h;
-      // up to 128 columns of O per TMEM round trip (all loads, one wait, stores)
-      constexpr int CW = D < 128 ? D : 128;
+                static_cast<int64_t>(h) * p.so_h + hf * (D / 2);
+      // this thread's D / 2 columns of O, up to 64 per TMEM round trip
+      constexpr int HD = D / 2;
+      constexpr int CW = HD < 64 ? HD : 64;
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += CW) {
+      for (int c0 = 0; c0 < HD; c0 += CW) {
         float o[CW];
 #pragma unroll
         for (int c = 0; c < CW / 32; ++c)
@@ -429,16 +463,16 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
-      if (row_ok) {
+      if (row_ok && hf == 0) {
         if (p.lse)
           p.lse[static_cast<int64_t>(row0 + t * BM + r) * p.H + h] =
-              (l > 0.f && ok) ? (m_used + __log2f(l)) * kLn2 : -INFINITY;
+              (l_tot > 0.f && ok) ? (m_used + __log2f(l_tot)) * kLn2 : -INFINITY;
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 17) {
     tc_fence_after();
     tmem_dealloc(taddr, 512);
   }
@@ -485,7 +519,7 @@ static int launch_prefill_tc(const PrefillArgs& a, cudaStream_t st) {
   const dim3 grid(static_cast<unsigned>((n_aligned + a.num_seqs + 1) * a.num_q_heads));
   auto kern = prefill_tc_kernel<T, D>;
   if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::SMEM)) return r;
-  kern<<<grid, 320, C::SMEM, st>>>(mq, mk, mv, p);
+  kern<<<grid, pf::NWARP * 32, C::SMEM, st>>>(mq, mk, mv, p);
   note_kernel("prefill_tc");
   return 0;
 }
