@@ -305,11 +305,45 @@ class PipelinedE2E:
                 if self.copy_back:
                     for h, d in zip(self.hout, res):
                         h.copy_(d, non_blocking=True)
-            for d in outs:
-                d.record_stream(self.d2h)
+            if not torch.cuda.is_current_stream_capturing():
+                for d in outs:
+                    d.record_stream(self.d2h)
         self.i += 1
 
-    def timed(self, steps, warmup, world):
+    def capture(self, n):
+        """One CUDA graph of n consecutive pipelined steps (copy streams and
+        events included), so that the host's launch cost per step -- the
+        public call's Python wrapper, the copies, the events -- cannot leave the
+        device idle, as in a serving engine that replays its decode step from a
+        graph.  n is even: the graph ends on the buffer set it starts on."""
+        assert n % 2 == 0 and self.i % 2 == 0
+        g = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(self.device)
+        cap.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(cap):
+            self.compute(*self.sets[0])  # per-stream caches (the decode workspace) exist before capture
+        torch.cuda.synchronize(self.device)
+        saved = self.comp
+        with torch.cuda.graph(g, stream=cap):
+            self.comp = cap
+            self.h2d.wait_stream(cap)
+            self.d2h.wait_stream(cap)
+            i0 = self.i
+            self.i = 0  # within the graph no step waits on a step before it
+            for _ in range(n):
+                self.step()
+            cap.wait_stream(self.h2d)
+            cap.wait_stream(self.d2h)
+            self.i = i0
+        self.comp = saved
+        torch.cuda.synchronize(self.device)
+        return g
+
+    def timed(self, steps, warmup, world, graph_steps=0):
+        """Device ms per step over exactly `steps` steps.  With graph_steps,
+        whole graphs of that many steps are replayed (the remainder runs as
+        plain steps)."""
+        g = self.capture(graph_steps) if graph_steps else None
         for _ in range(warmup):
             self.step()
         torch.cuda.synchronize(self.device)
@@ -317,10 +351,28 @@ class PipelinedE2E:
             torch.distributed.barrier()
         torch.cuda.synchronize(self.device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(self.h2d)
-        for _ in range(steps):
-            self.step()
-        e1.record(self.d2h if (self.copy_back or self.post is not None) else self.comp)
+        if g is None:
+            e0.record(self.h2d)
+            for _ in range(steps):
+                self.step()
+            e1.record(self.d2h if (self.copy_back or self.post is not None) else self.comp)
+        else:
+            st = torch.cuda.current_stream(self.device)
+            e0.record(st)
+            for _ in range(steps // graph_steps):
+                g.replay()
+            st.wait_stream(self.h2d)
+            st.wait_stream(self.d2h)
+            rem = steps % graph_steps
+            if rem:
+                self.h2d.wait_stream(st)
+                self.d2h.wait_stream(st)
+                self.comp.wait_stream(st)
+                for _ in range(rem):
+                    self.step()
+                st.wait_stream(self.comp)
+                st.wait_stream(self.d2h)
+            e1.record(st)
         torch.cuda.synchronize(self.device)
         return e0.elapsed_time(e1) / steps
 
@@ -398,7 +450,10 @@ def run_decode_ours(args, rank, world, device):
     n_all = sum(len(i) for i in ids)
     e2e = PipelinedE2E([q, bt, ctx], e2e_compute, [((n_all,) + tuple(q.shape[1:]), q.dtype)], device,
                        copy_back=rank == 0, post=gather)
-    e2e_ms = e2e.timed(args.steps, args.warmup, world)
+    # one GPU: eight pipelined steps per CUDA graph (host launch cost off the
+    # device's critical path); more GPUs: plain steps (the NCCL gather stays
+    # outside graphs)
+    e2e_ms = e2e.timed(args.steps, args.warmup, world, graph_steps=8 if world == 1 and not args.no_graph else 0)
     h2d, d2h = e2e.h2d_bytes(), e2e.d2h_bytes()
 
     per_rank = None
@@ -456,6 +511,8 @@ def run_decode_ours(args, rank, world, device):
                 "note": "public paged_attention_decode() with q / block tables / context lengths copied from pinned "
                         "host memory and the output copied back every step, copies on two copy streams overlapping "
                         "the neighbouring steps' kernels (two buffer sets); the KV cache is resident"
+                        + ("; eight such steps (calls, copies and events) replayed per CUDA graph, as a serving "
+                           "engine replays its decode step" if world == 1 and not args.no_graph else "")
                         + ("; includes the NCCL all-gather of every rank's output (on the copy-back stream, "
                            "overlapping the next step's kernels) and rank 0's copy of the whole result"
                            if world > 1 else "")},
@@ -1211,7 +1268,8 @@ def run_workload_ours(args, rank, world, device, W):
             # K // sets replays of it, then the remainder one set at a time.
             def all_sets():
                 for i in range(out_sets):
-                    w.use_outputs(i)
+                    if hasattr(w, "use_outputs"):
+                        w.use_outputs(i)
                     w.step()
             multi = capture_graph(all_sets, device)[0]
     with Clocks(device.index) as clk:
