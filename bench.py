@@ -1430,12 +1430,13 @@ def main():
         res = run_decode_ours(args, rank, world, device)
         if not args.no_workloads:
             # the metric's other figures (prefill / sparse TFLOP/s, compression
-            # GB/s), each measured like the headline: same steps and warm-up,
-            # own roofline, clocks, end-to-end leg and CPU baseline
+            # GB/s) and the mixed serving step (at 8 GPUs: the box-scale step),
+            # each measured like the headline: same steps and warm-up, own
+            # roofline, clocks, end-to-end leg and CPU baseline
             sub_args = argparse.Namespace(**vars(args))
             sub_args.cpu_seconds = args.workload_cpu_seconds
             wl = {}
-            for name in ("prefill", "sparse", "compress"):
+            for name in ("prefill", "sparse", "compress", "mixed"):
                 torch.cuda.empty_cache()
                 r = run_workload_ours(sub_args, rank, world, device, WORKLOADS[name])
                 if rank == 0:
