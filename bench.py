@@ -1286,7 +1286,9 @@ def run_workload_ours(args, rank, world, device, W):
         hin, fn, outs = w.e2e_pipeline()
         pe = PipelinedE2E(hin, fn, outs, device)
         del hin
-        e2e_ms = pe.timed(max(3, args.steps // 4), 2, world)
+        # each end-to-end step moves gigabytes over PCIe: a quarter of the
+        # steps, at least 3 and at most 8, bounds the run at any --steps
+        e2e_ms = pe.timed(min(8, max(3, args.steps // 4)), 2, world)
         h2d, d2h = pe.h2d_bytes(), pe.d2h_bytes()
         del pe
         pipelined = True
@@ -1294,7 +1296,7 @@ def run_workload_ours(args, rank, world, device, W):
         h2d, d2h = w.e2e_setup()
         if world > 1:
             torch.distributed.barrier()
-        e2e_ms = w.timed(w.e2e_step, max(2, args.steps // 4), 1, device)
+        e2e_ms = w.timed(w.e2e_step, min(8, max(2, args.steps // 4)), 1, device)
     work_all = float(w.work)
     gather_ms = None
     per_rank = None
