@@ -16,9 +16,13 @@
 // idx - ctx of the compressed K/V).  Only the producer's row addressing and the
 // validity mask differ from the prefill form.
 //
-// One CTA = one query token x one group of up to 64 query heads sharing a KV
+// A unit = one query token x one group of up to 64 query heads sharing a KV
 // head (MQA: all 64 heads of the token).  The 64 head rows are the MMA's
 // M = 64 dimension, so every gathered K/V row is read once for all heads.
+// Prefill runs one persistent CTA per SM, each taking units blockIdx.x,
+// blockIdx.x + gridDim.x, ...; the pipelines (gathers, MMAs, softmax) run on
+// across a unit boundary, so the next unit's Q and first rows load while the
+// current unit finishes.  Decode runs one unit per CTA.
 //
 // Tensor memory (M = 64 uses half of each 32-lane quadrant):
 //   lanes 0-15 of each quadrant: S (two 64-column buffers, columns 0-127) and
@@ -31,20 +35,21 @@
 // while the tensor core works on a third.
 //
 // Warp roles (288 threads):
-//   warps 4-7 gather producers: Q rows once (one TMA, staged in the last K
+//   warps 4-7 gather producers: per unit its Q rows (one TMA into a K ring
 //            stage), then for each tile of 64 indices, cp.async 16-byte copies
 //            of the gathered rows (8 lanes per 128-byte line, so every warp
 //            instruction moves 4 full lines) written straight into the
 //            128-byte-swizzled layout the MMA reads; K and V have rings of
 //            their own unless V is a prefix view of K (then the K rows serve
-//            both); masked rows are zero-filled; the next tile's indices are
-//            loaded while the current tile is in flight.
-//   warp 8   TMEM allocator + single-thread tcgen05.mma issuer:
+//            both); masked rows are zero-filled; a tile's raw indices are
+//            loaded two tiles ahead and its row addresses formed one ahead.
+//   warp 8   TMEM allocator + tcgen05.mma issuer (one elected lane):
 //            S_j = Q K_j^T (M=64, N=64, K=16 x Dqk/16, A from TMEM), O += P_j
 //            V_j (M=64, N<=256 per instruction, P from shared memory).  Issue
 //            order is greedy: whichever of "QK of the next loaded tile" and
 //            "PV of the next softmaxed tile" is ready goes first.
-//   warps 0-3 move Q from shared memory into TMEM once, then run the softmax:
+//   warps 0-3 move each unit's Q from shared memory into TMEM (once the
+//            previous unit's last S is read), then run the softmax:
 //            TMEM loads of shape 16x32bx2 let all 32 threads of a warp work
 //            on its 16 head rows (two threads per row, 32 columns each); lazy
 //            rescaling of O (only when the max grows by > 2^8); P written to
@@ -86,6 +91,10 @@ struct SparseTcParams {
   int num_win, block_size;
   int64_t wreach;      // block-table width x block_size: window positions at or past it are masked
   int64_t num_blocks;  // pages of the cache: a window position on a page id outside [0, num_blocks) is masked
+  // work units: unit u = (token u / Y, KV head x head chunk u % Y); a CTA
+  // takes units blockIdx.x, blockIdx.x + gridDim.x, ...
+  int64_t n_units;
+  int Y;
 };
 
 // Validity of slot c holding index j (decode: by slot position, SA:151-171 for
@@ -192,9 +201,9 @@ __global__ void __launch_bounds__(288, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAROFF);
-  uint64_t* q_full = bars + 0;   // Q landed in its staging stage
-  uint64_t* q_tmem = bars + 1;   // Q copied into TMEM (staging stage free)
-  uint64_t* k_full = bars + 2;   // [4]
+  uint64_t* o_free = bars + 0;   // per unit: its epilogue has read O (128 arrivals)
+  uint64_t* q_tmem = bars + 1;   // per unit: its Q is in TMEM (128 arrivals)
+  uint64_t* k_full = bars + 2;   // [4] K ring items: a unit's Q, then its tiles' K rows
   uint64_t* k_empty = bars + 6;  // [4]
   uint64_t* v_full = bars + 10;  // [4]
   uint64_t* v_empty = bars + 14; // [4]
@@ -204,21 +213,20 @@ __global__ void __launch_bounds__(288, 1)
   uint64_t* o_done = bars + 22;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + L::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  uint8_t* const qstage = smem + L::KOFF + (NSK - 1) * L::KST;
 
-  const int t = blockIdx.x;
-  const int kvh = blockIdx.y / p.head_chunks;
-  const int hc = blockIdx.y % p.head_chunks;
-  const int h0 = kvh * p.G + hc * 64;
-  const int nrows = min(64, p.G - hc * 64);
+  // This CTA's units: blockIdx.x + i * gridDim.x for i < n_my.  Tiles are
+  // counted over all of them (J = i * n_tiles + j), and so are the K ring's
+  // items: unit i's Q is item i * (n_tiles + 1), its tile j the items after
+  // it.  Every barrier phase follows these global counts.
   const int n_tiles = (p.k_topk + BN - 1) / BN;
+  const int64_t u0 = blockIdx.x;
+  const int n_my = u0 < p.n_units ? static_cast<int>((p.n_units - 1 - u0) / gridDim.x + 1) : 0;
+  auto unit_of = [&](int i) -> int64_t { return u0 + static_cast<int64_t>(i) * gridDim.x; };
+  auto q_item = [&](int i) -> int { return i * (n_tiles + 1); };
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int32_t* idx_row = p.topk + static_cast<int64_t>(t) * p.stk0;
-  const int ctx = DECODE ? p.ctx_lens[t] : 0;
-  const int32_t* bt_row = DECODE ? p.bt + static_cast<int64_t>(t) * p.sbt0 : nullptr;
 
   if (tid == 0) {
-    mbar_init(q_full, 1);
+    mbar_init(o_free, 128);
     mbar_init(q_tmem, 128);
     for (int i = 0; i < NSK; ++i) {
       mbar_init(&k_full[i], NPROD);
@@ -249,35 +257,65 @@ __global__ void __launch_bounds__(288, 1)
     // ---------------- gather producers ----------------
     const int pt = tid - 128;                 // 0..127
     const int rsub = pt >> 3, chunk = pt & 7;  // row within a 16-row group, 16-byte chunk within a line
-    if (pt == 0) {
-      tma_prefetch_desc(&tmQ);
-      mbar_arrive_expect_tx(q_full, L::NQB * L::BLK);
-#pragma unroll 1
-      for (int cb = 0; cb < L::NQB; ++cb) tma_load_2d(qstage + cb * L::BLK, &tmQ, q_full, cb * 64, t * p.H + h0);
-    }
+    if (pt == 0) tma_prefetch_desc(&tmQ);
     const T* kb = reinterpret_cast<const T*>(p.k);
     const T* vb = reinterpret_cast<const T*>(p.v);
     // Two-stage index pipeline: the raw indices of this thread's 4 slots of a
     // tile are loaded two tiles ahead (no branch on them, so the loads stay in
     // flight), and turned into row addresses one tile ahead; a branch on an
     // index that has just been loaded would stall the producer for a full
-    // memory latency every tile.
-    auto load_idx = [&](int j, int32_t* rr) {
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const int c = j * BN + g * 16 + rsub;
-        rr[g] = (j < n_tiles && c < p.k_topk) ? idx_row[c * p.stk1] : -1;
+    // memory latency every tile.  Tiles are numbered over all of the CTA's
+    // units, so the pipeline runs on across a unit boundary.
+    // Two cursors walk the CTA's tiles in order -- one loading raw indices,
+    // one forming row addresses -- and redo the per-unit arithmetic (token,
+    // KV head, lengths) only when they cross into the next unit.
+    struct Cursor {
+      int i, j;                 // unit of the CTA, tile within it
+      bool in;                  // i < n_my
+      const int32_t* ir;        // the unit's index row
+      int kvh, ctx;
+      const int32_t* bt_row;
+    };
+    auto open_unit = [&](Cursor& c) {
+      c.in = c.i < n_my;
+      const int64_t u = c.in ? unit_of(c.i) : 0;
+      const int t = static_cast<int>(u / p.Y);
+      c.ir = p.topk + static_cast<int64_t>(t) * p.stk0;
+      c.kvh = static_cast<int>(u % p.Y) / p.head_chunks;
+      c.ctx = (DECODE && c.in) ? p.ctx_lens[t] : 0;
+      c.bt_row = DECODE ? p.bt + static_cast<int64_t>(t) * p.sbt0 : nullptr;
+    };
+    auto advance = [&](Cursor& c) {
+      if (++c.j == n_tiles) {
+        c.j = 0;
+        ++c.i;
+        open_unit(c);
       }
     };
-    // K (and V unless shared) row addresses of the 4 slots of tile j; null = masked
-    auto make_rows = [&](int j, const int32_t* rr, const T** kr, const T** vr) {
+    Cursor cl{0, 0, false, nullptr, 0, 0, nullptr}, cm{0, 0, false, nullptr, 0, 0, nullptr};
+    open_unit(cl);
+    open_unit(cm);
+    // raw indices of the load cursor's tile, then advance it
+    auto load_idx = [&](int32_t* rr) {
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
-        const int c = j * BN + g * 16 + rsub;
+        const int c = cl.j * BN + g * 16 + rsub;
+        rr[g] = (cl.in && c < p.k_topk) ? cl.ir[c * p.stk1] : -1;
+      }
+      advance(cl);
+    };
+    // K (and V unless shared) row addresses of the make cursor's tile (null =
+    // masked), then advance it
+    auto make_rows = [&](const int32_t* rr, const T** kr, const T** vr) {
+      const int kvh = cm.kvh, ctx = cm.ctx;
+      const int32_t* bt_row = cm.bt_row;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int c = cm.j * BN + g * 16 + rsub;
         const int64_t r = rr[g];
         kr[g] = nullptr;
         vr[g] = nullptr;
-        if (!(j < n_tiles && c < p.k_topk) || !sp_slot_valid<DECODE>(p, c, r, ctx, bt_row)) continue;
+        if (!(cm.in && c < p.k_topk) || !sp_slot_valid<DECODE>(p, c, r, ctx, bt_row)) continue;
         if (!DECODE) {
           if (r < p.rows1) {
             kr[g] = kb + r * p.k_s0 + kvh * p.k_sh;
@@ -298,57 +336,83 @@ __global__ void __launch_bounds__(288, 1)
           if (!SHARED) vr[g] = reinterpret_cast<const T*>(p.cv) + cr * p.cv_s0 + kvh * p.cv_sh;
         }
       }
+      advance(cm);
     };
     const T* cur[4];
     const T* nxt[4];
     const T* vcur[4];
     const T* vnxt[4];
-    int32_t ia[4], ib[4];  // raw indices of tiles j + 1 and j + 2
-    load_idx(0, ia);
-    make_rows(0, ia, cur, vcur);
-    load_idx(1, ia);
+    int32_t ia[4], ib[4];  // raw indices of tiles J + 1 and J + 2
     bool ok = true;
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      load_idx(j + 2, ib);
-      make_rows(j + 1, ia, nxt, vnxt);
-      // ---- K rows of tile j ----
-      const int sk = j % NSK;
-      if (j >= NSK) ok = mbar_wait_sleep(&k_empty[sk], ((j / NSK) - 1) & 1);
-      else if (sk == NSK - 1) ok = mbar_wait_sleep(q_tmem, 0);  // the Q staging area is free
-      if (!ok) break;
-      uint8_t* kst = smem + L::KOFF + sk * L::KST;
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const int row = g * 16 + rsub;
-        const bool valid = cur[g] != nullptr;
-        // masked rows: a zero-byte copy (zero fill) from an in-bounds address
-        const T* src = (valid ? cur[g] : kb) + chunk * 8;
-        const uint32_t dst_off = row * 128 + ((chunk ^ (row & 7)) << 4);
-#pragma unroll
-        for (int cb = 0; cb < L::NQB; ++cb) cp_async_16(kst + cb * L::BLK + dst_off, src + cb * 64, valid);
+    int item = 0, J = 0;
+    // the Q of unit i (TMA), one K ring item
+    auto issue_q = [&](int i) -> bool {
+      const int sq = item % NSK;
+      if (item >= NSK && !mbar_wait_sleep(&k_empty[sq], ((item / NSK) - 1) & 1)) return false;
+      if (pt == 0) {
+        const int64_t u = unit_of(i);
+        const int y = static_cast<int>(u % p.Y);
+        const int h0 = (y / p.head_chunks) * p.G + (y % p.head_chunks) * 64;
+        uint8_t* qst = smem + L::KOFF + sq * L::KST;
+        mbar_arrive_expect_tx(&k_full[sq], L::NQB * L::BLK);
+#pragma unroll 1
+        for (int cb = 0; cb < L::NQB; ++cb)
+          tma_load_2d(qst + cb * L::BLK, &tmQ, &k_full[sq], cb * 64, static_cast<int>(u / p.Y) * p.H + h0);
+      } else {
+        mbar_arrive(&k_full[sq]);
       }
-      cp_async_mbar_arrive(&k_full[sk]);
-      if constexpr (!SHARED) {
-        // ---- V rows of tile j ----
-        const int sv = j % NSV;
-        if (j >= NSV && !(ok = mbar_wait_sleep(&v_empty[sv], ((j / NSV) - 1) & 1))) break;
-        uint8_t* vst = smem + L::VOFF + sv * L::VST;
+      ++item;
+      return true;
+    };
+    // the first Q goes out before the index pipeline is primed, so its copy
+    // overlaps the first index loads' memory latency
+    if (n_my > 0 && n_tiles > 0) ok = issue_q(0);
+    load_idx(ia);
+    make_rows(ia, cur, vcur);
+    load_idx(ia);
+    for (int i = 0; i < n_my && n_tiles > 0 && ok; ++i) {
+      if (i > 0 && !(ok = issue_q(i))) break;
+      for (int j = 0; j < n_tiles && ok; ++j, ++J, ++item) {
+        load_idx(ib);               // tile J + 2
+        make_rows(ia, nxt, vnxt);   // tile J + 1
+        // ---- K rows of tile J ----
+        const int sk = item % NSK;
+        if (item >= NSK) ok = mbar_wait_sleep(&k_empty[sk], ((item / NSK) - 1) & 1);
+        if (!ok) break;
+        uint8_t* kst = smem + L::KOFF + sk * L::KST;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           const int row = g * 16 + rsub;
-          const bool valid = vcur[g] != nullptr;
-          const T* src = (valid ? vcur[g] : vb) + chunk * 8;
+          const bool valid = cur[g] != nullptr;
+          // masked rows: a zero-byte copy (zero fill) from an in-bounds address
+          const T* src = (valid ? cur[g] : kb) + chunk * 8;
           const uint32_t dst_off = row * 128 + ((chunk ^ (row & 7)) << 4);
 #pragma unroll
-          for (int cb = 0; cb < L::NVB; ++cb) cp_async_16(vst + cb * L::BLK + dst_off, src + cb * 64, valid);
+          for (int cb = 0; cb < L::NQB; ++cb) cp_async_16(kst + cb * L::BLK + dst_off, src + cb * 64, valid);
         }
-        cp_async_mbar_arrive(&v_full[sv]);
-      }
+        cp_async_mbar_arrive(&k_full[sk]);
+        if constexpr (!SHARED) {
+          // ---- V rows of tile J ----
+          const int sv = J % NSV;
+          if (J >= NSV && !(ok = mbar_wait_sleep(&v_empty[sv], ((J / NSV) - 1) & 1))) break;
+          uint8_t* vst = smem + L::VOFF + sv * L::VST;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        cur[g] = nxt[g];
-        vcur[g] = vnxt[g];
-        ia[g] = ib[g];
+          for (int g = 0; g < 4; ++g) {
+            const int row = g * 16 + rsub;
+            const bool valid = vcur[g] != nullptr;
+            const T* src = (valid ? vcur[g] : vb) + chunk * 8;
+            const uint32_t dst_off = row * 128 + ((chunk ^ (row & 7)) << 4);
+#pragma unroll
+            for (int cb = 0; cb < L::NVB; ++cb) cp_async_16(vst + cb * L::BLK + dst_off, src + cb * 64, valid);
+          }
+          cp_async_mbar_arrive(&v_full[sv]);
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          cur[g] = nxt[g];
+          vcur[g] = vnxt[g];
+          ia[g] = ib[g];
+        }
       }
     }
     if (!ok) *abort_flag = 1;
@@ -359,7 +423,8 @@ __global__ void __launch_bounds__(288, 1)
     // commit, every barrier probe is made warp-uniform (all lanes must see the
     // phase complete), and an idle pass sleeps briefly so the spinning warp
     // leaves its SM sub-partition's issue slots to the softmax and gather warps.
-    if (n_tiles > 0) {
+    const int NT = n_my * n_tiles;
+    if (NT > 0) {
       auto ready = [&](uint64_t* bar, uint32_t parity) {
         return __all_sync(0xffffffffu, mbar_try_wait(smem_u32(bar), parity));
       };
@@ -378,90 +443,124 @@ __global__ void __launch_bounds__(288, 1)
       const uint32_t q_tmem_addr = taddr + L::QCOL;          // lanes 0-15
       const uint32_t o_main = taddr + (16u << 16);           // lanes 16-31
       const uint32_t o_tail = taddr + L::TCOL;               // lanes 0-15
-      bool ok = __all_sync(0xffffffffu, mbar_wait_sleep(q_tmem, 0));
-      int nq = 0, np = 0;  // next QK / PV to issue
-      const uint64_t t0 = globaltimer();
+      bool ok = true;
+      int nq = 0, np = 0;  // next QK / PV to issue (tiles over all of this CTA's units)
+      // their units, tiles within the unit and K ring items, kept incrementally
+      int iq = 0, jq = 0, itq = 1, ip = 0, jp = 0, itp = 1;
+      // The wait limit runs from the first idle check after the last MMA
+      // issued: progress only sets a flag, so no timer read sits on the issue path.
+      uint64_t t0 = globaltimer();
+      bool moved = false;
       uint32_t spins = 0;
-      while (ok && np < n_tiles) {
+      while (ok && np < NT) {
         bool did = false;
-        // QK of tile nq: its K stage must be loaded and its S buffer consumed (nq <= np + 1)
-        if (nq < n_tiles && nq <= np + 1 && ready(&k_full[nq % NSK], (nq / NSK) & 1)) {
-          fence_proxy_async_smem();
-          tc_fence_after();
-          const int sk = nq % NSK;
-          const uint32_t d_tmem = taddr + (nq & 1) * 64;
-          const uint64_t kd = k_desc0 + sk * kKStep;
+        // QK of tile nq: its unit's Q in TMEM (first tile of a unit), its K
+        // rows loaded, and its S buffer consumed (nq <= np + 1)
+        if (nq < NT && nq <= np + 1) {
+          const int it = itq;
+          if ((jq > 0 || ready(q_tmem, iq & 1)) && ready(&k_full[it % NSK], (it / NSK) & 1)) {
+            fence_proxy_async_smem();
+            tc_fence_after();
+            const int sk = it % NSK;
+            const uint32_t d_tmem = taddr + (nq & 1) * 64;
+            const uint64_t kd = k_desc0 + sk * kKStep;
 #pragma unroll
-          for (int kk = 0; kk < DQK / 16; ++kk) {
-            const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * L::BLK + (kk & 3) * 32) >> 4);
-            tc_mma_ts_w(d_tmem, q_tmem_addr + kk * 8, kd + koff, idesc_qk, kk > 0 ? 1u : 0u);
-          }
-          tc_commit_w(&s_full[nq & 1]);
-          if (!SHARED) tc_commit_w(&k_empty[sk]);  // K rows are done once S is computed
-          ++nq;
-          did = true;
-        }
-        // PV of tile np once its P is in shared memory (and, unshared, its V rows loaded)
-        if (np < nq && ready(p_full, np & 1) && (SHARED || ready(&v_full[np % NSVd], (np / NSVd) & 1))) {
-          if (!SHARED) fence_proxy_async_smem();
-          tc_fence_after();
-          const int sv = SHARED ? np % NSK : np % NSVd;
-          const uint64_t vd = v_desc0 + sv * kVStep;
-#pragma unroll
-          for (int half = 0; half < (L::OMAIN + 255) / 256; ++half) {
-#pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
-              const uint64_t a = p_desc + static_cast<uint64_t>((kk * 32) >> 4);
-              const uint64_t b = vd + static_cast<uint64_t>((half * 4 * L::BLK + kk * 2048) >> 4);
-              tc_mma_ss_w(o_main + half * 256, a, b, idesc_pv, (np > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < DQK / 16; ++kk) {
+              const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * L::BLK + (kk & 3) * 32) >> 4);
+              tc_mma_ts_w(d_tmem, q_tmem_addr + kk * 8, kd + koff, idesc_qk, kk > 0 ? 1u : 0u);
             }
-          }
-          if constexpr (L::OTAIL > 0) {
-#pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
-              const uint64_t a = p_desc + static_cast<uint64_t>((kk * 32) >> 4);
-              const uint64_t b = vd + static_cast<uint64_t>((8 * L::BLK + kk * 2048) >> 4);
-              tc_mma_ss_w(o_tail, a, b, idesc_tail, (np > 0 || kk > 0) ? 1u : 0u);
+            tc_commit_w(&s_full[nq & 1]);
+            if (!SHARED) tc_commit_w(&k_empty[sk]);  // K rows are done once S is computed
+            ++nq;
+            ++itq;
+            if (++jq == n_tiles) {  // the next unit: its Q item comes first
+              jq = 0;
+              ++iq;
+              ++itq;
             }
+            did = true;
           }
-          tc_commit_w(o_done);
-          if (SHARED) tc_commit_w(&k_empty[sv]);
-          else tc_commit_w(&v_empty[sv]);
-          tc_commit_w(p_free);
-          ++np;
-          did = true;
         }
-        if (!did) {
+        // PV of tile np once its P is in shared memory (and, unshared, its V
+        // rows loaded); a unit's first PV overwrites O, so it also waits for
+        // the previous unit's epilogue to have read O
+        if (np < nq) {
+          if ((jp > 0 || ip == 0 || ready(o_free, (ip - 1) & 1)) && ready(p_full, np & 1) &&
+              (SHARED || ready(&v_full[np % NSVd], (np / NSVd) & 1))) {
+            if (!SHARED) fence_proxy_async_smem();
+            tc_fence_after();
+            const int sv = SHARED ? itp % NSK : np % NSVd;
+            const uint64_t vd = v_desc0 + sv * kVStep;
+#pragma unroll
+            for (int half = 0; half < (L::OMAIN + 255) / 256; ++half) {
+#pragma unroll
+              for (int kk = 0; kk < BN / 16; ++kk) {
+                const uint64_t a = p_desc + static_cast<uint64_t>((kk * 32) >> 4);
+                const uint64_t b = vd + static_cast<uint64_t>((half * 4 * L::BLK + kk * 2048) >> 4);
+                tc_mma_ss_w(o_main + half * 256, a, b, idesc_pv, (jp > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+            if constexpr (L::OTAIL > 0) {
+#pragma unroll
+              for (int kk = 0; kk < BN / 16; ++kk) {
+                const uint64_t a = p_desc + static_cast<uint64_t>((kk * 32) >> 4);
+                const uint64_t b = vd + static_cast<uint64_t>((8 * L::BLK + kk * 2048) >> 4);
+                tc_mma_ss_w(o_tail, a, b, idesc_tail, (jp > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+            tc_commit_w(o_done);
+            if (SHARED) tc_commit_w(&k_empty[sv]);
+            else tc_commit_w(&v_empty[sv]);
+            tc_commit_w(p_free);
+            ++np;
+            ++itp;
+            if (++jp == n_tiles) {
+              jp = 0;
+              ++ip;
+              ++itp;
+            }
+            did = true;
+          }
+        }
+        if (did) {
+          moved = true;
+        } else {
           __nanosleep(32);
-          if ((++spins & 255u) == 0u &&
-              __any_sync(0xffffffffu, globaltimer() - t0 > TAK_WAIT_LIMIT_NS * 4 || *abort_flag != 0)) {
-            if (lane == 0) record_error(1);
-            ok = false;
+          if ((++spins & 255u) == 0u) {
+            const uint64_t now = globaltimer();
+            if (moved) {
+              t0 = now;
+              moved = false;
+            }
+            if (__any_sync(0xffffffffu, now - t0 > TAK_WAIT_LIMIT_NS * 4 || *abort_flag != 0)) {
+              if (lane == 0) record_error(1);
+              ok = false;
+            }
           }
         }
       }
       if (!ok) *abort_flag = 1;
     }
-  } else {
+  } else if (warp < 4) {
     // ---------------- Q into TMEM, softmax + epilogue: warps 0-3, 16 head rows per warp ----------------
     const int t16 = lane & 15, hi = lane >> 4;
     const int row = 16 * warp + t16;
-    const bool row_ok = row < nrows;
-    const int head = h0 + row;
-    const bool has_sink = p.sink != nullptr;
-    const float sink_log2 = (has_sink && row_ok) ? p.sink[head] * kLog2e : -INFINITY;
     const uint32_t s_lane = static_cast<uint32_t>(32 * warp) << 16;       // S, Q, O tail: lanes 0-15
     const uint32_t o_lane = static_cast<uint32_t>(32 * warp + 16) << 16;  // O: lanes 16-31
-    bool ok = mbar_wait(q_full, 0);
-    if (ok) {
-      // Q row `row`, 128-byte swizzled boxes of 64 columns -> TMEM columns
-      // QCOL + k/2 (two 16-bit elements per column): per instruction, threads
-      // 0-15 take box 2i and threads 16-31 box 2i + 1 of their rows
-      const uint8_t* qrow = qstage + row * 128;
+    // Q of unit i (its K ring item) -> TMEM columns QCOL + k/2 (two 16-bit
+    // elements per column): per instruction, threads 0-15 take box 2n and
+    // threads 16-31 box 2n + 1 of their rows.  Called once every QK of the
+    // previous unit has completed (its last S has been read).  The ring stage
+    // is handed back once all 128 threads have arrived on q_tmem, i.e. have
+    // read it.
+    auto move_q = [&](int i) -> bool {
+      const int it = q_item(i), sq = it % NSK;
+      if (!mbar_wait(&k_full[sq], (it / NSK) & 1)) return false;
+      const uint8_t* qrow = smem + L::KOFF + sq * L::KST + row * 128;
 #pragma unroll 1
-      for (int i = 0; i < L::NQB / 2; ++i) {
+      for (int n = 0; n < L::NQB / 2; ++n) {
         uint32_t r[32];
-        const uint8_t* box = qrow + (2 * i + hi) * L::BLK;
+        const uint8_t* box = qrow + (2 * n + hi) * L::BLK;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const uint4 u = *reinterpret_cast<const uint4*>(box + ((c ^ (row & 7)) << 4));
@@ -470,7 +569,7 @@ __global__ void __launch_bounds__(288, 1)
           r[4 * c + 2] = u.z;
           r[4 * c + 3] = u.w;
         }
-        tmem_st16x2(taddr + s_lane + L::QCOL + 64 * i, r);
+        tmem_st16x2(taddr + s_lane + L::QCOL + 64 * n, r);
       }
       if constexpr (L::NQB % 2) {
         // the odd last box: threads 0-15 its first 32 elements, threads 16-31 the rest
@@ -487,150 +586,180 @@ __global__ void __launch_bounds__(288, 1)
         tmem_st16x2_x16(taddr + s_lane + L::QCOL + 32 * (L::NQB - 1), r);
       }
       tmem_st_wait();
-    }
-    tc_fence_before();
-    mbar_arrive(q_tmem);
-    float m_run = -INFINITY, m_used = -INFINITY, l = 0.f;
-    auto tile_mask = [&](int j) -> uint32_t {
-      // validity of this thread's 32 columns of tile j (lane l: columns l and l+32)
-      const int c0 = j * BN + lane, c1 = c0 + 32;
-      const int64_t r0 = c0 < p.k_topk ? static_cast<int64_t>(idx_row[c0 * p.stk1]) : -1;
-      const int64_t r1 = c1 < p.k_topk ? static_cast<int64_t>(idx_row[c1 * p.stk1]) : -1;
-      const uint32_t lo =
-          __ballot_sync(0xffffffffu, c0 < p.k_topk && sp_slot_valid<DECODE>(p, c0, r0, ctx, bt_row));
-      const uint32_t hi_m =
-          __ballot_sync(0xffffffffu, c1 < p.k_topk && sp_slot_valid<DECODE>(p, c1, r1, ctx, bt_row));
-      return hi ? hi_m : lo;
-    };
-    // O columns [c*64, c*64 + 64) of this warp's rows: lanes 16-31 below 512, the tail on lanes 0-15
-    auto o_addr = [&](int c) -> uint32_t {
-      return c * 64 < L::OMAIN ? taddr + o_lane + c * 64 : taddr + s_lane + L::TCOL + (c * 64 - L::OMAIN);
-    };
-    uint32_t vnext = (ok && n_tiles > 0) ? tile_mask(0) : 0u;
-    for (int j = 0; ok && j < n_tiles; ++j) {
-      const int b = j & 1;
-      const uint32_t vbits = vnext;
-      if (j + 1 < n_tiles) vnext = tile_mask(j + 1);
-      if (!(ok = mbar_wait_sleep(&s_full[b], (j >> 1) & 1))) break;
-      tc_fence_after();
-      uint32_t sr[32];
-      tmem_ld16x2(taddr + s_lane + b * 64, sr);
-      tmem_ld_wait();
-      // every column of the warp's tile valid (the common case): no per-score tests
-      const bool all_valid = __all_sync(0xffffffffu, vbits == 0xffffffffu);
-      float mx = -INFINITY;
-      if (all_valid) {
-        float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < 32; c += 8) {
-          mx = fmax3(mx, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-          m1 = fmax3(m1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
-          m2 = fmax3(m2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
-          m3 = fmax3(m3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
-        }
-        mx = fmax3(mx, m1, fmaxf(m2, m3));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if ((vbits >> c) & 1u) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      tc_fence_before();
+      mbar_arrive(q_tmem);
+      if (tid == 0) {
+        if (!mbar_wait(q_tmem, i & 1)) return false;
+        fence_proxy_async_smem();
+        mbar_arrive(&k_empty[sq]);
       }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float m_new = fmaxf(m_run, mx * p.scale_log2);
-      const bool need = m_new != -INFINITY && m_new > m_used + 8.f;
-      const bool resc = need && m_used != -INFINITY;
-      if (__any_sync(0xffffffffu, resc)) {
-        if (!(ok = mbar_wait(o_done, (j - 1) & 1))) break;
+      return true;
+    };
+    bool ok = true;
+    if (n_tiles > 0 && n_my > 0) ok = move_q(0);
+    int J = 0;  // tiles over all of this CTA's units
+    for (int i = 0; i < n_my; ++i) {
+      const int64_t u = unit_of(i);
+      const int t = static_cast<int>(u / p.Y);
+      const int y = static_cast<int>(u % p.Y);
+      const int h0 = (y / p.head_chunks) * p.G + (y % p.head_chunks) * 64;
+      const int nrows = min(64, p.G - (y % p.head_chunks) * 64);
+      const bool row_ok = row < nrows;
+      const int head = h0 + row;
+      const bool has_sink = p.sink != nullptr;
+      const float sink_log2 = (has_sink && row_ok) ? p.sink[head] * kLog2e : -INFINITY;
+      const int32_t* idx_row = p.topk + static_cast<int64_t>(t) * p.stk0;
+      const int ctx = DECODE ? p.ctx_lens[t] : 0;
+      const int32_t* bt_row = DECODE ? p.bt + static_cast<int64_t>(t) * p.sbt0 : nullptr;
+      float m_run = -INFINITY, m_used = -INFINITY, l = 0.f;
+      auto tile_mask = [&](int j) -> uint32_t {
+        // validity of this thread's 32 columns of tile j (lane l: columns l and l+32)
+        const int c0 = j * BN + lane, c1 = c0 + 32;
+        const int64_t r0 = c0 < p.k_topk ? static_cast<int64_t>(idx_row[c0 * p.stk1]) : -1;
+        const int64_t r1 = c1 < p.k_topk ? static_cast<int64_t>(idx_row[c1 * p.stk1]) : -1;
+        const uint32_t lo =
+            __ballot_sync(0xffffffffu, c0 < p.k_topk && sp_slot_valid<DECODE>(p, c0, r0, ctx, bt_row));
+        const uint32_t hi_m =
+            __ballot_sync(0xffffffffu, c1 < p.k_topk && sp_slot_valid<DECODE>(p, c1, r1, ctx, bt_row));
+        return hi ? hi_m : lo;
+      };
+      // O columns [c*64, c*64 + 64) of this warp's rows: lanes 16-31 below 512, the tail on lanes 0-15
+      auto o_addr = [&](int c) -> uint32_t {
+        return c * 64 < L::OMAIN ? taddr + o_lane + c * 64 : taddr + s_lane + L::TCOL + (c * 64 - L::OMAIN);
+      };
+      uint32_t vnext = (ok && n_tiles > 0) ? tile_mask(0) : 0u;
+      for (int j = 0; ok && j < n_tiles; ++j, ++J) {
+        const int b = J & 1;
+        const uint32_t vbits = vnext;
+        if (j + 1 < n_tiles) vnext = tile_mask(j + 1);
+        if (!(ok = mbar_wait_sleep(&s_full[b], (J >> 1) & 1))) break;
         tc_fence_after();
-        const float f = resc ? fast_exp2(m_used - m_new) : 1.f;
-        uint32_t orow[32];
-#pragma unroll 1
-        for (int c = 0; c < DV / 64; ++c) {
-          tmem_ld16x2(o_addr(c), orow);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * f);
-          tmem_st16x2(o_addr(c), orow);
-        }
-        tmem_st_wait();
-        l *= f;
-      }
-      if (need) m_used = m_new;
-      m_run = m_new;
-      const float mu = m_used == -INFINITY ? 0.f : m_used;
-      uint32_t pk[16];
-      float ls = 0.f;
-      if (all_valid) {
-        // two scores per packed fp32 FMA (same rounding as the scalar form) and per packed row-sum add
-        const uint64_t sl2x2 = (static_cast<uint64_t>(__float_as_uint(p.scale_log2)) << 32) |
-                               __float_as_uint(p.scale_log2);
-        const uint64_t nmux2 = (static_cast<uint64_t>(__float_as_uint(-mu)) << 32) | __float_as_uint(-mu);
-        uint64_t lsx2 = 0;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          uint64_t x = (static_cast<uint64_t>(sr[2 * c + 1]) << 32) | sr[2 * c];
-          asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(x) : "l"(sl2x2), "l"(nmux2));
-          const float a = fast_exp2(__uint_as_float(static_cast<uint32_t>(x)));
-          const float bb = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
-          const uint64_t ab = (static_cast<uint64_t>(__float_as_uint(bb)) << 32) | __float_as_uint(a);
-          asm("add.rn.f32x2 %0, %0, %1;" : "+l"(lsx2) : "l"(ab));
-          pk[c] = Elem<T>::pack2(a, bb);
-        }
-        ls = __uint_as_float(static_cast<uint32_t>(lsx2)) + __uint_as_float(static_cast<uint32_t>(lsx2 >> 32));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const float a = ((vbits >> (2 * c)) & 1u) ? fast_exp2(__uint_as_float(sr[2 * c]) * p.scale_log2 - mu) : 0.f;
-          const float bb =
-              ((vbits >> (2 * c + 1)) & 1u) ? fast_exp2(__uint_as_float(sr[2 * c + 1]) * p.scale_log2 - mu) : 0.f;
-          ls += a + bb;
-          pk[c] = Elem<T>::pack2(a, bb);
-        }
-      }
-      l += ls;
-      if (j >= 1 && !(ok = mbar_wait_sleep(p_free, (j - 1) & 1))) break;
-      uint8_t* prow = smem + L::POFF + row * 128;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int chunk = (hi * 4 + k) ^ (row & 7);
-        *reinterpret_cast<uint4*>(prow + chunk * 16) = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(p_full);
-    }
-    if (ok && n_tiles > 0) ok = mbar_wait(o_done, (n_tiles - 1) & 1);
-    if (!ok) *abort_flag = 1;
-    tc_fence_after();
-    const float l_tot = l + __shfl_xor_sync(0xffffffffu, l, 16);
-    const float M = fmaxf(m_run, sink_log2);
-    const float f = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - M);
-    const float Lsum = l_tot * f + (has_sink && row_ok ? fast_exp2(sink_log2 - M) : 0.f);
-    const float inv = (Lsum > 0.f && ok) ? f / Lsum : 0.f;
-    T* orow_g = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(t) * p.so_t + static_cast<int64_t>(head) * p.so_h;
-#pragma unroll 1
-    for (int c = 0; c < DV / 64; ++c) {
-      uint32_t o[32];
-      if (n_tiles > 0) {
-        tmem_ld16x2(o_addr(c), o);
+        uint32_t sr[32];
+        tmem_ld16x2(taddr + s_lane + b * 64, sr);
         tmem_ld_wait();
-      } else {
+        // the unit's last S is in registers, so all of its QKs have completed:
+        // the next unit's Q may replace it in TMEM while this tile finishes
+        if (j == n_tiles - 1 && i + 1 < n_my && !(ok = move_q(i + 1))) break;
+        // every column of the warp's tile valid (the common case): no per-score tests
+        const bool all_valid = __all_sync(0xffffffffu, vbits == 0xffffffffu);
+        float mx = -INFINITY;
+        if (all_valid) {
+          float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0u;
-      }
-      if (row_ok) {
-        T* dst = orow_g + c * 64 + hi * 32;
+          for (int c = 0; c < 32; c += 8) {
+            mx = fmax3(mx, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+            m1 = fmax3(m1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+            m2 = fmax3(m2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+            m3 = fmax3(m3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+          }
+          mx = fmax3(mx, m1, fmaxf(m2, m3));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if ((vbits >> c) & 1u) mx = fmaxf(mx, __uint_as_float(sr[c]));
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m_run, mx * p.scale_log2);
+        const bool need = m_new != -INFINITY && m_new > m_used + 8.f;
+        const bool resc = need && m_used != -INFINITY;
+        if (__any_sync(0xffffffffu, resc)) {
+          if (!(ok = mbar_wait(o_done, (J - 1) & 1))) break;
+          tc_fence_after();
+          const float f = resc ? fast_exp2(m_used - m_new) : 1.f;
+          uint32_t orow[32];
+#pragma unroll 1
+          for (int c = 0; c < DV / 64; ++c) {
+            tmem_ld16x2(o_addr(c), orow);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * f);
+            tmem_st16x2(o_addr(c), orow);
+          }
+          tmem_st_wait();
+          l *= f;
+        }
+        if (need) m_used = m_new;
+        m_run = m_new;
+        const float mu = m_used == -INFINITY ? 0.f : m_used;
+        uint32_t pk[16];
+        float ls = 0.f;
+        if (all_valid) {
+          // two scores per packed fp32 FMA (same rounding as the scalar form) and per packed row-sum add
+          const uint64_t sl2x2 = (static_cast<uint64_t>(__float_as_uint(p.scale_log2)) << 32) |
+                                 __float_as_uint(p.scale_log2);
+          const uint64_t nmux2 = (static_cast<uint64_t>(__float_as_uint(-mu)) << 32) | __float_as_uint(-mu);
+          uint64_t lsx2 = 0;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            uint64_t x = (static_cast<uint64_t>(sr[2 * c + 1]) << 32) | sr[2 * c];
+            asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(x) : "l"(sl2x2), "l"(nmux2));
+            const float a = fast_exp2(__uint_as_float(static_cast<uint32_t>(x)));
+            const float bb = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
+            const uint64_t ab = (static_cast<uint64_t>(__float_as_uint(bb)) << 32) | __float_as_uint(a);
+            asm("add.rn.f32x2 %0, %0, %1;" : "+l"(lsx2) : "l"(ab));
+            pk[c] = Elem<T>::pack2(a, bb);
+          }
+          ls = __uint_as_float(static_cast<uint32_t>(lsx2)) + __uint_as_float(static_cast<uint32_t>(lsx2 >> 32));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float a = ((vbits >> (2 * c)) & 1u) ? fast_exp2(__uint_as_float(sr[2 * c]) * p.scale_log2 - mu) : 0.f;
+            const float bb =
+                ((vbits >> (2 * c + 1)) & 1u) ? fast_exp2(__uint_as_float(sr[2 * c + 1]) * p.scale_log2 - mu) : 0.f;
+            ls += a + bb;
+            pk[c] = Elem<T>::pack2(a, bb);
+          }
+        }
+        l += ls;
+        if (J >= 1 && !(ok = mbar_wait_sleep(p_free, (J - 1) & 1))) break;
+        uint8_t* prow = smem + L::POFF + row * 128;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          uint4 u;
-          u.x = Elem<T>::pack2(__uint_as_float(o[8 * k + 0]) * inv, __uint_as_float(o[8 * k + 1]) * inv);
-          u.y = Elem<T>::pack2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv);
-          u.z = Elem<T>::pack2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
-          u.w = Elem<T>::pack2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
-          *reinterpret_cast<uint4*>(dst + 8 * k) = u;
+          const int chunk = (hi * 4 + k) ^ (row & 7);
+          *reinterpret_cast<uint4*>(prow + chunk * 16) = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(p_full);
+      }
+      if (ok && n_tiles > 0) ok = mbar_wait(o_done, (J - 1) & 1);
+      if (!ok) *abort_flag = 1;
+      tc_fence_after();
+      const float l_tot = l + __shfl_xor_sync(0xffffffffu, l, 16);
+      const float M = fmaxf(m_run, sink_log2);
+      const float f = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - M);
+      const float Lsum = l_tot * f + (has_sink && row_ok ? fast_exp2(sink_log2 - M) : 0.f);
+      const float inv = (Lsum > 0.f && ok) ? f / Lsum : 0.f;
+      T* orow_g = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(t) * p.so_t + static_cast<int64_t>(head) * p.so_h;
+#pragma unroll 1
+      for (int c = 0; c < DV / 64; ++c) {
+        uint32_t o[32];
+        if (n_tiles > 0) {
+          tmem_ld16x2(o_addr(c), o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (row_ok) {
+          T* dst = orow_g + c * 64 + hi * 32;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint4 u;
+            u.x = Elem<T>::pack2(__uint_as_float(o[8 * k + 0]) * inv, __uint_as_float(o[8 * k + 1]) * inv);
+            u.y = Elem<T>::pack2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv);
+            u.z = Elem<T>::pack2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
+            u.w = Elem<T>::pack2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + 8 * k) = u;
+          }
         }
       }
+      if (row_ok && hi == 0 && p.lse)
+        p.lse[static_cast<int64_t>(t) * p.H + head] = (Lsum > 0.f && ok) ? (M + __log2f(Lsum)) * kLn2 : -INFINITY;
+      // O has been read: the next unit's first P.V may overwrite it
+      tc_fence_before();
+      mbar_arrive(o_free);
+      if (!ok) break;
     }
-    if (row_ok && hi == 0 && p.lse)
-      p.lse[static_cast<int64_t>(t) * p.H + head] = (Lsum > 0.f && ok) ? (M + __log2f(Lsum)) * kLn2 : -INFINITY;
   }
   tc_fence_before();
   __syncthreads();
@@ -707,10 +836,16 @@ static int launch_sparse_tc_mode(const SparseArgs& a, cudaStream_t st) {
     p.wreach = static_cast<int64_t>(a.max_blocks) * a.block_size;
     p.num_blocks = a.num_blocks;
   }
+  // units (token, KV head group).  Prefill runs persistent CTAs (one per SM,
+  // each walking its share of the units, so that the next unit's Q and rows
+  // stream in while the current one finishes); decode, with one unit per
+  // request, one unit per CTA
+  p.Y = a.num_kv_heads * p.head_chunks;
+  p.n_units = static_cast<int64_t>(a.num_tokens) * p.Y;
+  const int64_t ctas = a.decode ? p.n_units : std::min<int64_t>(p.n_units, num_sms());
   auto kern = sparse_tc_kernel<T, DQK, DV, SHARED, DECODE>;
   if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::SMEM)) return r;
-  dim3 grid(a.num_tokens, a.num_kv_heads * p.head_chunks);
-  kern<<<grid, 288, L::SMEM, st>>>(mq, p);
+  kern<<<static_cast<unsigned>(ctas), 288, L::SMEM, st>>>(mq, p);
   note_kernel("sparse_tc");
   return 0;
 }
@@ -763,6 +898,9 @@ int sparse_tc_launch(const SparseArgs& a, cudaStream_t st, bool* handled) {
   const int G = a.num_q_heads / a.num_kv_heads;
   if (G > 64 && G % 64 != 0) return 0;
   if (a.num_tokens > 2147483647 / 64) return 0;
+  // Q rows are TMA row coordinates t * H + h (int32), and decode launches one
+  // CTA per (token, KV head group) unit in one grid dimension
+  if (static_cast<int64_t>(a.num_tokens) * a.num_q_heads > 2147483647LL) return 0;
   // q rows [T * H, Dqk] must be dense over heads
   if ((reinterpret_cast<uintptr_t>(a.q) & 15) || a.sq[2] != 1 || a.sq[0] != static_cast<int64_t>(a.num_q_heads) * a.sq[1] ||
       (a.sq[1] * 2) % 16 != 0)
