@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(288, 1)
     const int NT = n_my * n_tiles;
     if (NT > 0) {
       auto ready = [&](uint64_t* bar, uint32_t parity) {
-        return __all_sync(0xffffffffu, mbar_try_wait(smem_u32(bar), parity));
+        return __all_sync(0xffffffffu, mbar_test_wait(smem_u32(bar), parity));
       };
       constexpr int AB = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       constexpr int NPV = L::OMAIN < 256 ? L::OMAIN : 256;
