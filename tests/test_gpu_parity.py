@@ -368,6 +368,22 @@ def test_sparse_prefill_mla_shape(with_sink, kernel_path):
     close_lse(lse, ref_lse)
 
 
+@pytest.mark.parametrize("H", [64, 128])
+def test_sparse_prefill_persistent_units(H):
+    """More (token, head group) units than SMs, so every persistent CTA walks
+    several units through one K ring (each unit's Q, then its tiles): the
+    576/512 latent kernel of the sparse bench with 64 heads (one unit per
+    token) and with 128 heads on one KV head (two 64-row units per token).
+    160 indices per token (three tiles, the last one ragged), -1 padding and
+    a fully masked row."""
+    q, k, v, idx, sink = _sparse_case(330, H, 1, 576, 512, 1200, 160, torch.bfloat16, 71 + H, shared_latent=True)
+    out, lse = SA.sparse_attn_prefill(q, k, v, idx, None, sink, return_lse=True)
+    assert T.last_kernel() == "sparse_tc"
+    ref, ref_lse = O.sparse_prefill(npy(q), npy(k), npy(v), idx.cpu(), None, sink.cpu())
+    close(out, ref, TOL16)
+    close_lse(lse, ref_lse)
+
+
 @pytest.mark.parametrize("variant", ["576v512_shared", "576v576_shared", "576v576_sep", "576v512_sep",
                                      "512v512_shared", "512v512_sep", "256v256_sep"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
