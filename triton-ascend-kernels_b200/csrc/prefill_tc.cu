@@ -57,7 +57,7 @@ struct PrefillTcParams {
 namespace pf {
 constexpr int BM = 128, BN = 128;
 constexpr int TILE = 128 * 128;                   // one 64-column block of 128 rows (bytes)
-constexpr int NBAR = 23;
+constexpr int NBAR = 25;
 constexpr float kRescaleThreshold = 8.f;          // log2 units
 // Shared-memory layout and tiling of head dim D: NT query tiles of 128 rows
 // per CTA, NST-stage K and V rings, NB 64-column boxes per row.
@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(pf::NWARP * 32, 1)
   uint64_t* p_full = bars + 11;  // [2] per tile
   uint64_t* o_done = bars + 13;  // [2] per tile
   uint64_t* pair_mb = bars + 15; // [2][4] per tile and lane quadrant: the two softmax warps' exchange
+  uint64_t* p_half = bars + 23;  // [2] per tile: the first 32-key chunk of each half of P stored
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -170,6 +171,7 @@ __global__ void __launch_bounds__(pf::NWARP * 32, 1)
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 256);
+      mbar_init(&p_half[i], 256);
       mbar_init(&o_done[i], 1);
     }
     *abort_flag = 0;
@@ -246,15 +248,21 @@ __global__ void __launch_bounds__(pf::NWARP * 32, 1)
         }
         tc_commit_w(&s_full[t]);
       };
-      auto pv = [&](int t, int j) {
+      // P.V in two parts: part 0 takes the K16 steps of P's first 32-key
+      // chunk in each column half (keys 0-31 and 64-95, steps 0, 1, 4, 5),
+      // issued as soon as the softmax has stored that chunk, so it runs while
+      // the softmax computes the second chunk; part 1 the rest, then the commit
+      auto pv = [&](int t, int j, int part) {
         const uint64_t vd = v_desc0 + ((j % NST) ? kTileStep : 0);
         const uint32_t p_tmem = taddr + 256 + t * 128;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
+        for (int i = 0; i < BN / 32; ++i) {
+          const int kk = (i >> 1) * 4 + part * 2 + (i & 1);
           tc_mma_ts_w(taddr + t * 128, p_tmem + (kk >> 2) * 64 + (kk & 3) * 8,
                       vd + static_cast<uint64_t>((kk * 2048) >> 4), idesc_pv,
-                    (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit_w(&o_done[t]);
+                      (j > 0 || part > 0 || i > 0) ? 1u : 0u);
+        }
+        if (part == 1) tc_commit_w(&o_done[t]);
       };
       bool ok = n_kv > 0 && wait(q_full, 0) && wait(&k_full[0], 0);
       if (ok) {
@@ -278,9 +286,12 @@ __global__ void __launch_bounds__(pf::NWARP * 32, 1)
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (j < n_t[t]) {
+            if (!(ok = wait(&p_half[t], j & 1))) break;
+            tc_fence_after();
+            pv(t, j, 0);
             if (!(ok = wait(&p_full[t], j & 1))) break;
             tc_fence_after();
-            pv(t, j);
+            pv(t, j, 1);
             if (t == 1 || j >= n_t[1]) tc_commit_w(&v_empty[st]);
             if (j + 1 < n_t[t]) {
               if (!k_next && !(ok = wait(&k_full[(j + 1) % NST], ((j + 1) / NST) & 1))) break;
@@ -420,6 +431,12 @@ __global__ void __launch_bounds__(pf::NWARP * 32, 1)
           }
         }
         tmem_st16(s_tmem + hf * 64 + 16 * c4, pk);
+        if (c4 == 0) {
+          // the first chunk of P: the issuer starts P.V on it
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(&p_half[t]);
+        }
       }
       ls0 += __uint_as_float(static_cast<uint32_t>(lsx2));
       ls1 += __uint_as_float(static_cast<uint32_t>(lsx2 >> 32));
