@@ -157,8 +157,10 @@ __device__ __forceinline__ void tmem_st16x2_x16(uint32_t taddr, const uint32_t* 
 
 // Shared-memory plan of one head-dim variant.  K stages hold DQK columns of
 // 64 gathered rows; V stages (only when V is not a prefix view of K) DV
-// columns.  Q (64 x DQK) is staged in the last K stage before it moves to
-// TMEM.  Stage counts are the most that fit next to P (at most 4).
+// columns.  Each unit's Q (64 x DQK) passes through the K ring as one item
+// before it moves to TMEM.  Stage counts are the most that fit next to P (at
+// most 4; at least 2 K stages for every variant, so a unit's Q and its first
+// tile are in flight together).
 template <int DQK, int DV, bool SHARED>
 struct SpLayout {
   static constexpr int BLK = 64 * 128;  // 64 rows x 128 B: one 64-column block of a 64-row tile
