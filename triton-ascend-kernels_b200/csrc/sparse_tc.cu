@@ -188,7 +188,7 @@ struct SpLayout {
   static constexpr int TMEM_NEED = (TCOL + OTAIL) > OMAIN ? (TCOL + OTAIL) : OMAIN;
   static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;  // a power of two
   static_assert(SMEM <= 232448, "shared memory");
-  static_assert(NSK >= 1 && (SHARED || NSV >= 1), "stages");
+  static_assert(NSK >= 2 && (SHARED || NSV >= 1), "stages: a unit's Q item and a tile share the K ring");
   static_assert(OTAIL == 0 || OTAIL == 64, "a V wider than 512 columns has one 64-column tail");
 };
 
