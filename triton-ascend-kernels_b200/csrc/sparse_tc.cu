@@ -47,7 +47,9 @@
 //            S_j = Q K_j^T (M=64, N=64, K=16 x Dqk/16, A from TMEM), O += P_j
 //            V_j (M=64, N<=256 per instruction, P from shared memory).  Issue
 //            order is greedy: whichever of "QK of the next loaded tile" and
-//            "PV of the next softmaxed tile" is ready goes first.
+//            "PV of the next softmaxed tile" is ready goes first, the barriers
+//            tested without waiting (mbarrier.test_wait), so QK(j+1) runs on
+//            the tensor core while the softmax of tile j runs.
 //   warps 0-3 move each unit's Q from shared memory into TMEM (once the
 //            previous unit's last S is read), then run the softmax:
 //            TMEM loads of shape 16x32bx2 let all 32 threads of a warp work
