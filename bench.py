@@ -1160,22 +1160,17 @@ class MixedWL(Workload):
         return {"prefill_ms": round(pms, 3), "prefill_tflops": round(self.pre_flops / (pms * 1e-3) / 1e12, 1),
                 "decode_ms": round(dms, 3), "decode_gbs": round(self.dec_bytes / (dms * 1e-3) / 1e9, 1)}
 
-    def e2e_setup(self):
-        self.h = [t.cpu().pin_memory() for t in (self.q, self.k, self.v, self.qd, self.bt, self.ctx)]
-        self.d = [torch.empty_like(t) for t in (self.q, self.k, self.v, self.qd, self.btd, self.ctxd)]
-        self.hout = [torch.empty(self.q.shape, dtype=torch.bfloat16).pin_memory(),
-                     torch.empty(self.qd.shape, dtype=torch.bfloat16).pin_memory()]
-        return (sum(t.numel() * t.element_size() for t in self.h),
-                sum(t.numel() * t.element_size() for t in self.hout))
-
-    def e2e_step(self):
-        for d, h in zip(self.d, self.h):
-            d.copy_(h, non_blocking=True)
-        q, k, v, qd, bt, ctx = self.d
-        o1 = self.FP.flash_attention_prefill(q, k, v, self.cu, True)
-        o2 = self.PD.paged_attention_decode(qd, self.kc, self.vc, bt, ctx, 128, 128)
-        self.hout[0].copy_(o1, non_blocking=True)
-        self.hout[1].copy_(o2, non_blocking=True)
+    def e2e_pipeline(self):
+        """Host q / k / v of the prefill share and the decode queries, block
+        tables and lengths in, both outputs back, through the public
+        flash_attention_prefill() and paged_attention_decode(); the paged K/V
+        cache stays resident, as in a serving engine."""
+        def fn(q, k, v, qd, bt, ctx):
+            o1 = self.FP.flash_attention_prefill(q, k, v, self.cu, True)
+            o2 = self.PD.paged_attention_decode(qd, self.kc, self.vc, bt, ctx, 128, 128)
+            return o1, o2
+        return ([self.q.cpu(), self.k.cpu(), self.v.cpu(), self.qd.cpu(), self.bt, self.ctx], fn,
+                [(tuple(self.q.shape), torch.bfloat16), (tuple(self.qd.shape), torch.bfloat16)])
 
     def reference_sample(self):
         from oracle import attention_oracle as O
