@@ -892,19 +892,14 @@ class CsaWL(Workload):
         return {"compress_ms": round(ev[0].elapsed_time(ev[1]), 3), "index_ms": round(ev[1].elapsed_time(ev[2]), 3),
                 "attention_ms": round(ev[2].elapsed_time(ev[3]), 3)}
 
-    def e2e_setup(self):
-        self.hq, self.hkv, self.hg = (t.cpu().pin_memory() for t in (self.q, self.kv, self.gate))
-        self.hout = torch.empty(self.q.shape, dtype=torch.bfloat16).pin_memory()
-        self.dq, self.dkv, self.dg = (torch.empty_like(t) for t in (self.q, self.kv, self.gate))
-        return (sum(t.numel() * t.element_size() for t in (self.hq, self.hkv, self.hg)),
-                self.hout.numel() * self.hout.element_size())
-
-    def e2e_step(self):
-        for d, h in ((self.dq, self.hq), (self.dkv, self.hkv), (self.dg, self.hg)):
-            d.copy_(h, non_blocking=True)
-        o = self.CSA.csa_prefill_forward(self.dq, self.dkv, self.dkv, self.cu_h, self.n_win, self.top_k, self.m,
-                                         self.sink, gate=self.dg)
-        self.hout.copy_(o, non_blocking=True)
+    def e2e_pipeline(self):
+        """Host q / latent / gate logits in, the output back, through the
+        public csa_prefill_forward() (which reads the compressed-slot offsets
+        on the host each call, as the reference's does)."""
+        def fn(q, kv, gate):
+            return self.CSA.csa_prefill_forward(q, kv, kv, self.cu_h, self.n_win, self.top_k, self.m,
+                                                self.sink, gate=gate)
+        return ([self.q.cpu(), self.kv.cpu(), self.gate.cpu()], fn, [(tuple(self.q.shape), torch.bfloat16)])
 
     def reference_sample(self):
         from oracle import attention_oracle as O
@@ -1040,22 +1035,15 @@ class CsaDecodeWL(Workload):
         work = rows * 1024 + self.cap * 1024 + pages * 4 + 2 * self.ctx_h.numel() * 4
         return work, ms
 
-    def e2e_setup(self):
-        # per step a serving engine sends the new queries, lengths and block tables
-        self.hq = self.q.cpu().pin_memory()
-        self.hctx, self.hbt = self.ctx_h.pin_memory(), self.bt_h.pin_memory()
-        self.hout = torch.empty(self.q.shape, dtype=torch.bfloat16).pin_memory()
-        self.dq, self.dctx, self.dbt = (torch.empty_like(t) for t in (self.q, self.ctx, self.bt))
-        return (sum(t.numel() * t.element_size() for t in (self.hq, self.hctx, self.hbt)),
-                self.hout.numel() * self.hout.element_size())
-
-    def e2e_step(self):
-        for d, h in ((self.dq, self.hq), (self.dctx, self.hctx), (self.dbt, self.hbt)):
-            d.copy_(h, non_blocking=True)
-        # the reference-compatible call: compressed rows sized from the lengths read on the host
-        o = self.CSA.csa_decode_forward(self.dq, self.kc, self.kc, self.dbt, self.dctx, self.n_win, self.top_k,
-                                        self.m, self.P, self.sink)
-        self.hout.copy_(o, non_blocking=True)
+    def e2e_pipeline(self):
+        """Per step a serving engine sends the new queries, lengths and block
+        tables and reads the output back; the paged latent cache stays
+        resident.  The call is the timed step's (max_compressed = the slot
+        bound, so it reads nothing back to the host)."""
+        def fn(q, ctx, bt):
+            return self.CSA.csa_decode_forward(q, self.kc, self.kc, bt, ctx, self.n_win, self.top_k,
+                                               self.m, self.P, self.sink, max_compressed=self.cap)
+        return ([self.q.cpu(), self.ctx_h, self.bt_h], fn, [(tuple(self.q.shape), torch.bfloat16)])
 
     def reference_sample(self):
         from oracle import attention_oracle as O
