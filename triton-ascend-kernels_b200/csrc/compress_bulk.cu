@@ -27,6 +27,7 @@
 // error and the waiting warp leaves its loop (the producer waits, bounded, for
 // the copies it issued before it exits).
 #include <algorithm>
+#include <cstdio>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -358,6 +359,13 @@ __global__ void __launch_bounds__(288) compress_dual_kernel(const CompressArgs c
 
   const int u = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Launched as a programmatic dependent: no global memory is read before the
+  // grid ahead in the stream has completed (its outputs may be this grid's
+  // inputs), and from here on the grid after this one may be scheduled, so a
+  // chain of these launches overlaps each grid's launch with the drain of the
+  // one before.  Without the launch attribute both are no-ops.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (u >= hca.comp_offsets[hca.num_seqs]) return;  // num_compressed may be a capacity
   const int s = find_slot_seq(hca.comp_offsets, hca.num_seqs, u);
   const int i = u - hca.comp_offsets[s];
@@ -589,8 +597,23 @@ static bool compress_dual_typed(const CompressArgs& csa, const CompressArgs& hca
   const int span = (a.sk[0] * 2 == nk * 16 && a.sv[0] * 2 == nv * 16) ? 1 : 0;
   auto kern = (csa.stride == 4 && ch % 8 == 0) ? compress_dual_kernel<T, 4> : compress_dual_kernel<T, 0>;
   if ((*err = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem))) return true;
-  kern<<<dim3(static_cast<unsigned>(hca.num_compressed), a.num_kv_heads), threads, smem, st>>>(csa, hca, ch, nst,
-                                                                                              span);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(hca.num_compressed), a.num_kv_heads);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, csa, hca, ch, nst, span);
+  if (e != cudaSuccess) {
+    char buf[160];
+    std::snprintf(buf, sizeof(buf), "CSA + HCA compression: launch failed: %s", cudaGetErrorString(e));
+    *err = set_error(3, buf);
+    return true;
+  }
   note_kernel("compress_dual");
   return true;
 }
