@@ -1261,11 +1261,10 @@ def run_workload_ours(args, rank, world, device, W):
         else:
             ms = timed_steps(lambda n: [multi.replay() for _ in range(n // out_sets)] +
                              [graphs[i].replay() for i in range(n % out_sets)], args.steps, args.warmup, device)
-    pipelined = False
     if args.no_e2e:
         h2d = d2h = 0
         e2e_ms = float("nan")
-    elif hasattr(w, "e2e_pipeline"):
+    else:
         hin, fn, outs = w.e2e_pipeline()
         pe = PipelinedE2E(hin, fn, outs, device)
         del hin
@@ -1274,12 +1273,6 @@ def run_workload_ours(args, rank, world, device, W):
         e2e_ms = pe.timed(min(8, max(3, args.steps // 4)), 2, world)
         h2d, d2h = pe.h2d_bytes(), pe.d2h_bytes()
         del pe
-        pipelined = True
-    else:
-        h2d, d2h = w.e2e_setup()
-        if world > 1:
-            torch.distributed.barrier()
-        e2e_ms = w.timed(w.e2e_step, min(8, max(2, args.steps // 4)), 1, device)
     work_all = float(w.work)
     gather_ms = None
     per_rank = None
@@ -1332,8 +1325,7 @@ def run_workload_ours(args, rank, world, device, W):
         "e2e": {"value": round(work_all / (e2e_ms * 1e-3) / scale, 2), "unit": w.unit, "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "note": ("public API with inputs copied from pinned host memory and outputs copied back every step"
-                         + ("; copies on two copy streams overlapping the neighbouring steps' kernels"
-                            if pipelined else "; copies in series with the kernels")
+                         + "; copies on two copy streams overlapping the neighbouring steps' kernels"
                          + ("; per GPU, each rank copying its own share" if world > 1 else ""))},
         "gpu_launches": args.steps * w.launches,
         "clocks": clk.summary(),

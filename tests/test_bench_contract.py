@@ -49,3 +49,14 @@ def test_roofline_traffic_comes_from_the_workloads_own_capture():
         assert w.kernel in open(path).readline(), (name, w.profile)
         assert bench.profile_traffic(w.profile) > 0, (name, w.profile)
     assert not bench.WORKLOADS["csa"].profile     # its summary holds no per-launch traffic of the attention
+
+
+def test_every_workload_times_a_pipelined_end_to_end_leg():
+    """Every workload's `e2e` goes through PipelinedE2E: host inputs copied in
+    on one copy stream while the previous step computes, outputs copied back
+    on another, all inside the timed region."""
+    sys.path.insert(0, REPO)
+    import bench
+
+    for name, w in bench.WORKLOADS.items():
+        assert callable(getattr(w, "e2e_pipeline", None)), name
