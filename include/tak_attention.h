@@ -244,7 +244,11 @@ int tak_compress_kv_paged(const void* k_cache, const int64_t* k_strides, const v
  * <= 2048 and head_dim + head_dim_v <= 2048; else on the TMA-box kernel when
  * m_prime + m <= 256 and the head dims are multiples of 128; other shapes
  * (fp32 among them) run as two tak_compress_kv passes with the same results.
- * total_tokens = rows of K/V/gate. */
+ * total_tokens = rows of K/V/gate.  The bulk-copy kernel is launched with
+ * programmatic stream serialization: it waits in-kernel for the grid before it
+ * on the stream (whose outputs may be its inputs) and lets the grid after it be
+ * scheduled while it drains; a following launch without that attribute waits
+ * for it as usual. */
 int tak_compress_kv_csa_hca(const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
                             const float* gate, int64_t gate_stride, const int32_t* cu_seqlens, int64_t num_seqs,
                             int64_t total_tokens, const int32_t* csa_offsets, int64_t num_csa, void* csa_k,
