@@ -847,6 +847,10 @@ static int launch_sparse_tc_mode(const SparseArgs& a, cudaStream_t st) {
   p.Y = a.num_kv_heads * p.head_chunks;
   p.n_units = static_cast<int64_t>(a.num_tokens) * p.Y;
   const int64_t ctas = a.decode ? p.n_units : std::min<int64_t>(p.n_units, num_sms());
+  // a CTA counts its tiles and K ring items (a unit's Q, then its tiles) in
+  // 32-bit integers: sizes past that take the generic kernel
+  if (ctas > 0 && ((p.n_units + ctas - 1) / ctas) * ((static_cast<int64_t>(a.k_topk) + 63) / 64 + 1) > INT32_MAX)
+    return -1;
   auto kern = sparse_tc_kernel<T, DQK, DV, SHARED, DECODE>;
   if (const int r = ensure_smem_attr(reinterpret_cast<const void*>(kern), L::SMEM)) return r;
   kern<<<static_cast<unsigned>(ctas), 288, L::SMEM, st>>>(mq, p);
