@@ -11,7 +11,7 @@ import pytest
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-@pytest.mark.parametrize("workload", ["decode", "compress"])
+@pytest.mark.parametrize("workload", ["decode", "prefill", "sparse", "compress", "csa", "csa_decode", "mixed"])
 def test_reference_arm_json_line(workload):
     cmd = [sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--workload", workload,
            "--steps", "1", "--warmup", "1", "--cpu-seconds", "0.2"]
